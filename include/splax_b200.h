@@ -1,0 +1,181 @@
+/*
+ * splax_b200 C ABI: the splatting hot path of amacati/splax as plain C entry points.
+ *
+ * Each entry point replaces one of the XLA FFI targets the reference builds with
+ * warp.jax_callable and wraps in nested_vmap (splax/_batching.py:32-115). Arguments follow
+ * the Warp wrappers' order and meaning; every array is a device pointer plus its leading
+ * length ("rows") as the reference's FFI bridge sees it after collapsing vmap batches
+ * (vmap_method="expand_dims"): a per-gaussian input has n rows when shared across the batch
+ * and B*n rows when batched, a viewmat 4 or 4*B rows, a transform stack K or B*K matrices,
+ * an image B*H rows. Inner widths are fixed: xys 2, conics 3, colors 3, quats 4 (xyzw),
+ * matrices 4x4 row-major, images W*3 (colour) or W (scalars). All floats are fp32.
+ *
+ * Streams: all work is enqueued on `stream` (a cudaStream_t; NULL = legacy default stream)
+ * of the current CUDA device. Rasterize entry points block the calling thread once, on the
+ * intersection-count readback, exactly like the reference (splax/_cache.py:130-155), so they
+ * cannot be captured into a CUDA graph.
+ *
+ * Scratch: the sort keys and values (2 x 1.25 x intersections), tile bins, per-image depth
+ * ranges and packed blend records are owned by the library per device, grow-only, and
+ * dropped when the (B, n, tiles) signature changes or on splax_clear_cache()
+ * (splax/_cache.py:52-90, 158-164). Calls that overlap on the GPU on one device (two
+ * streams at once) share that scratch and must be serialised by the caller.
+ *
+ * Errors: a nonzero return is an SPLAX_ERR_* code; splax_last_error() gives the message of
+ * the calling thread's last failure. Device-side checks (bounded spin-waits, emitted count vs
+ * cum_tiles_hit, negative 64-bit depth keys, int32 count overflow) raise a device error word
+ * that the next count readback (or splax_check_device_errors) reports.
+ */
+#ifndef SPLAX_B200_H
+#define SPLAX_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SPLAX_OK 0
+#define SPLAX_ERR_INVALID_ARGUMENT 1 /* ValueError in the reference */
+#define SPLAX_ERR_KEY_OVERFLOW 2     /* splax/_rasterize/_sort/_sort.py:61-66 (ValueError) */
+#define SPLAX_ERR_OUT_OF_MEMORY 3
+#define SPLAX_ERR_CUDA 4
+#define SPLAX_ERR_DEVICE 5         /* device-side check failed, see splax_last_error() */
+#define SPLAX_ERR_COUNT_OVERFLOW 6 /* intersections exceed the int32 range of the ABI */
+
+/* Message of the calling thread's last failed call ("" if none). */
+const char *splax_last_error(void);
+
+/* Library version string. */
+const char *splax_version(void);
+
+/* FFI target "project": _project_warp, splax/_project/_kernels.py:31-107 (:110-119).
+ * Writes xys (total,2), depths, radii, conics (total,3), num_tiles_hit and the global
+ * inclusive scan cum_tiles_hit for total = B*n (camera, gaussian) pairs. */
+int splax_project(const float *means3d, int64_t means3d_rows, const float *scales,
+                  int64_t scales_rows, const float *quats_xyzw, int64_t quats_rows,
+                  const float *viewmat, int64_t viewmat_rows, const float *opacities,
+                  int64_t opacities_rows, const float *gaussian_transforms,
+                  int64_t transforms_rows, const int32_t *transform_ids, int32_t num_gaussians,
+                  int32_t num_transforms, int32_t has_transforms, int32_t img_h, int32_t img_w,
+                  float fx, float fy, float cx, float cy, float glob_scale, float clip_thresh,
+                  int64_t total, float *xys, float *depths, int32_t *radii, float *conics,
+                  int32_t *num_tiles_hit, int32_t *cum_tiles_hit, void *stream);
+
+/* FFI target "project_bwd": _project_bwd_warp, splax/_project/_kernels.py:257-341 (:344-353).
+ * B = out_rows / num_gaussians images; outputs v_mean3d (B*n,3), v_scale (B*n,3),
+ * v_quat (B*n,4) xyzw, v_viewmat (4B,4), v_transforms (B*K,4,4), all overwritten. */
+int splax_project_bwd(const float *means3d, int64_t means3d_rows, const float *scales,
+                      int64_t scales_rows, const float *quats_xyzw, int64_t quats_rows,
+                      const float *viewmat, int64_t viewmat_rows, const int32_t *radii,
+                      int64_t radii_rows, const float *conics, int64_t conics_rows,
+                      const float *v_xy, int64_t v_xy_rows, const float *v_depth,
+                      int64_t v_depth_rows, const float *v_conic, int64_t v_conic_rows,
+                      const float *gaussian_transforms, int64_t transforms_rows,
+                      const int32_t *transform_ids, int32_t num_gaussians, int32_t num_transforms,
+                      int32_t has_transforms, float fx, float fy, float glob_scale,
+                      int64_t out_rows, float *v_mean3d, float *v_scale, float *v_quat,
+                      float *v_viewmat, float *v_transforms, void *stream);
+
+/* FFI target "rasterize": _rasterize_warp, splax/_rasterize/_kernels.py:37-87 (:90-99).
+ * geom_rows = rows of xys / depths / radii / conics / cum_tiles_hit (= B*n); out_rows = B*H.
+ * key_bits: 0 = the reference's automatic width (splax/_rasterize/_sort/_sort.py:23-26),
+ * 32 or 64 to force one, the role of the reference's monkeypatchable _use_32bit_keys hook.
+ * Writes final_Ts (B*H,W), final_idx (B*H,W) and out_img (B*H,W,3). */
+int splax_rasterize(const float *colors, int64_t colors_rows, const float *opacities,
+                    int64_t opacities_rows, const float *map_opacities, int64_t map_opacities_rows,
+                    const float *background, int64_t background_rows, const float *xys,
+                    const float *depths, const int32_t *radii, const float *conics,
+                    const int32_t *cum_tiles_hit, int64_t geom_rows, int32_t num_gaussians,
+                    int32_t img_h, int32_t img_w, int64_t out_rows, int32_t key_bits,
+                    float *final_Ts, int32_t *final_idx, float *out_img, void *stream);
+
+/* FFI target "rasterize_depth": _rasterize_depth_warp, splax/_rasterize/_kernels.py:208-262
+ * (:265-274). As splax_rasterize plus out_depth (B*H,W), the alpha-blended expected depth. */
+int splax_rasterize_depth(const float *colors, int64_t colors_rows, const float *opacities,
+                          int64_t opacities_rows, const float *map_opacities,
+                          int64_t map_opacities_rows, const float *background,
+                          int64_t background_rows, const float *xys, const float *depths,
+                          const int32_t *radii, const float *conics, const int32_t *cum_tiles_hit,
+                          int64_t geom_rows, int32_t num_gaussians, int32_t img_h, int32_t img_w,
+                          int64_t out_rows, int32_t key_bits, float *final_Ts, int32_t *final_idx,
+                          float *out_img, float *out_depth, void *stream);
+
+/* FFI target "rasterize_bwd": _rasterize_bwd_warp, splax/_rasterize/_kernels.py:386-500
+ * (:503-512). B_geom = geom_rows / n renders were sorted; B_out = grad_rows / n images
+ * receive cotangents (B_out may exceed B_geom = 1: a shared render against B targets).
+ * v_out_img has v_out_rows = H (broadcast) or B_out*H rows. Outputs (grad_rows rows):
+ * v_colors (,3), v_opacity, v_xy (,2), v_conic (,3), overwritten. */
+int splax_rasterize_bwd(const float *colors, int64_t colors_rows, const float *opacities,
+                        int64_t opacities_rows, const float *map_opacities,
+                        int64_t map_opacities_rows, const float *background,
+                        int64_t background_rows, const float *xys, const float *depths,
+                        const int32_t *radii, const float *conics, const int32_t *cum_tiles_hit,
+                        int64_t geom_rows, const float *final_Ts, const int32_t *final_idx,
+                        const float *v_out_img, int64_t v_out_rows, int32_t num_gaussians,
+                        int32_t img_h, int32_t img_w, int64_t grad_rows, int32_t key_bits,
+                        float *v_colors, float *v_opacity, float *v_xy, float *v_conic,
+                        void *stream);
+
+/* FFI target "rasterize_bwd_depth": _rasterize_bwd_depth_warp,
+ * splax/_rasterize/_kernels.py:797-914 (:917-926). As splax_rasterize_bwd plus the depth
+ * cotangent v_out_depth (v_out_depth_rows = H or B_out*H) and the output v_depths. */
+int splax_rasterize_bwd_depth(const float *colors, int64_t colors_rows, const float *opacities,
+                              int64_t opacities_rows, const float *map_opacities,
+                              int64_t map_opacities_rows, const float *background,
+                              int64_t background_rows, const float *xys, const float *depths,
+                              const int32_t *radii, const float *conics,
+                              const int32_t *cum_tiles_hit, int64_t geom_rows,
+                              const float *final_Ts, const int32_t *final_idx,
+                              const float *v_out_img, int64_t v_out_rows,
+                              const float *v_out_depth, int64_t v_out_depth_rows,
+                              int32_t num_gaussians, int32_t img_h, int32_t img_w,
+                              int64_t grad_rows, int32_t key_bits, float *v_colors,
+                              float *v_opacity, float *v_xy, float *v_conic, float *v_depths,
+                              void *stream);
+
+/* sort_and_bin, splax/_rasterize/_sort/_sort.py:29-171, exposed for parity tests: copies
+ * the sorted flat gaussian ids (capacity gaussian_ids_cap) and the (B*T) int2 tile bins into
+ * caller buffers, and optionally the sorted keys (as int64, NULL to skip). Writes the
+ * intersection count and the key width used. */
+int splax_sort_and_bin(const float *xys, const float *depths, const int32_t *radii,
+                       const float *conics, const float *map_opacities,
+                       int64_t map_opacities_rows, const int32_t *cum_tiles_hit,
+                       int32_t num_gaussians, int32_t num_images, int32_t img_h, int32_t img_w,
+                       int32_t key_bits, int32_t *gaussian_ids, int64_t gaussian_ids_cap,
+                       int64_t *sorted_keys, int32_t *tile_bins, int64_t *num_intersects,
+                       int32_t *used_key_bits, void *stream);
+
+/* clear_cache, splax/_cache.py:158-164: release the scratch of every device. */
+void splax_clear_cache(void);
+
+/* Inspection of the current device's scratch entry (the reference's _scratch_cache, read by
+ * tests/test_warp_rasterize.py:350,358): out[0] sort capacity, [1] key width (32/64, 0 when
+ * empty), [2] bytes held, [3..5] signature (B, n, tiles). Returns the entries written. */
+int splax_scratch_info(int64_t *out, int32_t out_len);
+
+/* Synchronise `stream` and report any pending device-side error word. */
+int splax_check_device_errors(void *stream);
+
+/* Test hook for failure paths: after `successes` more device allocations, the next one fails
+ * as out-of-memory (negative disables). Host-side only; no GPU fault is involved. */
+void splax_debug_fail_alloc_after(int64_t successes);
+
+/* Opt-in profiling (no counterpart in the reference, which has no built-in profiling):
+ * `timing` records CUDA events around every launch sequence on its stream; `count_work`
+ * switches the blend kernels to instrumented builds that count per-pixel evaluations and
+ * contributions (the roofline's work units). Both default off. */
+void splax_profile_enable(int32_t timing, int32_t count_work);
+
+/* Zero the current device's timers and work counters. */
+int splax_profile_reset(void);
+
+/* JSON of the current device's per-kernel launches / kernels / milliseconds and work units
+ * since the last reset; synchronises on pending timing events. Returns the length written,
+ * or a negated SPLAX_ERR_* code. */
+int splax_profile_report(char *buf, int32_t len);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SPLAX_B200_H */

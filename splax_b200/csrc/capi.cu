@@ -1,0 +1,963 @@
+// C ABI of libsplax_b200 (declared in include/splax_b200.h): argument validation, the
+// per-device grow-only scratch cache (splax/_cache.py:52-164), the host orchestration of
+// sort_and_bin with its single count readback (splax/_rasterize/_sort/_sort.py:29-171) and
+// the launch sequences of the six FFI targets.
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/splax_b200.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace splax {
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(e == cudaErrorMemoryAllocation ? SPLAX_ERR_OUT_OF_MEMORY : SPLAX_ERR_CUDA,
+              std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define SPLAX_CUDA(call)                                  \
+  do {                                                    \
+    cudaError_t e_ = (call);                              \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #call);   \
+  } while (0)
+
+std::atomic<int64_t> g_fail_after{-1};
+
+struct DevBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
+};
+
+cudaError_t buf_free(DevBuf& b) {
+  cudaError_t e = cudaSuccess;
+  if (b.p) e = cudaFree(b.p);
+  b.p = nullptr;
+  b.bytes = 0;
+  return e;
+}
+
+// Grow-only device buffer; contents are not preserved across growth.
+cudaError_t buf_reserve(DevBuf& b, size_t bytes) {
+  if (bytes == 0) bytes = 16;
+  if (b.p && b.bytes >= bytes) return cudaSuccess;
+  buf_free(b);
+  int64_t left = g_fail_after.load();
+  if (left == 0) {
+    g_fail_after.store(-1);
+    return cudaErrorMemoryAllocation;
+  }
+  if (left > 0) g_fail_after.store(left - 1);
+  cudaError_t e = cudaMalloc(&b.p, bytes);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    b.p = nullptr;
+    return e;
+  }
+  b.bytes = bytes;
+  return cudaSuccess;
+}
+
+constexpr double kScratchHeadroom = 1.25;  // splax/_cache.py:149
+
+// ------------------------------------------------------------------ profiling (opt-in)
+std::atomic<bool> g_timing{false};
+std::atomic<bool> g_count_work{false};
+
+enum Kind { kProjectFwd, kProjectBwd, kDepthMinmax, kEmit, kRadixSort, kTileBins, kRasterFwd,
+            kRasterBwd, kNumKinds };
+const char* kKindNames[kNumKinds] = {"project_fwd", "project_bwd", "depth_minmax", "emit_keys",
+                                     "radix_sort", "tile_bins", "raster_fwd", "raster_bwd"};
+
+// CUDA-event timing of each launch sequence on the stream it runs on, resolved lazily.
+struct KernelTimer {
+  struct Pending {
+    int kind;
+    int kernels;
+    cudaEvent_t a, b;
+  };
+  std::vector<cudaEvent_t> pool;
+  std::vector<Pending> pending;
+  double ms[kNumKinds] = {};
+  int64_t launches[kNumKinds] = {};
+  int64_t kernels[kNumKinds] = {};
+
+  cudaEvent_t get() {
+    cudaEvent_t e = nullptr;
+    if (!pool.empty()) {
+      e = pool.back();
+      pool.pop_back();
+    } else {
+      cudaEventCreate(&e);
+    }
+    return e;
+  }
+  void begin(int kind, int nkernels, cudaStream_t s) {
+    if (!g_timing.load(std::memory_order_relaxed)) return;
+    Pending p{kind, nkernels, get(), get()};
+    cudaEventRecord(p.a, s);
+    pending.push_back(p);
+  }
+  void end(cudaStream_t s) {
+    if (!g_timing.load(std::memory_order_relaxed) || pending.empty()) return;
+    cudaEventRecord(pending.back().b, s);
+  }
+  void collect() {
+    for (const Pending& p : pending) {
+      float t = 0.0f;
+      if (cudaEventSynchronize(p.b) == cudaSuccess && cudaEventElapsedTime(&t, p.a, p.b) == cudaSuccess) {
+        ms[p.kind] += t;
+        launches[p.kind] += 1;
+        kernels[p.kind] += p.kernels;
+      }
+      pool.push_back(p.a);
+      pool.push_back(p.b);
+    }
+    pending.clear();
+  }
+  void reset() {
+    collect();
+    for (int k = 0; k < kNumKinds; ++k) {
+      ms[k] = 0.0;
+      launches[k] = 0;
+      kernels[k] = 0;
+    }
+  }
+};
+
+// Host-side work units for the roofline (what the launches processed).
+struct WorkUnits {
+  int64_t pairs_fwd = 0;       // (camera, gaussian) pairs projected
+  int64_t pairs_bwd = 0;       // pairs through the projection backward
+  int64_t intersections = 0;   // keys emitted and sorted
+  int64_t key_bytes = 0;       // sum of intersections * key size
+  int64_t sort_passes = 0;     // sum of intersections * radix passes
+  int64_t visible = 0;         // not tracked on the host (device counters below)
+  int64_t pixels_fwd = 0, pixels_bwd = 0;
+  int64_t bins = 0;
+};
+
+struct DeviceState {
+  std::mutex mu;
+  int device = -1;
+  // scratch entry keyed on the workload signature (B, n, tiles)
+  int64_t sig_B = -1, sig_n = -1, sig_T = -1;
+  int key_bits = 0;
+  int64_t isect_cap = 0;
+  DevBuf keys[2], vals[2], records, tile_bins, depth_mm, status;
+  // signature-independent pieces
+  DevBuf misc;        // [0] error word, [1] project ticket, [2..9] sort tile counters
+  DevBuf hist;        // radix histograms and offsets
+  DevBuf proj_status; // projection scan look-back words
+  int32_t* pinned = nullptr;  // [0] count, [1] error word
+  cudaEvent_t ev = nullptr;
+  DevBuf work;                // device work counters: fwd evals, fwd contribs, bwd evals, bwd contribs
+  KernelTimer timer;
+  WorkUnits units;
+
+  unsigned long long* work_fwd() {
+    return g_count_work.load() ? static_cast<unsigned long long*>(work.p) : nullptr;
+  }
+  unsigned long long* work_bwd() {
+    return g_count_work.load() ? static_cast<unsigned long long*>(work.p) + 2 : nullptr;
+  }
+
+  unsigned* err_word() { return static_cast<unsigned*>(misc.p); }
+  int* sort_counters() { return static_cast<int*>(misc.p) + 2; }
+
+  size_t bytes_held() const {
+    size_t s = 0;
+    for (const DevBuf* b : {&keys[0], &keys[1], &vals[0], &vals[1], &records, &tile_bins,
+                            &depth_mm, &status, &misc, &hist, &proj_status})
+      s += b->bytes;
+    return s;
+  }
+
+  void drop_entry() {
+    for (DevBuf* b : {&keys[0], &keys[1], &vals[0], &vals[1], &records, &tile_bins, &depth_mm,
+                      &status})
+      buf_free(*b);
+    sig_B = sig_n = sig_T = -1;
+    key_bits = 0;
+    isect_cap = 0;
+  }
+
+  int init() {
+    if (ev) return SPLAX_OK;
+    SPLAX_CUDA(buf_reserve(misc, 64));
+    SPLAX_CUDA(cudaMemset(misc.p, 0, 64));
+    SPLAX_CUDA(buf_reserve(hist, sizeof(uint32_t) * 2 * 8 * 256));
+    SPLAX_CUDA(buf_reserve(work, 4 * sizeof(unsigned long long)));
+    SPLAX_CUDA(cudaMemset(work.p, 0, 4 * sizeof(unsigned long long)));
+    SPLAX_CUDA(cudaMallocHost(&pinned, 2 * sizeof(int32_t)));
+    SPLAX_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    return SPLAX_OK;
+  }
+};
+
+std::mutex g_states_mu;
+std::vector<std::unique_ptr<DeviceState>> g_states;
+
+int current_state(DeviceState** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  std::lock_guard<std::mutex> lk(g_states_mu);
+  if (static_cast<int>(g_states.size()) <= dev) g_states.resize(dev + 1);
+  if (!g_states[dev]) {
+    g_states[dev] = std::make_unique<DeviceState>();
+    g_states[dev]->device = dev;
+  }
+  *out = g_states[dev].get();
+  return SPLAX_OK;
+}
+
+int bit_length(int64_t v) {
+  int b = 0;
+  while (v > 0) {
+    ++b;
+    v >>= 1;
+  }
+  return b;
+}
+
+const char* describe_device_error(unsigned w) {
+  if (w & kErrLookbackTimeout) return "a look-back wait exceeded its iteration limit";
+  if (w & kErrEmitCount)
+    return "emitted intersections disagree with cum_tiles_hit (geometry, map_opacities and "
+           "cum_tiles_hit must come from the same projection)";
+  if (w & kErrNegativeDepthKey)
+    return "a visible gaussian has a negative depth, which the 64-bit sort key cannot order "
+           "(use clip_thresh >= 0)";
+  if (w & kErrCountOverflow) return "the intersection count exceeds the int32 range";
+  if (w & kErrBinRange) return "a sorted key decoded to a tile bin outside the batch";
+  return "unknown device error";
+}
+
+int report_device_error(DeviceState& st, unsigned w, cudaStream_t stream) {
+  cudaMemsetAsync(st.err_word(), 0, sizeof(unsigned), stream);
+  int code = (w & kErrCountOverflow) ? SPLAX_ERR_COUNT_OVERFLOW : SPLAX_ERR_DEVICE;
+  return fail(code, std::string("device check failed: ") + describe_device_error(w));
+}
+
+struct SortOut {
+  const int32_t* gids = nullptr;
+  const void* keys = nullptr;
+  const int32_t* bins = nullptr;
+  const float4* records = nullptr;
+  int64_t count = 0;
+  int32_t tbx = 0, tby = 0, num_tiles = 0;
+  int key_bits = 0;
+};
+
+struct SortIn {
+  const float* xys;
+  const float* depths;
+  const int32_t* radii;
+  const float* conics;
+  const float* map_opacities;
+  int64_t map_rows;
+  const float* opacities;
+  int64_t opac_rows;
+  const float* colors;
+  int64_t color_rows;
+  const int32_t* cum;
+  int64_t n, B;
+  int32_t img_h, img_w;
+  int key_req;
+};
+
+// sort_and_bin (splax/_rasterize/_sort/_sort.py:29-171) plus the record packing.
+int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut& out) {
+  int rc = st.init();
+  if (rc) return rc;
+  const int32_t tbx = (in.img_w + kBlockWidth - 1) / kBlockWidth;
+  const int32_t tby = (in.img_h + kBlockWidth - 1) / kBlockWidth;
+  const int64_t num_tiles = static_cast<int64_t>(tbx) * tby;
+  const int tile_n_bits = bit_length(num_tiles - 1);
+  const int image_n_bits = bit_length(in.B - 1);
+  const int upper = tile_n_bits + image_n_bits;
+  const int depth_bits = 31 - upper;
+  const bool packed = in.key_req == 0 ? depth_bits >= 16 : in.key_req == 32;
+  if (!packed && upper > 32) {
+    char msg[256];
+    snprintf(msg, sizeof msg,
+             "batched intersection key overflow: image_n_bits(%d) + tile_n_bits(%d) = %d > 32 "
+             "(batch B=%lld, n_tiles=%lld). Reduce batch size or resolution.",
+             image_n_bits, tile_n_bits, upper, static_cast<long long>(in.B),
+             static_cast<long long>(num_tiles));
+    return fail(SPLAX_ERR_KEY_OVERFLOW, msg);
+  }
+  if (packed && depth_bits < 1)
+    return fail(SPLAX_ERR_KEY_OVERFLOW, "32-bit keys requested but image and tile ids leave no "
+                                        "depth bits");
+  const int64_t total = in.B * in.n;
+  const int64_t bins_len = in.B * num_tiles;
+  // scratch entry for this signature
+  if (st.sig_B != in.B || st.sig_n != in.n || st.sig_T != num_tiles) {
+    SPLAX_CUDA(cudaStreamSynchronize(stream));
+    st.drop_entry();
+    rc = 0;
+    cudaError_t e;
+    if ((e = buf_reserve(st.tile_bins, sizeof(int2) * bins_len)) != cudaSuccess ||
+        (e = buf_reserve(st.depth_mm, sizeof(int32_t) * 2 * (in.B > 0 ? in.B : 1))) !=
+            cudaSuccess ||
+        (e = buf_reserve(st.records, sizeof(float4) * kRecordFloat4 * (total > 0 ? total : 1))) !=
+            cudaSuccess) {
+      st.drop_entry();
+      return cuda_fail(e, "scratch allocation (tile bins, depth ranges, records)");
+    }
+    st.sig_B = in.B;
+    st.sig_n = in.n;
+    st.sig_T = num_tiles;
+  }
+  // the one device-to-host sync: intersection count and the device error word
+  SPLAX_CUDA(cudaMemcpyAsync(&st.pinned[0], in.cum + (total - 1), sizeof(int32_t),
+                             cudaMemcpyDeviceToHost, stream));
+  SPLAX_CUDA(cudaMemcpyAsync(&st.pinned[1], st.err_word(), sizeof(int32_t),
+                             cudaMemcpyDeviceToHost, stream));
+  SPLAX_CUDA(cudaEventRecord(st.ev, stream));
+  // count-independent work runs inside the sync bubble
+  SPLAX_CUDA(cudaMemsetAsync(st.tile_bins.p, 0, sizeof(int2) * bins_len, stream));
+  int32_t* depth_mm = static_cast<int32_t*>(st.depth_mm.p);
+  if (packed) {
+    st.timer.begin(kDepthMinmax, 2, stream);
+    launch_depth_minmax(in.depths, in.radii, total, in.n, static_cast<int32_t>(in.B), depth_mm,
+                        stream);
+    st.timer.end(stream);
+  }
+  SPLAX_CUDA(cudaEventSynchronize(st.ev));
+  const unsigned werr = static_cast<unsigned>(st.pinned[1]);
+  if (werr) return report_device_error(st, werr, stream);
+  const int64_t count = static_cast<int64_t>(st.pinned[0]);
+  if (count < 0)
+    return fail(SPLAX_ERR_COUNT_OVERFLOW,
+                "cum_tiles_hit[-1] is negative: the intersection count overflowed int32");
+  const int kb = packed ? 32 : 64;
+  const size_t key_size = packed ? 4 : 8;
+  if (st.isect_cap < count || st.key_bits != kb) {
+    const int64_t cap = std::max<int64_t>(static_cast<int64_t>(count * kScratchHeadroom) + 1,
+                                          st.key_bits == kb ? st.isect_cap : 0);
+    SPLAX_CUDA(cudaStreamSynchronize(stream));
+    for (DevBuf* b : {&st.keys[0], &st.keys[1], &st.vals[0], &st.vals[1], &st.status}) buf_free(*b);
+    st.isect_cap = 0;
+    const int64_t tiles = (cap + sort_tile_items(!packed) - 1) / sort_tile_items(!packed);
+    cudaError_t e;
+    if ((e = buf_reserve(st.keys[0], key_size * cap)) != cudaSuccess ||
+        (e = buf_reserve(st.keys[1], key_size * cap)) != cudaSuccess ||
+        (e = buf_reserve(st.vals[0], sizeof(int32_t) * cap)) != cudaSuccess ||
+        (e = buf_reserve(st.vals[1], sizeof(int32_t) * cap)) != cudaSuccess ||
+        (e = buf_reserve(st.status, sizeof(unsigned long long) * 256 * tiles)) != cudaSuccess) {
+      st.drop_entry();
+      return cuda_fail(e, "sort scratch allocation");
+    }
+    st.isect_cap = cap;
+  }
+  st.key_bits = kb;
+  out.tbx = tbx;
+  out.tby = tby;
+  out.num_tiles = static_cast<int32_t>(num_tiles);
+  out.key_bits = kb;
+  out.count = count;
+  out.bins = static_cast<const int32_t*>(st.tile_bins.p);
+  out.records = static_cast<const float4*>(st.records.p);
+  out.gids = static_cast<const int32_t*>(st.vals[0].p);
+  out.keys = st.keys[0].p;
+  if (count == 0) return SPLAX_OK;
+
+  EmitArgs ea;
+  ea.xys = in.xys;
+  ea.depths = in.depths;
+  ea.radii = in.radii;
+  ea.conics = in.conics;
+  ea.map_opacities = in.map_opacities;
+  ea.map_opac_rows = in.map_rows;
+  ea.opacities = in.opacities;
+  ea.opac_rows = in.opac_rows;
+  ea.colors = in.colors;
+  ea.color_rows = in.color_rows;
+  ea.cum = in.cum;
+  ea.n = in.n;
+  ea.total = total;
+  ea.count = count;
+  ea.tile_n_bits = tile_n_bits;
+  ea.depth_bits = depth_bits;
+  ea.tbx = tbx;
+  ea.tby = tby;
+  ea.depth_mm = depth_mm;
+  ea.keys = st.keys[0].p;
+  ea.vals = static_cast<int32_t*>(st.vals[0].p);
+  ea.records = in.colors ? static_cast<float4*>(st.records.p) : nullptr;
+  ea.err = st.err_word();
+  st.timer.begin(kEmit, 1, stream);
+  launch_emit(ea, !packed, stream);
+  st.timer.end(stream);
+
+  SortScratch ss;
+  ss.keys[0] = st.keys[0].p;
+  ss.keys[1] = st.keys[1].p;
+  ss.vals[0] = static_cast<int32_t*>(st.vals[0].p);
+  ss.vals[1] = static_cast<int32_t*>(st.vals[1].p);
+  ss.hist = static_cast<uint32_t*>(st.hist.p);
+  ss.status = static_cast<unsigned long long*>(st.status.p);
+  ss.status_words = static_cast<int64_t>(st.status.bytes / sizeof(unsigned long long));
+  ss.tile_counters = st.sort_counters();
+  ss.err = st.err_word();
+  const int bits = packed ? 31 : 32 + upper;
+  const int passes = (bits + 7) / 8;
+  st.timer.begin(kRadixSort, count > 1 ? 2 + passes : 0, stream);
+  const int fin = radix_sort_pairs(ss, !packed, count, bits, stream);
+  st.timer.end(stream);
+  out.gids = ss.vals[fin];
+  out.keys = ss.keys[fin];
+  st.timer.begin(kTileBins, 1, stream);
+  launch_tile_bins(out.keys, !packed, count, packed ? depth_bits : 32, tile_n_bits,
+                   static_cast<int32_t>(num_tiles), bins_len, static_cast<int32_t*>(st.tile_bins.p),
+                   st.err_word(), stream);
+  st.timer.end(stream);
+  st.units.intersections += count;
+  st.units.key_bytes += count * static_cast<int64_t>(key_size);
+  st.units.sort_passes += count > 1 ? count * passes : 0;
+  st.units.bins += bins_len;
+  SPLAX_CUDA(cudaGetLastError());
+  return SPLAX_OK;
+}
+
+bool sync_check_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("SPLAX_SYNC_CHECK");
+    return v && v[0] == '1';
+  }();
+  return on;
+}
+
+int finish(DeviceState& st, cudaStream_t stream) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
+  if (!sync_check_enabled()) return SPLAX_OK;
+  SPLAX_CUDA(cudaStreamSynchronize(stream));
+  unsigned w = 0;
+  SPLAX_CUDA(cudaMemcpy(&w, st.err_word(), sizeof(unsigned), cudaMemcpyDeviceToHost));
+  if (w) return report_device_error(st, w, stream);
+  return SPLAX_OK;
+}
+
+bool bad_rows(int64_t rows, int64_t n, int64_t total) {
+  // a per-gaussian operand is shared (n rows) or batched (total rows)
+  return !(rows == n || rows == total);
+}
+
+int rasterize_common(const float* colors, int64_t colors_rows, const float* opacities,
+                     int64_t opacities_rows, const float* map_opacities, int64_t map_rows,
+                     const float* background, int64_t background_rows, const float* xys,
+                     const float* depths, const int32_t* radii, const float* conics,
+                     const int32_t* cum, int64_t geom_rows, int32_t n, int32_t img_h,
+                     int32_t img_w, int64_t out_rows, int32_t key_bits, float* final_Ts,
+                     int32_t* final_idx, float* out_img, float* out_depth, cudaStream_t stream) {
+  if (n <= 0 || img_h <= 0 || img_w <= 0 || out_rows <= 0 || out_rows % img_h != 0)
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "rasterize: invalid n, image size or output rows");
+  const int64_t B = out_rows / img_h;
+  if (geom_rows != B * n)
+    return fail(SPLAX_ERR_INVALID_ARGUMENT,
+                "rasterize: projected geometry must have B*n rows for B = out_rows / img_h");
+  if (bad_rows(colors_rows, n, geom_rows) || bad_rows(opacities_rows, n, geom_rows) ||
+      bad_rows(map_rows, n, geom_rows) || !(background_rows == 1 || background_rows == B))
+    return fail(SPLAX_ERR_INVALID_ARGUMENT,
+                "rasterize: operand rows must be n or B*n (background 1 or B)");
+  if (key_bits != 0 && key_bits != 32 && key_bits != 64)
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "rasterize: key_bits must be 0, 32 or 64");
+  DeviceState* st;
+  int rc = current_state(&st);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(st->mu);
+  SortIn in{xys, depths, radii, conics, map_opacities, map_rows, opacities, opacities_rows,
+            colors, colors_rows, cum, n, B, img_h, img_w, key_bits};
+  SortOut so;
+  rc = sort_and_bin(*st, in, stream, so);
+  if (rc) return rc;
+  RasterFwdArgs ra;
+  ra.img_h = img_h;
+  ra.img_w = img_w;
+  ra.tbx = so.tbx;
+  ra.num_tiles = so.num_tiles;
+  ra.num_images = B;
+  ra.tile_bins = so.bins;
+  ra.gids = so.gids;
+  ra.records = so.records;
+  ra.num_records = B * static_cast<int64_t>(n);
+  ra.background = background;
+  ra.sel_bg = background_rows > 1;
+  ra.final_Ts = final_Ts;
+  ra.final_idx = final_idx;
+  ra.out_img = out_img;
+  ra.out_depth = out_depth;
+  ra.work = st->work_fwd();
+  st->timer.begin(kRasterFwd, 1, stream);
+  launch_raster_fwd(ra, stream);
+  st->timer.end(stream);
+  st->units.pixels_fwd += B * static_cast<int64_t>(img_h) * img_w;
+  return finish(*st, stream);
+}
+
+int rasterize_bwd_common(const float* colors, int64_t colors_rows, const float* opacities,
+                         int64_t opacities_rows, const float* map_opacities, int64_t map_rows,
+                         const float* background, int64_t background_rows, const float* xys,
+                         const float* depths, const int32_t* radii, const float* conics,
+                         const int32_t* cum, int64_t geom_rows, const float* final_Ts,
+                         const int32_t* final_idx, const float* v_out_img, int64_t v_out_rows,
+                         const float* v_out_depth, int64_t v_out_depth_rows, int32_t n,
+                         int32_t img_h, int32_t img_w, int64_t grad_rows, int32_t key_bits,
+                         float* v_colors, float* v_opacity, float* v_xy, float* v_conic,
+                         float* v_depths, cudaStream_t stream) {
+  if (n <= 0 || img_h <= 0 || img_w <= 0 || geom_rows <= 0 || geom_rows % n != 0 ||
+      grad_rows <= 0 || grad_rows % n != 0)
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "rasterize_bwd: invalid n, image size or rows");
+  const int64_t B_geom = geom_rows / n, B_out = grad_rows / n;
+  if (B_geom != 1 && B_geom != B_out)
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "rasterize_bwd: geometry batch must be 1 or B_out");
+  if (v_out_rows <= 0 || v_out_rows % img_h != 0 ||
+      (v_out_depth && (v_out_depth_rows <= 0 || v_out_depth_rows % img_h != 0)))
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "rasterize_bwd: cotangent rows must be k*img_h");
+  if (bad_rows(colors_rows, n, geom_rows) || bad_rows(opacities_rows, n, geom_rows) ||
+      bad_rows(map_rows, n, geom_rows) || !(background_rows == 1 || background_rows == B_out))
+    return fail(SPLAX_ERR_INVALID_ARGUMENT,
+                "rasterize_bwd: operand rows must be n or B*n (background 1 or B_out)");
+  if (key_bits != 0 && key_bits != 32 && key_bits != 64)
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "rasterize_bwd: key_bits must be 0, 32 or 64");
+  DeviceState* st;
+  int rc = current_state(&st);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(st->mu);
+  SPLAX_CUDA(cudaMemsetAsync(v_colors, 0, sizeof(float) * 3 * grad_rows, stream));
+  SPLAX_CUDA(cudaMemsetAsync(v_opacity, 0, sizeof(float) * grad_rows, stream));
+  SPLAX_CUDA(cudaMemsetAsync(v_xy, 0, sizeof(float) * 2 * grad_rows, stream));
+  SPLAX_CUDA(cudaMemsetAsync(v_conic, 0, sizeof(float) * 3 * grad_rows, stream));
+  if (v_depths) SPLAX_CUDA(cudaMemsetAsync(v_depths, 0, sizeof(float) * grad_rows, stream));
+  SortIn in{xys, depths, radii, conics, map_opacities, map_rows, opacities, opacities_rows,
+            colors, colors_rows, cum, n, B_geom, img_h, img_w, key_bits};
+  SortOut so;
+  rc = sort_and_bin(*st, in, stream, so);
+  if (rc) return rc;
+  if (so.count == 0) return finish(*st, stream);
+  RasterBwdArgs ba;
+  ba.img_h = img_h;
+  ba.img_w = img_w;
+  ba.tbx = so.tbx;
+  ba.num_tiles = so.num_tiles;
+  ba.n = n;
+  ba.B_out = B_out;
+  ba.sel_geom = B_geom > 1;
+  ba.sel_bg = background_rows > 1;
+  ba.vout_rows = v_out_rows;
+  ba.vdepth_rows = v_out_depth_rows;
+  ba.tile_bins = so.bins;
+  ba.gids = so.gids;
+  ba.records = so.records;
+  ba.num_records = B_geom * static_cast<int64_t>(n);
+  ba.background = background;
+  ba.final_Ts = final_Ts;
+  ba.final_idx = final_idx;
+  ba.v_out_img = v_out_img;
+  ba.v_out_depth = v_out_depth;
+  ba.v_colors = v_colors;
+  ba.v_opacity = v_opacity;
+  ba.v_xy = v_xy;
+  ba.v_conic = v_conic;
+  ba.v_depths = v_depths;
+  ba.work = st->work_bwd();
+  st->timer.begin(kRasterBwd, 1, stream);
+  launch_raster_bwd(ba, stream);
+  st->timer.end(stream);
+  st->units.pixels_bwd += B_out * static_cast<int64_t>(img_h) * img_w;
+  return finish(*st, stream);
+}
+
+}  // namespace
+}  // namespace splax
+
+using namespace splax;
+
+extern "C" {
+
+const char* splax_last_error(void) { return g_last_error.c_str(); }
+
+const char* splax_version(void) { return "splax_b200 0.1.0 (sm_100a)"; }
+
+int splax_project(const float* means3d, int64_t means3d_rows, const float* scales,
+                  int64_t scales_rows, const float* quats_xyzw, int64_t quats_rows,
+                  const float* viewmat, int64_t viewmat_rows, const float* opacities,
+                  int64_t opacities_rows, const float* gaussian_transforms,
+                  int64_t transforms_rows, const int32_t* transform_ids, int32_t num_gaussians,
+                  int32_t num_transforms, int32_t has_transforms, int32_t img_h, int32_t img_w,
+                  float fx, float fy, float cx, float cy, float glob_scale, float clip_thresh,
+                  int64_t total, float* xys, float* depths, int32_t* radii, float* conics,
+                  int32_t* num_tiles_hit, int32_t* cum_tiles_hit, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const int64_t n = num_gaussians;
+  if (n <= 0 || total <= 0 || total % n != 0 || img_h <= 0 || img_w <= 0)
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "project: invalid num_gaussians, total or image size");
+  const int64_t B = total / n;
+  if (bad_rows(means3d_rows, n, total) || bad_rows(scales_rows, n, total) ||
+      bad_rows(quats_rows, n, total) || bad_rows(opacities_rows, n, total) ||
+      !(viewmat_rows == 4 || viewmat_rows == 4 * B))
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "project: operand rows must be n or B*n (viewmat 4 or 4B)");
+  if (has_transforms &&
+      (num_transforms <= 0 ||
+       !(transforms_rows == num_transforms || transforms_rows == num_transforms * B) ||
+       transform_ids == nullptr))
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "project: transforms must have K or B*K matrices");
+  DeviceState* st;
+  int rc = current_state(&st);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(st->mu);
+  rc = st->init();
+  if (rc) return rc;
+  const int64_t tiles = project_scan_tiles(total);
+  // [ticket (8 bytes)] [look-back words]
+  SPLAX_CUDA(buf_reserve(st->proj_status, sizeof(unsigned long long) * (tiles + 1)));
+  SPLAX_CUDA(cudaMemsetAsync(st->proj_status.p, 0, sizeof(unsigned long long) * (tiles + 1), stream));
+  ProjectArgs a;
+  a.means = means3d;
+  a.scales = scales;
+  a.quats = quats_xyzw;
+  a.viewmat = viewmat;
+  a.opacities = opacities;
+  a.transforms = gaussian_transforms;
+  a.transform_ids = transform_ids;
+  a.n = n;
+  a.total = total;
+  a.num_transforms = num_transforms;
+  a.has_transforms = has_transforms != 0;
+  a.sel_means = means3d_rows > n;
+  a.sel_scales = scales_rows > n;
+  a.sel_quats = quats_rows > n;
+  a.sel_view = viewmat_rows > 4;
+  a.sel_opac = opacities_rows > n;
+  a.sel_transforms = transforms_rows > num_transforms;
+  a.img_h = img_h;
+  a.img_w = img_w;
+  a.fx = fx;
+  a.fy = fy;
+  a.cx = cx;
+  a.cy = cy;
+  a.glob_scale = glob_scale;
+  a.clip_thresh = clip_thresh;
+  a.xys = xys;
+  a.depths = depths;
+  a.radii = radii;
+  a.conics = conics;
+  a.num_tiles_hit = num_tiles_hit;
+  a.cum_tiles_hit = cum_tiles_hit;
+  unsigned long long* words = static_cast<unsigned long long*>(st->proj_status.p);
+  st->timer.begin(kProjectFwd, 1, stream);
+  launch_project_fwd(a, words + 1, reinterpret_cast<int*>(words), st->err_word(), stream);
+  st->timer.end(stream);
+  st->units.pairs_fwd += total;
+  return finish(*st, stream);
+}
+
+int splax_project_bwd(const float* means3d, int64_t means3d_rows, const float* scales,
+                      int64_t scales_rows, const float* quats_xyzw, int64_t quats_rows,
+                      const float* viewmat, int64_t viewmat_rows, const int32_t* radii,
+                      int64_t radii_rows, const float* conics, int64_t conics_rows,
+                      const float* v_xy, int64_t v_xy_rows, const float* v_depth,
+                      int64_t v_depth_rows, const float* v_conic, int64_t v_conic_rows,
+                      const float* gaussian_transforms, int64_t transforms_rows,
+                      const int32_t* transform_ids, int32_t num_gaussians, int32_t num_transforms,
+                      int32_t has_transforms, float fx, float fy, float glob_scale,
+                      int64_t out_rows, float* v_mean3d, float* v_scale, float* v_quat,
+                      float* v_viewmat, float* v_transforms, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const int64_t n = num_gaussians;
+  if (n <= 0 || out_rows <= 0 || out_rows % n != 0)
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "project_bwd: invalid num_gaussians or output rows");
+  const int64_t B = out_rows / n;
+  if (bad_rows(means3d_rows, n, out_rows) || bad_rows(scales_rows, n, out_rows) ||
+      bad_rows(quats_rows, n, out_rows) || bad_rows(radii_rows, n, out_rows) ||
+      bad_rows(conics_rows, n, out_rows) || bad_rows(v_xy_rows, n, out_rows) ||
+      bad_rows(v_depth_rows, n, out_rows) || bad_rows(v_conic_rows, n, out_rows) ||
+      !(viewmat_rows == 4 || viewmat_rows == 4 * B))
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "project_bwd: operand rows must be n or B*n");
+  const int32_t K = num_transforms > 0 ? num_transforms : 1;
+  if (has_transforms && !(transforms_rows == K || transforms_rows == K * B))
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "project_bwd: transforms must have K or B*K matrices");
+  DeviceState* st;
+  int rc = current_state(&st);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(st->mu);
+  rc = st->init();
+  if (rc) return rc;
+  SPLAX_CUDA(cudaMemsetAsync(v_viewmat, 0, sizeof(float) * 16 * B, stream));
+  SPLAX_CUDA(cudaMemsetAsync(v_transforms, 0, sizeof(float) * 16 * K * B, stream));
+  ProjectBwdArgs a;
+  a.means = means3d;
+  a.scales = scales;
+  a.quats = quats_xyzw;
+  a.viewmat = viewmat;
+  a.radii = radii;
+  a.conics = conics;
+  a.v_xy = v_xy;
+  a.v_depth = v_depth;
+  a.v_conic = v_conic;
+  a.transforms = gaussian_transforms;
+  a.transform_ids = transform_ids;
+  a.n = n;
+  a.B = B;
+  a.num_transforms = K;
+  a.has_transforms = has_transforms != 0;
+  a.sel_means = means3d_rows > n;
+  a.sel_scales = scales_rows > n;
+  a.sel_quats = quats_rows > n;
+  a.sel_view = viewmat_rows > 4;
+  a.sel_radii = radii_rows > n;
+  a.sel_conics = conics_rows > n;
+  a.sel_vxy = v_xy_rows > n;
+  a.sel_vdepth = v_depth_rows > n;
+  a.sel_vconic = v_conic_rows > n;
+  a.sel_transforms = transforms_rows > K;
+  a.fx = fx;
+  a.fy = fy;
+  a.glob_scale = glob_scale;
+  a.v_mean3d = v_mean3d;
+  a.v_scale = v_scale;
+  a.v_quat = v_quat;
+  a.v_viewmat = v_viewmat;
+  a.v_transforms = v_transforms;
+  st->timer.begin(kProjectBwd, 1, stream);
+  launch_project_bwd(a, stream);
+  st->timer.end(stream);
+  st->units.pairs_bwd += out_rows;
+  return finish(*st, stream);
+}
+
+int splax_rasterize(const float* colors, int64_t colors_rows, const float* opacities,
+                    int64_t opacities_rows, const float* map_opacities, int64_t map_opacities_rows,
+                    const float* background, int64_t background_rows, const float* xys,
+                    const float* depths, const int32_t* radii, const float* conics,
+                    const int32_t* cum_tiles_hit, int64_t geom_rows, int32_t num_gaussians,
+                    int32_t img_h, int32_t img_w, int64_t out_rows, int32_t key_bits,
+                    float* final_Ts, int32_t* final_idx, float* out_img, void* stream) {
+  return rasterize_common(colors, colors_rows, opacities, opacities_rows, map_opacities,
+                          map_opacities_rows, background, background_rows, xys, depths, radii,
+                          conics, cum_tiles_hit, geom_rows, num_gaussians, img_h, img_w, out_rows,
+                          key_bits, final_Ts, final_idx, out_img, nullptr,
+                          static_cast<cudaStream_t>(stream));
+}
+
+int splax_rasterize_depth(const float* colors, int64_t colors_rows, const float* opacities,
+                          int64_t opacities_rows, const float* map_opacities,
+                          int64_t map_opacities_rows, const float* background,
+                          int64_t background_rows, const float* xys, const float* depths,
+                          const int32_t* radii, const float* conics, const int32_t* cum_tiles_hit,
+                          int64_t geom_rows, int32_t num_gaussians, int32_t img_h, int32_t img_w,
+                          int64_t out_rows, int32_t key_bits, float* final_Ts, int32_t* final_idx,
+                          float* out_img, float* out_depth, void* stream) {
+  if (!out_depth) return fail(SPLAX_ERR_INVALID_ARGUMENT, "rasterize_depth: out_depth is NULL");
+  return rasterize_common(colors, colors_rows, opacities, opacities_rows, map_opacities,
+                          map_opacities_rows, background, background_rows, xys, depths, radii,
+                          conics, cum_tiles_hit, geom_rows, num_gaussians, img_h, img_w, out_rows,
+                          key_bits, final_Ts, final_idx, out_img, out_depth,
+                          static_cast<cudaStream_t>(stream));
+}
+
+int splax_rasterize_bwd(const float* colors, int64_t colors_rows, const float* opacities,
+                        int64_t opacities_rows, const float* map_opacities,
+                        int64_t map_opacities_rows, const float* background,
+                        int64_t background_rows, const float* xys, const float* depths,
+                        const int32_t* radii, const float* conics, const int32_t* cum_tiles_hit,
+                        int64_t geom_rows, const float* final_Ts, const int32_t* final_idx,
+                        const float* v_out_img, int64_t v_out_rows, int32_t num_gaussians,
+                        int32_t img_h, int32_t img_w, int64_t grad_rows, int32_t key_bits,
+                        float* v_colors, float* v_opacity, float* v_xy, float* v_conic,
+                        void* stream) {
+  return rasterize_bwd_common(colors, colors_rows, opacities, opacities_rows, map_opacities,
+                              map_opacities_rows, background, background_rows, xys, depths,
+                              radii, conics, cum_tiles_hit, geom_rows, final_Ts, final_idx,
+                              v_out_img, v_out_rows, nullptr, 0, num_gaussians, img_h, img_w,
+                              grad_rows, key_bits, v_colors, v_opacity, v_xy, v_conic, nullptr,
+                              static_cast<cudaStream_t>(stream));
+}
+
+int splax_rasterize_bwd_depth(const float* colors, int64_t colors_rows, const float* opacities,
+                              int64_t opacities_rows, const float* map_opacities,
+                              int64_t map_opacities_rows, const float* background,
+                              int64_t background_rows, const float* xys, const float* depths,
+                              const int32_t* radii, const float* conics,
+                              const int32_t* cum_tiles_hit, int64_t geom_rows,
+                              const float* final_Ts, const int32_t* final_idx,
+                              const float* v_out_img, int64_t v_out_rows,
+                              const float* v_out_depth, int64_t v_out_depth_rows,
+                              int32_t num_gaussians, int32_t img_h, int32_t img_w,
+                              int64_t grad_rows, int32_t key_bits, float* v_colors,
+                              float* v_opacity, float* v_xy, float* v_conic, float* v_depths,
+                              void* stream) {
+  if (!v_out_depth || !v_depths)
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "rasterize_bwd_depth: depth buffers are NULL");
+  return rasterize_bwd_common(colors, colors_rows, opacities, opacities_rows, map_opacities,
+                              map_opacities_rows, background, background_rows, xys, depths,
+                              radii, conics, cum_tiles_hit, geom_rows, final_Ts, final_idx,
+                              v_out_img, v_out_rows, v_out_depth, v_out_depth_rows, num_gaussians,
+                              img_h, img_w, grad_rows, key_bits, v_colors, v_opacity, v_xy,
+                              v_conic, v_depths, static_cast<cudaStream_t>(stream));
+}
+
+int splax_sort_and_bin(const float* xys, const float* depths, const int32_t* radii,
+                       const float* conics, const float* map_opacities,
+                       int64_t map_opacities_rows, const int32_t* cum_tiles_hit,
+                       int32_t num_gaussians, int32_t num_images, int32_t img_h, int32_t img_w,
+                       int32_t key_bits, int32_t* gaussian_ids, int64_t gaussian_ids_cap,
+                       int64_t* sorted_keys, int32_t* tile_bins, int64_t* num_intersects,
+                       int32_t* used_key_bits, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (num_gaussians <= 0 || num_images <= 0 || img_h <= 0 || img_w <= 0)
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "sort_and_bin: invalid sizes");
+  const int64_t total = static_cast<int64_t>(num_images) * num_gaussians;
+  if (bad_rows(map_opacities_rows, num_gaussians, total))
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "sort_and_bin: map_opacities rows must be n or B*n");
+  DeviceState* st;
+  int rc = current_state(&st);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(st->mu);
+  // no colours: the blend records are not packed
+  SortIn in{xys, depths, radii, conics, map_opacities, map_opacities_rows, nullptr, 1, nullptr, 1,
+            cum_tiles_hit, num_gaussians, num_images, img_h, img_w, key_bits};
+  SortOut so;
+  rc = sort_and_bin(*st, in, stream, so);
+  if (rc) return rc;
+  if (so.count > gaussian_ids_cap)
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "sort_and_bin: gaussian_ids capacity too small");
+  if (so.count > 0) {
+    SPLAX_CUDA(cudaMemcpyAsync(gaussian_ids, so.gids, sizeof(int32_t) * so.count,
+                               cudaMemcpyDeviceToDevice, stream));
+  }
+  SPLAX_CUDA(cudaMemcpyAsync(tile_bins, so.bins,
+                             sizeof(int2) * static_cast<int64_t>(num_images) * so.num_tiles,
+                             cudaMemcpyDeviceToDevice, stream));
+  if (sorted_keys && so.count > 0) {
+    // widen to int64 on the host side of the caller's buffer: copy raw, then expand
+    if (so.key_bits == 64) {
+      SPLAX_CUDA(cudaMemcpyAsync(sorted_keys, so.keys, sizeof(int64_t) * so.count,
+                                 cudaMemcpyDeviceToDevice, stream));
+    } else {
+      SPLAX_CUDA(cudaMemcpy2DAsync(sorted_keys, sizeof(int64_t), so.keys, sizeof(int32_t),
+                                   sizeof(int32_t), so.count, cudaMemcpyDeviceToDevice, stream));
+      SPLAX_CUDA(cudaMemset2DAsync(reinterpret_cast<char*>(sorted_keys) + 4, sizeof(int64_t), 0,
+                                   sizeof(int32_t), so.count, stream));
+    }
+  }
+  *num_intersects = so.count;
+  *used_key_bits = so.key_bits;
+  return finish(*st, stream);
+}
+
+void splax_clear_cache(void) {
+  std::lock_guard<std::mutex> lk(g_states_mu);
+  int prev = 0;
+  cudaGetDevice(&prev);
+  for (auto& s : g_states) {
+    if (!s) continue;
+    std::lock_guard<std::mutex> lk2(s->mu);
+    if (cudaSetDevice(s->device) != cudaSuccess) continue;
+    cudaDeviceSynchronize();
+    s->drop_entry();
+  }
+  cudaSetDevice(prev);
+}
+
+int splax_scratch_info(int64_t* out, int32_t out_len) {
+  DeviceState* st;
+  int rc = current_state(&st);
+  if (rc) return -rc;
+  std::lock_guard<std::mutex> lk(st->mu);
+  const int64_t vals[6] = {st->isect_cap, st->key_bits, static_cast<int64_t>(st->bytes_held()),
+                           st->sig_B, st->sig_n, st->sig_T};
+  int k = 0;
+  for (; k < out_len && k < 6; ++k) out[k] = vals[k];
+  return k;
+}
+
+int splax_check_device_errors(void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  DeviceState* st;
+  int rc = current_state(&st);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(st->mu);
+  if (!st->ev) return SPLAX_OK;
+  SPLAX_CUDA(cudaStreamSynchronize(stream));
+  unsigned w = 0;
+  SPLAX_CUDA(cudaMemcpy(&w, st->err_word(), sizeof(unsigned), cudaMemcpyDeviceToHost));
+  if (w) return report_device_error(*st, w, stream);
+  return SPLAX_OK;
+}
+
+void splax_debug_fail_alloc_after(int64_t successes) { g_fail_after.store(successes); }
+
+void splax_profile_enable(int32_t timing, int32_t count_work) {
+  g_timing.store(timing != 0);
+  g_count_work.store(count_work != 0);
+}
+
+int splax_profile_reset(void) {
+  DeviceState* st;
+  int rc = current_state(&st);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(st->mu);
+  rc = st->init();
+  if (rc) return rc;
+  st->timer.reset();
+  st->units = WorkUnits{};
+  SPLAX_CUDA(cudaMemset(st->work.p, 0, 4 * sizeof(unsigned long long)));
+  return SPLAX_OK;
+}
+
+int splax_profile_report(char* buf, int32_t len) {
+  DeviceState* st;
+  int rc = current_state(&st);
+  if (rc) return -rc;
+  std::lock_guard<std::mutex> lk(st->mu);
+  rc = st->init();
+  if (rc) return -rc;
+  st->timer.collect();
+  unsigned long long w[4] = {0, 0, 0, 0};
+  if (cudaMemcpy(w, st->work.p, sizeof(w), cudaMemcpyDeviceToHost) != cudaSuccess) return -SPLAX_ERR_CUDA;
+  std::string js = "{\"kernels\": {";
+  char tmp[256];
+  for (int k = 0; k < kNumKinds; ++k) {
+    snprintf(tmp, sizeof tmp, "%s\"%s\": {\"launches\": %lld, \"kernels\": %lld, \"ms\": %.6f}",
+             k ? ", " : "", kKindNames[k], static_cast<long long>(st->timer.launches[k]),
+             static_cast<long long>(st->timer.kernels[k]), st->timer.ms[k]);
+    js += tmp;
+  }
+  const WorkUnits& u = st->units;
+  snprintf(tmp, sizeof tmp,
+           "}, \"units\": {\"pairs_fwd\": %lld, \"pairs_bwd\": %lld, \"intersections\": %lld, "
+           "\"key_bytes\": %lld, \"sort_pass_keys\": %lld, \"bins\": %lld, ",
+           (long long)u.pairs_fwd, (long long)u.pairs_bwd, (long long)u.intersections,
+           (long long)u.key_bytes, (long long)u.sort_passes, (long long)u.bins);
+  js += tmp;
+  snprintf(tmp, sizeof tmp,
+           "\"pixels_fwd\": %lld, \"pixels_bwd\": %lld, \"fwd_evals\": %llu, "
+           "\"fwd_contribs\": %llu, \"bwd_evals\": %llu, \"bwd_contribs\": %llu}}",
+           (long long)u.pixels_fwd, (long long)u.pixels_bwd, w[0], w[1], w[2], w[3]);
+  js += tmp;
+  if (static_cast<int32_t>(js.size()) + 1 > len) return -SPLAX_ERR_INVALID_ARGUMENT;
+  memcpy(buf, js.c_str(), js.size() + 1);
+  return static_cast<int>(js.size());
+}
+
+}  // extern "C"

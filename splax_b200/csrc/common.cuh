@@ -1,0 +1,239 @@
+// Shared device helpers of the splax_b200 kernels: constants, the deterministic logarithm,
+// saturating float->int truncation and the opacity-aware ellipse tile walk.
+//
+// Files that produce integer outputs (project.cu, sort.cu) are compiled with --fmad=false and
+// IEEE division / square root, so every float operation below rounds exactly as written and
+// the tile counts, radii and keys are bit-identical to the C oracle's restatement.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace splax {
+
+// splax/_intersect.py:17-20, splax/_rasterize/_kernels.py:188-192
+constexpr int kBlockWidth = 16;            // 16x16 pixel tiles
+constexpr int kBlockSize = 256;            // pixels per tile
+constexpr float kGaussianExtendSq = static_cast<float>(3.33 * 3.33);  // rounded to fp32
+constexpr float kAlphaThreshold = 1.0f / 255.0f;
+constexpr float kAlphaMax = 0.999f;
+constexpr float kTransmittanceMin = 1e-4f;
+
+// Device error word bits (read back by the host after a launch sequence).
+constexpr unsigned kErrLookbackTimeout = 1u << 0;  // a bounded spin-wait gave up
+constexpr unsigned kErrEmitCount = 1u << 1;        // emission disagreed with cum_tiles_hit
+constexpr unsigned kErrNegativeDepthKey = 1u << 2; // 64-bit key of a negative depth
+constexpr unsigned kErrCountOverflow = 1u << 3;    // intersections exceed int32
+constexpr unsigned kErrBinRange = 1u << 4;         // a sorted key decoded outside B*T bins
+
+constexpr long long kSpinLimit = 1ll << 24;  // iterations before a look-back wait gives up
+
+__device__ __forceinline__ int32_t f2i(float x) {
+  // cvt.rzi.s32.f32: truncation, saturating, NaN -> 0 (what wp.int32(x) does on the GPU)
+  return static_cast<int32_t>(x);
+}
+__device__ __forceinline__ float fmin_w(float a, float b) { return a < b ? a : b; }
+__device__ __forceinline__ float fmax_w(float a, float b) { return a > b ? a : b; }
+__device__ __forceinline__ int32_t imin(int32_t a, int32_t b) { return a < b ? a : b; }
+__device__ __forceinline__ int32_t imax(int32_t a, int32_t b) { return a > b ? a : b; }
+
+// Natural logarithm: atanh series log(m) = 2 atanh((m-1)/(m+1)) (Abramowitz & Stegun
+// 4.1.27) on m in [sqrt(1/2), sqrt(2)), Cody-Waite split of ln 2 for the exponent. Written as
+// plain IEEE operations in a fixed order so the integer tile walk it feeds is reproducible
+// on any IEEE fp32 host.
+__device__ __forceinline__ float splat_logf(float x) {
+  if (!(x > 0.0f)) return x == 0.0f ? -__int_as_float(0x7f800000) : __int_as_float(0x7fc00000);
+  if (x == __int_as_float(0x7f800000)) return x;
+  int32_t e = 0;
+  uint32_t bits = __float_as_uint(x);
+  if (bits < 0x00800000u) {
+    x = __fmul_rn(x, 8388608.0f);
+    bits = __float_as_uint(x);
+    e = -23;
+  }
+  e += static_cast<int32_t>(bits >> 23) - 127;
+  float m = __uint_as_float((bits & 0x007fffffu) | 0x3f800000u);
+  if (m > 1.41421356f) {
+    m = __fmul_rn(m, 0.5f);
+    e += 1;
+  }
+  float s = __fdiv_rn(__fsub_rn(m, 1.0f), __fadd_rn(m, 1.0f));
+  float s2 = __fmul_rn(s, s);
+  float p = 0.0909090936f;
+  p = __fadd_rn(__fmul_rn(p, s2), 0.111111112f);
+  p = __fadd_rn(__fmul_rn(p, s2), 0.142857149f);
+  p = __fadd_rn(__fmul_rn(p, s2), 0.200000003f);
+  p = __fadd_rn(__fmul_rn(p, s2), 0.333333343f);
+  p = __fadd_rn(__fmul_rn(p, s2), 1.0f);
+  float fe = static_cast<float>(e);
+  float lm = __fmul_rn(__fmul_rn(2.0f, s), p);
+  return __fadd_rn(__fmul_rn(fe, 0.693145751953125f),
+                   __fadd_rn(lm, __fmul_rn(fe, 1.42860677e-06f)));
+}
+
+// Opacity-aware isocontour level t = min(3.33^2, 2 ln(opac / (1/255))),
+// splax/_project/_kernels.py:227.
+__device__ __forceinline__ float iso_level(float opac) {
+  return fmin_w(kGaussianExtendSq, 2.0f * splat_logf(opac / kAlphaThreshold));
+}
+
+// Tight ellipse and its tile walk state (splax/_intersect.py:23-107). Component 0 of the
+// bbox / rect pairs is the walk's outer axis.
+struct Ellipse {
+  float A, B, C, disc, t, px, py;
+  float bmin0, bmin1, bmax0, bmax1, amin1, amax1;
+  int32_t rmin0, rmin1, rmax0, rmax1;
+  bool valid, isY;
+};
+
+__device__ __forceinline__ void ellipse_init(float A, float B, float C, float t, float px,
+                                             float py, int32_t tile_w, int32_t tile_h,
+                                             Ellipse& s) {
+  s.valid = false;
+  s.isY = false;
+  s.A = A; s.B = B; s.C = C; s.t = t; s.px = px; s.py = py;
+  float disc = B * B - A * C;
+  s.disc = disc;
+  float nt = -t / disc;
+  float x_ext = sqrtf(nt * C);
+  float y_ext = sqrtf(nt * A);
+  float bminx = px - x_ext, bminy = py - y_ext;
+  float bmaxx = px + x_ext, bmaxy = py + y_ext;
+  float bxc = B * x_ext / C;
+  float bya = B * y_ext / A;
+  float aminx = py + bxc, aminy = px + bya;  // bbox_argmin = (py + Bx/C, px + By/A)
+  float amaxx = py - bxc, amaxy = px - bya;
+  const float ts = static_cast<float>(kBlockWidth);
+  int32_t rminx = imax(0, imin(tile_w, f2i(bminx / ts)));
+  int32_t rminy = imax(0, imin(tile_h, f2i(bminy / ts)));
+  int32_t rmaxx = imax(0, imin(tile_w, f2i(bmaxx / ts + 1.0f)));
+  int32_t rmaxy = imax(0, imin(tile_h, f2i(bmaxy / ts + 1.0f)));
+  int32_t xs = rmaxx - rminx, ys = rmaxy - rminy;
+  if (ys * xs == 0) return;
+  bool isY = ys < xs;
+  s.isY = isY;
+  if (isY) {
+    s.rmin0 = rminy; s.rmin1 = rminx; s.rmax0 = rmaxy; s.rmax1 = rmaxx;
+    s.bmin0 = bminy; s.bmin1 = bminx; s.bmax0 = bmaxy; s.bmax1 = bmaxx;
+    s.amin1 = aminx; s.amax1 = amaxx;
+  } else {
+    s.rmin0 = rminx; s.rmin1 = rminy; s.rmax0 = rmaxx; s.rmax1 = rmaxy;
+    s.bmin0 = bminx; s.bmin1 = bminy; s.bmax0 = bmaxx; s.bmax1 = bmaxy;
+    s.amin1 = aminy; s.amax1 = amaxy;
+  }
+  s.valid = true;
+}
+
+// Cross-axis extent of the ellipse at one line of the outer axis (splax/_intersect.py:110-133)
+__device__ __forceinline__ void ellipse_intersect(const Ellipse& s, float coord, float& lo,
+                                                  float& hi) {
+  float pu = s.isY ? s.py : s.px;
+  float pv = s.isY ? s.px : s.py;
+  float coeff = s.isY ? s.A : s.C;
+  float h = coord - pu;
+  float sq = sqrtf(s.disc * h * h + s.t * coeff);
+  float bh = (-s.B) * h;
+  lo = (bh - sq) / coeff + pv;
+  hi = (bh + sq) / coeff + pv;
+}
+
+// Leading line of the walk (splax/_intersect.py:136-143)
+__device__ __forceinline__ void ellipse_init_span(const Ellipse& s, float& i0, float& i1) {
+  float line0 = static_cast<float>(s.rmin0) * static_cast<float>(kBlockWidth);
+  if (s.bmin0 <= line0) {
+    ellipse_intersect(s, line0, i0, i1);
+    return;
+  }
+  i0 = s.bmax1;
+  i1 = s.bmin1;
+}
+
+// One outer column: [mn, mx) cross-axis tiles; rolls the intersect pair (splax/_intersect.py:
+// 146-169).
+__device__ __forceinline__ void ellipse_column(int32_t u, const Ellipse& s, float& i0,
+                                               float& i1, int32_t& mn, int32_t& mx) {
+  const float block = static_cast<float>(kBlockWidth);
+  float min_line = static_cast<float>(u) * block;
+  float max_line = min_line + block;
+  float j0 = i0, j1 = i1;
+  if (max_line <= s.bmax0) ellipse_intersect(s, max_line, j0, j1);
+  float emin = (min_line <= s.amin1 && s.amin1 < max_line) ? s.bmin1 : fmin_w(i0, j0);
+  float emax = (min_line <= s.amax1 && s.amax1 < max_line) ? s.bmax1 : fmax_w(i1, j1);
+  mn = imax(s.rmin1, imin(s.rmax1, f2i(emin / block)));
+  mx = imin(s.rmax1, imax(s.rmin1, f2i(emax / block + 1.0f)));
+  i0 = j0;
+  i1 = j1;
+}
+
+__device__ __forceinline__ int32_t ellipse_tile_count(const Ellipse& s) {
+  if (!s.valid) return 0;
+  float i0, i1;
+  ellipse_init_span(s, i0, i1);
+  int32_t count = 0;
+  for (int32_t u = s.rmin0; u < s.rmax0; ++u) {
+    int32_t mn, mx;
+    ellipse_column(u, s, i0, i1, mn, mx);
+    count += mx - mn;
+  }
+  return count;
+}
+
+// Ordered-integer image of a float, so atomicMin / atomicMax on int32 order like floats.
+__device__ __forceinline__ int32_t float_to_ordered(float f) {
+  int32_t i = __float_as_int(f);
+  return i >= 0 ? i : i ^ 0x7fffffff;
+}
+__device__ __forceinline__ float ordered_to_float(int32_t i) {
+  return __int_as_float(i >= 0 ? i : i ^ 0x7fffffff);
+}
+
+// Release / acquire accesses for look-back status words.
+__device__ __forceinline__ void st_release(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Warp reduce-scatter of K per-lane values: after the call, every lane whose return value c
+// is >= 0 and whose lane bit 0 is clear holds in v[0] the warp-wide sum of component c (each
+// component has exactly one such holder). A butterfly that halves the slot count at every
+// exchange, so K values cost about K shuffles instead of 5K for K full reductions.
+template <int K, int OFF>
+struct ReduceScatter {
+  static __device__ __forceinline__ void run(float* v, int lane, int& comp, int& real) {
+    if constexpr (K == 1) {
+#pragma unroll
+      for (int off = OFF; off > 0; off >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
+    } else {
+      constexpr int H = (K + 1) / 2;
+      const bool bit = (lane & OFF) != 0;
+#pragma unroll
+      for (int j = 0; j < H; ++j) {
+        float lo = v[j];
+        float hi = (j + H < K) ? v[j + H] : 0.0f;
+        float recv = __shfl_xor_sync(0xffffffffu, bit ? lo : hi, OFF);
+        v[j] = (bit ? hi : lo) + recv;
+      }
+      if (bit) {
+        comp += H;
+        real = real - H;
+      } else {
+        real = real < H ? real : H;
+      }
+      ReduceScatter<H, OFF / 2>::run(v, lane, comp, real);
+    }
+  }
+};
+
+template <int K>
+__device__ __forceinline__ int warp_reduce_scatter(float (&v)[K], int lane) {
+  static_assert(K >= 1 && K <= 32, "1..32 components");
+  int comp = 0, real = K;
+  ReduceScatter<K, 16>::run(v, lane, comp, real);
+  return (real >= 1 && (lane & 1) == 0) ? comp : -1;
+}
+
+}  // namespace splax

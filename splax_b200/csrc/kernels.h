@@ -1,0 +1,150 @@
+// Kernel argument blocks and launchers shared between the .cu files of libsplax_b200.
+// Host-only interface: the C-ABI in capi.cu fills these from the caller's pointers and sizes.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace splax {
+
+struct ProjectArgs {
+  const float* means;
+  const float* scales;
+  const float* quats;  // xyzw
+  const float* viewmat;
+  const float* opacities;
+  const float* transforms;
+  const int32_t* transform_ids;
+  int64_t n, total;
+  int32_t num_transforms;
+  bool has_transforms, sel_means, sel_scales, sel_quats, sel_view, sel_opac, sel_transforms;
+  int32_t img_h, img_w;
+  float fx, fy, cx, cy, glob_scale, clip_thresh;
+  float* xys;
+  float* depths;
+  int32_t* radii;
+  float* conics;
+  int32_t* num_tiles_hit;
+  int32_t* cum_tiles_hit;
+};
+
+struct ProjectBwdArgs {
+  const float* means;
+  const float* scales;
+  const float* quats;
+  const float* viewmat;
+  const int32_t* radii;
+  const float* conics;
+  const float* v_xy;
+  const float* v_depth;
+  const float* v_conic;
+  const float* transforms;
+  const int32_t* transform_ids;
+  int64_t n, B;
+  int32_t num_transforms;
+  bool has_transforms, sel_means, sel_scales, sel_quats, sel_view, sel_radii, sel_conics,
+      sel_vxy, sel_vdepth, sel_vconic, sel_transforms;
+  float fx, fy, glob_scale;
+  float* v_mean3d;
+  float* v_scale;
+  float* v_quat;
+  float* v_viewmat;     // (B, 4, 4), zeroed by the caller
+  float* v_transforms;  // (B, K, 4, 4), zeroed by the caller
+};
+
+// Per-gaussian record staged by the blend kernels: 3 x float4 =
+// (x, y, conic_a, conic_b), (conic_c, opacity, r, g), (b, depth, 0, 0).
+constexpr int kRecordFloat4 = 3;
+
+struct EmitArgs {
+  const float* xys;
+  const float* depths;
+  const int32_t* radii;
+  const float* conics;
+  const float* map_opacities;
+  int64_t map_opac_rows;
+  const float* opacities;  // blend opacities, packed into the record
+  int64_t opac_rows;
+  const float* colors;
+  int64_t color_rows;
+  const int32_t* cum;
+  int64_t n, total;
+  int64_t count;  // intersections (cum[total-1]); emission never writes past it
+  int32_t tile_n_bits, depth_bits, tbx, tby;
+  const int32_t* depth_mm;  // ordered-int per-image [min, max] (32-bit keys only)
+  void* keys;               // uint32 or uint64 keys
+  int32_t* vals;
+  float4* records;
+  unsigned* err;
+};
+
+void launch_project_fwd(const ProjectArgs& a, unsigned long long* status, int* ticket,
+                        unsigned* err, cudaStream_t stream);
+int64_t project_scan_tiles(int64_t total);
+void launch_project_bwd(const ProjectBwdArgs& a, cudaStream_t stream);
+
+// sort.cu
+void launch_depth_minmax(const float* depths, const int32_t* radii, int64_t total, int64_t n,
+                         int32_t B, int32_t* depth_mm, cudaStream_t stream);
+void launch_emit(const EmitArgs& a, bool key64, cudaStream_t stream);
+// Onesweep radix sort of (key, value) pairs over `bits` low key bits, ping-ponging between
+// the two buffers; returns the index (0 or 1) of the buffer holding the result.
+struct SortScratch {
+  void* keys[2];
+  int32_t* vals[2];
+  uint32_t* hist;                 // [passes][256] counts, then [passes][256] offsets
+  unsigned long long* status;     // look-back words, status_words entries
+  int64_t status_words;
+  int* tile_counters;             // one per pass
+  unsigned* err;
+};
+int sort_tile_items(bool key64);
+int radix_sort_pairs(const SortScratch& s, bool key64, int64_t count, int bits,
+                     cudaStream_t stream);
+void launch_tile_bins(const void* keys, bool key64, int64_t count, int shift, int32_t tile_n_bits,
+                      int32_t num_tiles, int64_t num_bins, int32_t* tile_bins, unsigned* err,
+                      cudaStream_t stream);
+
+// raster_fwd.cu
+struct RasterFwdArgs {
+  int32_t img_h, img_w, tbx, num_tiles;
+  int64_t num_images;
+  const int32_t* tile_bins;  // int2 per bin
+  const int32_t* gids;
+  const float4* records;
+  int64_t num_records;  // flat ids outside [0, num_records) are staged as transparent
+  const float* background;
+  bool sel_bg;
+  float* final_Ts;
+  int32_t* final_idx;
+  float* out_img;
+  float* out_depth;  // nullptr for the plain blend
+  unsigned long long* work;  // optional: [0] evaluations, [1] contributions
+};
+void launch_raster_fwd(const RasterFwdArgs& a, cudaStream_t stream);
+
+// raster_bwd.cu
+struct RasterBwdArgs {
+  int32_t img_h, img_w, tbx, num_tiles;
+  int64_t n, B_out;
+  bool sel_geom, sel_bg;
+  int64_t vout_rows, vdepth_rows;
+  const int32_t* tile_bins;
+  const int32_t* gids;
+  const float4* records;
+  int64_t num_records;
+  const float* background;
+  const float* final_Ts;
+  const int32_t* final_idx;
+  const float* v_out_img;
+  const float* v_out_depth;  // nullptr for the plain blend
+  float* v_colors;
+  float* v_opacity;
+  float* v_xy;
+  float* v_conic;
+  float* v_depths;
+  unsigned long long* work;  // optional: [0] evaluations, [1] contributions
+};
+void launch_raster_bwd(const RasterBwdArgs& a, cudaStream_t stream);
+
+}  // namespace splax

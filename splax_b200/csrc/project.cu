@@ -1,0 +1,468 @@
+// Projection forward (tile count + fused global scan) and projection backward.
+//
+// Forward: one thread per (camera, gaussian) pair of the flat B*N launch, the work of
+// _project_kernel (splax/_project/_kernels.py:122-248) followed by the global inclusive scan
+// (:104-107) done in the same kernel with a decoupled look-back, so num_tiles_hit is never
+// re-read. Compiled with --fmad=false: every float op rounds as written, which makes the
+// integer outputs (radii, tile counts, cum) bit-identical to the C oracle.
+//
+// Backward: _project_bwd_kernel (:356-484) with its vjp helpers (:487-664); the per-image
+// viewmat cotangent is reduced per block with a warp reduce-scatter before one atomic per
+// entry per block.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace splax {
+namespace {
+
+__device__ __forceinline__ void mat_mul(const float* A, const float* B, float* C) {
+#pragma unroll
+  for (int i = 0; i < 3; ++i)
+#pragma unroll
+    for (int j = 0; j < 3; ++j)
+      C[3 * i + j] = (A[3 * i] * B[j] + A[3 * i + 1] * B[3 + j]) + A[3 * i + 2] * B[6 + j];
+}
+__device__ __forceinline__ void mat_T(const float* A, float* C) {
+#pragma unroll
+  for (int i = 0; i < 3; ++i)
+#pragma unroll
+    for (int j = 0; j < 3; ++j) C[3 * i + j] = A[3 * j + i];
+}
+__device__ __forceinline__ void mat_vec(const float* A, const float* v, float* o) {
+#pragma unroll
+  for (int i = 0; i < 3; ++i) o[i] = (A[3 * i] * v[0] + A[3 * i + 1] * v[1]) + A[3 * i + 2] * v[2];
+}
+// rows r..r+2 of a (rows, 4) row-major matrix (_load_affine, :609-624)
+__device__ __forceinline__ void load_affine(const float* m, float* R, float* t) {
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    R[3 * i] = m[4 * i];
+    R[3 * i + 1] = m[4 * i + 1];
+    R[3 * i + 2] = m[4 * i + 2];
+    t[i] = m[4 * i + 3];
+  }
+}
+// rotation of a unit xyzw quaternion; its derivative is _quat_vjp (:570-599)
+__device__ __forceinline__ void quat_to_mat(float x, float y, float z, float w, float* R) {
+  R[0] = 1.0f - 2.0f * (y * y + z * z);
+  R[1] = 2.0f * (x * y - w * z);
+  R[2] = 2.0f * (x * z + w * y);
+  R[3] = 2.0f * (x * y + w * z);
+  R[4] = 1.0f - 2.0f * (x * x + z * z);
+  R[5] = 2.0f * (y * z - w * x);
+  R[6] = 2.0f * (x * z - w * y);
+  R[7] = 2.0f * (y * z + w * x);
+  R[8] = 1.0f - 2.0f * (x * x + y * y);
+}
+
+struct Geom {
+  float W[9], p[3], M[9], R_tf[9], mean[3];
+  bool moved;
+};
+
+// _apply_transform + _project_geom (:627-664)
+__device__ __forceinline__ void project_geom(const ProjectArgs& a, int64_t idx, int64_t bid,
+                                             int64_t gid, Geom& g, float* q, float* sc) {
+  int64_t m_idx = a.sel_means ? idx : gid;
+  int64_t s_idx = a.sel_scales ? idx : gid;
+  int64_t q_idx = a.sel_quats ? idx : gid;
+  int64_t vb = (a.sel_view ? bid : 0) * 4;
+  g.mean[0] = a.means[3 * m_idx];
+  g.mean[1] = a.means[3 * m_idx + 1];
+  g.mean[2] = a.means[3 * m_idx + 2];
+  q[0] = a.quats[4 * q_idx];
+  q[1] = a.quats[4 * q_idx + 1];
+  q[2] = a.quats[4 * q_idx + 2];
+  q[3] = a.quats[4 * q_idx + 3];
+  sc[0] = a.scales[3 * s_idx];
+  sc[1] = a.scales[3 * s_idx + 1];
+  sc[2] = a.scales[3 * s_idx + 2];
+#pragma unroll
+  for (int i = 0; i < 9; ++i) g.R_tf[i] = (i % 4 == 0) ? 1.0f : 0.0f;
+  g.moved = false;
+  int32_t tf_id = a.has_transforms ? a.transform_ids[gid] : -1;
+  if (tf_id >= a.num_transforms) tf_id = -1;  // out-of-range ids are treated as static
+  if (tf_id >= 0) {
+    int64_t tf_idx = a.sel_transforms ? bid * a.num_transforms + tf_id : tf_id;
+    float t[3], o[3];
+    load_affine(a.transforms + tf_idx * 16, g.R_tf, t);
+    mat_vec(g.R_tf, g.mean, o);
+#pragma unroll
+    for (int i = 0; i < 3; ++i) g.mean[i] = o[i] + t[i];
+    g.moved = true;
+  }
+  float trans[3], Wm[3];
+  load_affine(a.viewmat + vb * 4, g.W, trans);
+  mat_vec(g.W, g.mean, Wm);
+#pragma unroll
+  for (int i = 0; i < 3; ++i) g.p[i] = Wm[i] + trans[i];
+  float R[9];
+  quat_to_mat(q[0], q[1], q[2], q[3], R);
+  float s[3] = {a.glob_scale * sc[0], a.glob_scale * sc[1], a.glob_scale * sc[2]};
+#pragma unroll
+  for (int i = 0; i < 3; ++i)
+#pragma unroll
+    for (int j = 0; j < 3; ++j) g.M[3 * i + j] = R[3 * i + j] * s[j];
+  if (g.moved) {
+    float Mt[9];
+    mat_mul(g.R_tf, g.M, Mt);
+#pragma unroll
+    for (int i = 0; i < 9; ++i) g.M[i] = Mt[i];
+  }
+}
+
+constexpr unsigned long long kFlagAgg = 1ull << 62;
+constexpr unsigned long long kFlagInc = 2ull << 62;
+constexpr unsigned long long kValMask = (1ull << 62) - 1;
+
+// Projection of one pair; returns its tile count (0 when culled), writing every output row.
+__device__ __forceinline__ int32_t project_one(const ProjectArgs& a, int64_t idx) {
+  int64_t bid = idx / a.n, gid = idx % a.n;
+  a.xys[2 * idx] = 0.0f;
+  a.xys[2 * idx + 1] = 0.0f;
+  a.depths[idx] = 0.0f;
+  a.radii[idx] = 0;
+  a.conics[3 * idx] = 0.0f;
+  a.conics[3 * idx + 1] = 0.0f;
+  a.conics[3 * idx + 2] = 0.0f;
+  a.num_tiles_hit[idx] = 0;
+  Geom g;
+  float q[4], sc[3];
+  project_geom(a, idx, bid, gid, g, q, sc);
+  if (g.p[2] <= a.clip_thresh) return 0;
+  float Mt[9], V3[9];
+  mat_T(g.M, Mt);
+  mat_mul(g.M, Mt, V3);
+  // EWA projection of the covariance (:188-212)
+  float tan_fovx = 0.5f * static_cast<float>(a.img_w) / a.fx;
+  float tan_fovy = 0.5f * static_cast<float>(a.img_h) / a.fy;
+  float lim_x = 1.3f * tan_fovx, lim_y = 1.3f * tan_fovy;
+  float tx = g.p[0], ty = g.p[1], tz = g.p[2];
+  tx = tz * fmin_w(lim_x, fmax_w(-lim_x, tx / tz));
+  ty = tz * fmin_w(lim_y, fmax_w(-lim_y, ty / tz));
+  float rz = 1.0f / tz;
+  float rz2 = rz * rz;
+  float J[9] = {a.fx * rz, 0.0f, (-a.fx * tx) * rz2, 0.0f, a.fy * rz, (-a.fy * ty) * rz2,
+                0.0f, 0.0f, 0.0f};
+  float T[9], TV[9];
+  mat_mul(J, g.W, T);
+  mat_mul(T, V3, TV);
+  float c00 = (TV[0] * T[0] + TV[1] * T[1]) + TV[2] * T[2];
+  float c01 = (TV[0] * T[3] + TV[1] * T[4]) + TV[2] * T[5];
+  float c11 = (TV[3] * T[3] + TV[4] * T[4]) + TV[5] * T[5];
+  float cxx = c00 + 0.3f, cxy = c01, cyy = c11 + 0.3f;
+  float det = cxx * cyy - cxy * cxy;
+  if (det == 0.0f) return 0;
+  float inv_det = 1.0f / det;
+  float ca = cyy * inv_det, cb = -cxy * inv_det, cc = cxx * inv_det;
+  float rw = 1.0f / (g.p[2] + 1e-6f);
+  float center_x = (g.p[0] * rw) * a.fx + a.cx;
+  float center_y = (g.p[1] * rw) * a.fy + a.cy;
+  int32_t tbx = (a.img_w + kBlockWidth - 1) / kBlockWidth;
+  int32_t tby = (a.img_h + kBlockWidth - 1) / kBlockWidth;
+  float opac = a.opacities[a.sel_opac ? idx : gid];
+  if (opac < kAlphaThreshold) return 0;
+  float t = iso_level(opac);
+  float ext = sqrtf(t);
+  float radius_x = ceilf(ext * sqrtf(cxx));
+  float radius_y = ceilf(ext * sqrtf(cyy));
+  if (radius_x <= 0.0f && radius_y <= 0.0f) return 0;
+  if (center_x + radius_x <= 0.0f || center_x - radius_x >= static_cast<float>(a.img_w) ||
+      center_y + radius_y <= 0.0f || center_y - radius_y >= static_cast<float>(a.img_h))
+    return 0;
+  Ellipse e;
+  ellipse_init(ca, cb, cc, t, center_x, center_y, tbx, tby, e);
+  int32_t count = ellipse_tile_count(e);
+  if (count <= 0) return 0;
+  a.num_tiles_hit[idx] = count;
+  a.depths[idx] = g.p[2];
+  a.radii[idx] = f2i(fmax_w(radius_x, radius_y));
+  a.xys[2 * idx] = center_x;
+  a.xys[2 * idx + 1] = center_y;
+  a.conics[3 * idx] = ca;
+  a.conics[3 * idx + 1] = cb;
+  a.conics[3 * idx + 2] = cc;
+  return count;
+}
+
+constexpr int kProjThreads = 256;
+
+__global__ void __launch_bounds__(kProjThreads)
+project_fwd_kernel(ProjectArgs a, unsigned long long* status, int* ticket, unsigned* err) {
+  __shared__ int s_tile;
+  __shared__ long long s_warp[kProjThreads / 32];
+  __shared__ long long s_prefix;
+  if (threadIdx.x == 0) s_tile = atomicAdd(ticket, 1);
+  __syncthreads();
+  const int tile = s_tile;
+  const int64_t idx = static_cast<int64_t>(tile) * kProjThreads + threadIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  long long count = idx < a.total ? project_one(a, idx) : 0;
+  // block inclusive scan
+  long long v = count;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    long long o = __shfl_up_sync(0xffffffffu, v, off);
+    if (lane >= off) v += o;
+  }
+  if (lane == 31) s_warp[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    long long w = lane < kProjThreads / 32 ? s_warp[lane] : 0;
+#pragma unroll
+    for (int off = 1; off < kProjThreads / 32; off <<= 1) {
+      long long o = __shfl_up_sync(0xffffffffu, w, off);
+      if (lane >= off) w += o;
+    }
+    if (lane < kProjThreads / 32) s_warp[lane] = w;  // inclusive warp totals
+  }
+  __syncthreads();
+  if (warp > 0) v += s_warp[warp - 1];
+  // decoupled look-back on the block aggregate (thread 0), bounded spin
+  if (threadIdx.x == 0) {
+    unsigned long long agg = static_cast<unsigned long long>(s_warp[kProjThreads / 32 - 1]);
+    long long prefix = 0;
+    if (tile == 0) {
+      st_release(&status[0], kFlagInc | agg);
+    } else {
+      st_release(&status[tile], kFlagAgg | agg);
+      int j = tile - 1;
+      long long spins = 0;
+      while (j >= 0) {
+        unsigned long long s = ld_acquire(&status[j]);
+        unsigned long long flag = s & ~kValMask;
+        if (flag == 0) {
+          if (++spins > kSpinLimit) {
+            atomicOr(err, kErrLookbackTimeout);
+            break;
+          }
+          continue;
+        }
+        prefix += static_cast<long long>(s & kValMask);
+        if (flag == kFlagInc) break;
+        --j;
+      }
+      st_release(&status[tile], kFlagInc | (static_cast<unsigned long long>(prefix) + agg));
+    }
+    s_prefix = prefix;
+    if (static_cast<int64_t>(tile + 1) * kProjThreads >= a.total &&
+        prefix + static_cast<long long>(agg) > 0x7fffffffll)
+      atomicOr(err, kErrCountOverflow);
+  }
+  __syncthreads();
+  if (idx < a.total) a.cum_tiles_hit[idx] = static_cast<int32_t>(static_cast<uint32_t>(s_prefix + v));
+}
+
+// ------------------------------------------------------------------ backward
+
+constexpr int kBwdThreads = 256;
+
+__global__ void __launch_bounds__(kBwdThreads) project_bwd_kernel(ProjectBwdArgs a) {
+  const int64_t blocks_per_image = (a.n + kBwdThreads - 1) / kBwdThreads;
+  const int64_t image_id = blockIdx.x / blocks_per_image;
+  const int64_t gid = (blockIdx.x % blocks_per_image) * kBwdThreads + threadIdx.x;
+  const int64_t idx = image_id * a.n + gid;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // 12 viewmat entries, then 12 transform entries
+  float vv[12];
+#pragma unroll
+  for (int k = 0; k < 12; ++k) vv[k] = 0.0f;
+  float vtf[12];
+#pragma unroll
+  for (int k = 0; k < 12; ++k) vtf[k] = 0.0f;
+  int32_t tf_id = -1;
+  bool live = false;
+  if (gid < a.n) {
+    tf_id = a.has_transforms ? a.transform_ids[gid] : -1;
+    if (tf_id >= a.num_transforms) tf_id = -1;
+    live = a.radii[a.sel_radii ? idx : gid] > 0;
+  }
+  bool moved = false;
+  if (live) {
+    ProjectArgs pa;
+    pa.means = a.means; pa.scales = a.scales; pa.quats = a.quats; pa.viewmat = a.viewmat;
+    pa.transforms = a.transforms; pa.transform_ids = a.transform_ids;
+    pa.n = a.n; pa.num_transforms = a.num_transforms; pa.has_transforms = a.has_transforms;
+    pa.sel_means = a.sel_means; pa.sel_scales = a.sel_scales; pa.sel_quats = a.sel_quats;
+    pa.sel_view = a.sel_view; pa.sel_transforms = a.sel_transforms;
+    pa.glob_scale = a.glob_scale;
+    Geom g;
+    float q[4], sc[3];
+    project_geom(pa, idx, image_id, gid, g, q, sc);
+    const float fx = a.fx, fy = a.fy, gs = a.glob_scale;
+    moved = g.moved;
+    float Mt[9], V[9], R[9];
+    mat_T(g.M, Mt);
+    mat_mul(g.M, Mt, V);
+    quat_to_mat(q[0], q[1], q[2], q[3], R);
+    float s[3] = {gs * sc[0], gs * sc[1], gs * sc[2]};
+    const float* p = g.p;
+    float rz = 1.0f / p[2];
+    float rz2 = rz * rz;
+    float J[9] = {fx * rz, 0.0f, (-fx * p[0]) * rz2, 0.0f, fy * rz, (-fy * p[1]) * rz2,
+                  0.0f, 0.0f, 0.0f};
+    float T[9];
+    mat_mul(J, g.W, T);
+    const int64_t c_idx = a.sel_conics ? idx : gid;
+    const int64_t vc_idx = a.sel_vconic ? idx : gid;
+    const int64_t vx_idx = a.sel_vxy ? idx : gid;
+    const int64_t vd_idx = a.sel_vdepth ? idx : gid;
+    const float* conic = a.conics + 3 * c_idx;
+    const float* vcon = a.v_conic + 3 * vc_idx;
+    float X0 = conic[0], X1 = conic[1], X3 = conic[2];
+    float G0 = vcon[0], G1 = 0.5f * vcon[1], G3 = vcon[2];
+    float XG0 = X0 * G0 + X1 * G1, XG1 = X0 * G1 + X1 * G3;
+    float XG2 = X1 * G0 + X3 * G1, XG3 = X1 * G1 + X3 * G3;
+    float S0 = XG0 * X0 + XG1 * X1, S1 = XG0 * X1 + XG1 * X3;
+    float S2 = XG2 * X0 + XG3 * X1, S3 = XG2 * X1 + XG3 * X3;
+    float vc0 = -S0, vc1 = -(S1 + S2), vc2 = -S3;
+    // _proj_vjp (:487-533)
+    const float vx0 = a.v_xy[2 * vx_idx], vx1 = a.v_xy[2 * vx_idx + 1];
+    const float vdep = a.v_depth[vd_idx];
+    float tx = p[0], ty = p[1], tz = p[2];
+    float rz3 = rz2 * rz;
+    float rw = 1.0f / (tz + 1e-6f);
+    float vpx = fx * vx0, vpy = fy * vx1;
+    float vvx = vpx * rw, vvy = vpy * rw;
+    float vvz = (-(vpx * tx + vpy * ty) * rw) * rw + vdep;
+    float vcov[9] = {vc0, 0.5f * vc1, 0.0f, 0.5f * vc1, vc2, 0.0f, 0.0f, 0.0f, 0.0f};
+    float Tt[9], tmp[9], v_V[9], v_T[9], Wt[9], v_J[9], vc2m[9];
+    mat_T(T, Tt);
+    mat_mul(Tt, vcov, tmp);
+    mat_mul(tmp, T, v_V);
+#pragma unroll
+    for (int k = 0; k < 9; ++k) vc2m[k] = 2.0f * vcov[k];
+    mat_mul(vc2m, T, tmp);
+    mat_mul(tmp, V, v_T);
+    mat_T(g.W, Wt);
+    mat_mul(v_T, Wt, v_J);
+    float v_t_x = (-fx * rz2) * v_J[2];
+    float v_t_y = (-fy * rz2) * v_J[5];
+    float v_t_z = (((-fx * rz2) * v_J[0] + (((2.0f * fx) * tx) * rz3) * v_J[2]) - (fy * rz2) * v_J[4]) +
+                  (((2.0f * fy) * ty) * rz3) * v_J[5];
+    float v_p[3] = {vvx + v_t_x, vvy + v_t_y, vvz + v_t_z};
+    float v_mean_world[3], v_Vs[9], v_M_world[9];
+    mat_vec(Wt, v_p, v_mean_world);
+#pragma unroll
+    for (int k = 0; k < 9; ++k) v_Vs[k] = v_V[k] + v_V[3 * (k % 3) + k / 3];
+    mat_mul(v_Vs, g.M, v_M_world);
+    // _transform_vjp (:536-557)
+    float v_mean_out[3], v_M[9];
+    if (moved) {
+      float Rtt[9], M_local[9], Mlt[9], vMM[9];
+      mat_T(g.R_tf, Rtt);
+      mat_vec(Rtt, v_mean_world, v_mean_out);
+      mat_mul(Rtt, v_M_world, v_M);
+      mat_mul(Rtt, g.M, M_local);
+      mat_T(M_local, Mlt);
+      mat_mul(v_M_world, Mlt, vMM);
+      const int64_t m_idx = a.sel_means ? idx : gid;
+      const float ml[3] = {a.means[3 * m_idx], a.means[3 * m_idx + 1], a.means[3 * m_idx + 2]};
+#pragma unroll
+      for (int r = 0; r < 3; ++r) {
+#pragma unroll
+        for (int c = 0; c < 3; ++c) vtf[4 * r + c] = v_mean_world[r] * ml[c] + vMM[3 * r + c];
+        vtf[4 * r + 3] = v_mean_world[r];
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 3; ++k) v_mean_out[k] = v_mean_world[k];
+#pragma unroll
+      for (int k = 0; k < 9; ++k) v_M[k] = v_M_world[k];
+    }
+    a.v_mean3d[3 * idx] = v_mean_out[0];
+    a.v_mean3d[3 * idx + 1] = v_mean_out[1];
+    a.v_mean3d[3 * idx + 2] = v_mean_out[2];
+    // _scale_vjp (:560-567)
+#pragma unroll
+    for (int c = 0; c < 3; ++c)
+      a.v_scale[3 * idx + c] = ((R[c] * v_M[c] + R[3 + c] * v_M[3 + c]) + R[6 + c] * v_M[6 + c]) * gs;
+    // _quat_vjp (:570-599), written xyzw
+    float vR[9];
+#pragma unroll
+    for (int r = 0; r < 3; ++r)
+#pragma unroll
+      for (int c = 0; c < 3; ++c) vR[3 * r + c] = v_M[3 * r + c] * s[c];
+    const float x = q[0], y = q[1], z = q[2], w = q[3];
+    float vq_w = 2.0f * (x * (vR[7] - vR[5]) + y * (vR[2] - vR[6]) + z * (vR[3] - vR[1]));
+    float vq_x = 2.0f * (-2.0f * x * (vR[4] + vR[8]) + y * (vR[3] + vR[1]) + z * (vR[6] + vR[2]) +
+                         w * (vR[7] - vR[5]));
+    float vq_y = 2.0f * (x * (vR[3] + vR[1]) - 2.0f * y * (vR[0] + vR[8]) + z * (vR[7] + vR[5]) +
+                         w * (vR[2] - vR[6]));
+    float vq_z = 2.0f * (x * (vR[6] + vR[2]) + y * (vR[7] + vR[5]) - 2.0f * z * (vR[0] + vR[4]) +
+                         w * (vR[3] - vR[1]));
+    a.v_quat[4 * idx] = vq_x;
+    a.v_quat[4 * idx + 1] = vq_y;
+    a.v_quat[4 * idx + 2] = vq_z;
+    a.v_quat[4 * idx + 3] = vq_w;
+    // _view_vjp (:602-606)
+    float Jt[9], JtvT[9];
+    mat_T(J, Jt);
+    mat_mul(Jt, v_T, JtvT);
+#pragma unroll
+    for (int r = 0; r < 3; ++r) {
+#pragma unroll
+      for (int c = 0; c < 3; ++c) vv[4 * r + c] = v_p[r] * g.mean[c] + JtvT[3 * r + c];
+      vv[4 * r + 3] = v_p[r];
+    }
+  } else if (gid < a.n) {
+    a.v_mean3d[3 * idx] = 0.0f;
+    a.v_mean3d[3 * idx + 1] = 0.0f;
+    a.v_mean3d[3 * idx + 2] = 0.0f;
+    a.v_scale[3 * idx] = 0.0f;
+    a.v_scale[3 * idx + 1] = 0.0f;
+    a.v_scale[3 * idx + 2] = 0.0f;
+    a.v_quat[4 * idx] = 0.0f;
+    a.v_quat[4 * idx + 1] = 0.0f;
+    a.v_quat[4 * idx + 2] = 0.0f;
+    a.v_quat[4 * idx + 3] = 0.0f;
+  }
+  // per-image viewmat cotangent: warp reduce-scatter, then one atomic per entry per warp
+  // (rows image_id*4 + r of the (4B, 4) output; row 3 stays zero)
+  {
+    const int c = warp_reduce_scatter<12>(vv, lane);
+    if (c >= 0 && vv[0] != 0.0f) atomicAdd(&a.v_viewmat[16 * image_id + c], vv[0]);
+  }
+  // transform cotangent (:461-484): reduce when the block is uniformly on one transform,
+  // per-thread atomics otherwise
+  if (a.has_transforms) {
+    __shared__ int s_tmin, s_tmax;
+    if (threadIdx.x == 0) { s_tmin = 0x7fffffff; s_tmax = -0x7fffffff; }
+    __syncthreads();
+    atomicMin(&s_tmin, tf_id);
+    atomicMax(&s_tmax, tf_id);
+    __syncthreads();
+    const int tmin = s_tmin, tmax = s_tmax;
+    if (tmin == tmax && tmin >= 0) {
+      const int c = warp_reduce_scatter<12>(vtf, lane);
+      if (c >= 0 && vtf[0] != 0.0f)
+        atomicAdd(&a.v_transforms[16 * (image_id * a.num_transforms + tmin) + c], vtf[0]);
+    } else if (moved) {
+      float* out = a.v_transforms + 16 * (image_id * a.num_transforms + tf_id);
+#pragma unroll
+      for (int k = 0; k < 12; ++k) atomicAdd(&out[k], vtf[k]);
+    }
+  }
+  (void)warp;
+}
+
+}  // namespace
+
+void launch_project_fwd(const ProjectArgs& a, unsigned long long* status, int* ticket,
+                        unsigned* err, cudaStream_t stream) {
+  const int64_t blocks = (a.total + kProjThreads - 1) / kProjThreads;
+  if (blocks == 0) return;
+  project_fwd_kernel<<<static_cast<unsigned>(blocks), kProjThreads, 0, stream>>>(a, status, ticket,
+                                                                                 err);
+}
+
+int64_t project_scan_tiles(int64_t total) { return (total + kProjThreads - 1) / kProjThreads; }
+
+void launch_project_bwd(const ProjectBwdArgs& a, cudaStream_t stream) {
+  const int64_t blocks_per_image = (a.n + kBwdThreads - 1) / kBwdThreads;
+  const int64_t blocks = blocks_per_image * a.B;
+  if (blocks == 0) return;
+  project_bwd_kernel<<<static_cast<unsigned>(blocks), kBwdThreads, 0, stream>>>(a);
+}
+
+}  // namespace splax

@@ -1,0 +1,428 @@
+// Intersection keys, their radix sort and the per-tile bin edges: the device half of
+// sort_and_bin (splax/_rasterize/_sort/_sort.py:29-171).
+//
+//  depth min/max   per-image [dmin, dmax] of visible depths (_sort/_kernels.py:31-73), a
+//                  warp-reduced atomic min/max on order-preserving integers.
+//  emission        the ellipse tile walk once more per visible gaussian (_kernels.py:76-211),
+//                  writing keys and flat ids at the cum offsets, and packing the gaussian's
+//                  blend record (xy, conic, opacity, colour, depth) for the blend kernels.
+//  radix sort      stable LSD onesweep: one upfront histogram pass over all digits, then one
+//                  kernel per 8-bit digit that ranks keys with warp ballots, resolves the
+//                  tile's global digit offsets by a decoupled look-back (bounded spin) and
+//                  scatters through shared memory so the global writes coalesce per digit.
+//                  Only the significant key bits are sorted.
+//  bin edges       [start, end) per (image, tile) from the sorted keys (_kernels.py:214-269).
+//
+// Compiled with --fmad=false so the emitted walk and quantised depths match the projection's
+// count and the C oracle bit for bit.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace splax {
+namespace {
+
+// ------------------------------------------------------------------ depth min / max
+constexpr int kMmThreads = 256;
+constexpr int kMmItems = 16;
+
+__global__ void seed_minmax_kernel(int32_t* mm, int32_t B) {
+  int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < B) {
+    mm[2 * b] = float_to_ordered(1.0e30f);
+    mm[2 * b + 1] = float_to_ordered(-1.0e30f);
+  }
+}
+
+__global__ void __launch_bounds__(kMmThreads)
+depth_minmax_kernel(const float* __restrict__ depths, const int32_t* __restrict__ radii,
+                    int64_t total, int64_t n, int32_t* mm) {
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kMmThreads * kMmItems;
+  int64_t img_cur = -1;
+  int32_t lo = 0x7fffffff, hi = static_cast<int32_t>(0x80000000u);
+#pragma unroll 4
+  for (int k = 0; k < kMmItems; ++k) {
+    const int64_t idx = base + k * kMmThreads + threadIdx.x;
+    if (idx >= total) break;
+    if (radii[idx] <= 0) continue;
+    const int64_t im = idx / n;
+    const int32_t d = float_to_ordered(depths[idx]);
+    if (im != img_cur) {
+      if (img_cur >= 0) {
+        atomicMin(&mm[2 * img_cur], lo);
+        atomicMax(&mm[2 * img_cur + 1], hi);
+      }
+      img_cur = im;
+      lo = d;
+      hi = d;
+    } else {
+      lo = min(lo, d);
+      hi = max(hi, d);
+    }
+  }
+  // one atomic pair per warp when the warp sits inside one image, per lane otherwise
+  const int rep = __reduce_max_sync(0xffffffffu, static_cast<int>(img_cur));
+  const bool uniform = __all_sync(0xffffffffu, img_cur == rep || img_cur < 0);
+  if (uniform) {
+    const int32_t wlo = __reduce_min_sync(0xffffffffu, lo);
+    const int32_t whi = __reduce_max_sync(0xffffffffu, hi);
+    if ((threadIdx.x & 31) == 0 && rep >= 0) {
+      atomicMin(&mm[2 * rep], wlo);
+      atomicMax(&mm[2 * rep + 1], whi);
+    }
+  } else if (img_cur >= 0) {
+    atomicMin(&mm[2 * img_cur], lo);
+    atomicMax(&mm[2 * img_cur + 1], hi);
+  }
+}
+
+// ------------------------------------------------------------------ key emission
+template <bool K64>
+__global__ void __launch_bounds__(256) emit_kernel(EmitArgs a) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= a.total) return;
+  if (a.radii[idx] <= 0) return;
+  const int64_t bid = idx / a.n;
+  int64_t cur = idx > 0 ? static_cast<int64_t>(static_cast<uint32_t>(a.cum[idx - 1])) : 0;
+  int64_t end = static_cast<int64_t>(static_cast<uint32_t>(a.cum[idx]));
+  if (end > a.count || cur > end) {  // cum_tiles_hit does not describe this geometry
+    atomicOr(a.err, kErrEmitCount);
+    end = min(end, a.count);
+    cur = min(cur, end);
+  }
+  const float x = a.xys[2 * idx], y = a.xys[2 * idx + 1];
+  const float ca = a.conics[3 * idx], cb = a.conics[3 * idx + 1], cc = a.conics[3 * idx + 2];
+  const float depth = a.depths[idx];
+  if (a.records) {
+    const int64_t ci = idx % a.color_rows;
+    const float op = a.opacities[idx % a.opac_rows];
+    float4* rec = a.records + kRecordFloat4 * idx;
+    rec[0] = make_float4(x, y, ca, cb);
+    rec[1] = make_float4(cc, op, a.colors[3 * ci], a.colors[3 * ci + 1]);
+    rec[2] = make_float4(a.colors[3 * ci + 2], depth, 0.0f, 0.0f);
+  }
+  uint64_t enc;
+  uint32_t depth_q = 0;
+  if constexpr (K64) {
+    const int32_t dbits = __float_as_int(depth);
+    // the reference sign-extends a negative depth into the image and tile fields
+    if (dbits < 0) atomicOr(a.err, kErrNegativeDepthKey);
+    enc = (static_cast<uint64_t>(bid) << (32 + a.tile_n_bits)) | static_cast<uint32_t>(dbits);
+  } else {
+    const float dmin = ordered_to_float(a.depth_mm[2 * bid]);
+    const float drange = ordered_to_float(a.depth_mm[2 * bid + 1]) - dmin;
+    const int32_t qmax = static_cast<int32_t>((1u << a.depth_bits) - 1u);
+    const float maxq = static_cast<float>(qmax);
+    if (drange > 0.0f) {
+      const float f = (depth - dmin) / drange;
+      depth_q = static_cast<uint32_t>(imin(imax(f2i(f * maxq), 0), qmax));
+    }
+    enc = static_cast<uint64_t>(bid) << (a.depth_bits + a.tile_n_bits);
+  }
+  const float t = iso_level(a.map_opacities[idx % a.map_opac_rows]);
+  Ellipse e;
+  ellipse_init(ca, cb, cc, t, x, y, a.tbx, a.tby, e);
+  bool bad = false;
+  if (e.valid) {
+    float i0, i1;
+    ellipse_init_span(e, i0, i1);
+    for (int32_t u = e.rmin0; u < e.rmax0 && !bad; ++u) {
+      int32_t mn, mx;
+      ellipse_column(u, e, i0, i1, mn, mx);
+      for (int32_t v = mn; v < mx; ++v) {
+        if (cur >= end) {
+          bad = true;
+          break;
+        }
+        const uint64_t tile =
+            static_cast<uint64_t>(e.isY ? u * a.tbx + v : v * a.tbx + u);
+        if constexpr (K64) {
+          reinterpret_cast<uint64_t*>(a.keys)[cur] = enc | (tile << 32);
+        } else {
+          reinterpret_cast<uint32_t*>(a.keys)[cur] =
+              static_cast<uint32_t>(enc | (tile << a.depth_bits) | depth_q);
+        }
+        a.vals[cur] = static_cast<int32_t>(idx);
+        ++cur;
+      }
+    }
+  }
+  if (bad || cur != end) atomicOr(a.err, kErrEmitCount);
+}
+
+// ------------------------------------------------------------------ onesweep radix sort
+constexpr int kSortThreads = 256;
+constexpr int kSortWarps = kSortThreads / 32;
+constexpr int kItems32 = 16;  // 4096 keys per tile for 32-bit keys
+constexpr int kItems64 = 12;  // 3072 keys per tile for 64-bit keys
+constexpr int kHistItems = 32;
+constexpr unsigned long long kFlagAgg = 1ull << 62;
+constexpr unsigned long long kFlagInc = 2ull << 62;
+constexpr unsigned long long kValMask = (1ull << 62) - 1;
+
+template <typename K>
+__global__ void __launch_bounds__(kSortThreads)
+radix_hist_kernel(const K* __restrict__ keys, int64_t count, int passes, uint32_t* hist) {
+  __shared__ uint32_t s[8][256];
+  for (int i = threadIdx.x; i < 8 * 256; i += kSortThreads) (&s[0][0])[i] = 0;
+  __syncthreads();
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kSortThreads * kHistItems;
+#pragma unroll 4
+  for (int k = 0; k < kHistItems; ++k) {
+    const int64_t i = base + k * kSortThreads + threadIdx.x;
+    if (i >= count) break;
+    const uint64_t key = static_cast<uint64_t>(keys[i]);
+    for (int p = 0; p < passes; ++p) atomicAdd(&s[p][(key >> (8 * p)) & 255u], 1u);
+  }
+  __syncthreads();
+  for (int p = 0; p < passes; ++p) {
+    const uint32_t c = s[p][threadIdx.x];
+    if (c) atomicAdd(&hist[p * 256 + threadIdx.x], c);
+  }
+}
+
+__device__ __forceinline__ uint32_t block_exclusive_scan_256(uint32_t v, uint32_t* s_warp) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t inc = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    uint32_t o = __shfl_up_sync(0xffffffffu, inc, off);
+    if (lane >= off) inc += o;
+  }
+  if (lane == 31) s_warp[warp] = inc;
+  __syncthreads();
+  uint32_t wpre = 0;
+  for (int w = 0; w < warp; ++w) wpre += s_warp[w];
+  return wpre + inc - v;
+}
+
+// exclusive scan of each pass's 256-digit histogram: offsets[p][d]
+__global__ void radix_scan_kernel(const uint32_t* hist, uint32_t* offsets) {
+  __shared__ uint32_t s_warp[kSortWarps];
+  const int p = blockIdx.x;
+  const uint32_t v = hist[p * 256 + threadIdx.x];
+  offsets[p * 256 + threadIdx.x] = block_exclusive_scan_256(v, s_warp);
+}
+
+template <typename K, int ITEMS>
+__global__ void __launch_bounds__(kSortThreads)
+onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* __restrict__ kout,
+                int32_t* __restrict__ vout, int64_t count, int shift,
+                const uint32_t* __restrict__ goff, unsigned long long* status, int* tile_counter,
+                unsigned* err) {
+  constexpr int TILE = kSortThreads * ITEMS;
+  __shared__ uint32_t s_wh[kSortWarps][256];
+  __shared__ uint32_t s_bx[256];
+  __shared__ long long s_gb[256];
+  __shared__ uint32_t s_warp[kSortWarps];
+  __shared__ int s_tile;
+  extern __shared__ __align__(16) unsigned char s_raw[];
+  K* s_keys = reinterpret_cast<K*>(s_raw);
+  int32_t* s_vals = reinterpret_cast<int32_t*>(s_raw + TILE * sizeof(K));
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i < kSortWarps * 256; i += kSortThreads) (&s_wh[0][0])[i] = 0;
+  if (tid == 0) s_tile = atomicAdd(tile_counter, 1);
+  __syncthreads();
+  const int64_t tile = s_tile;
+  const int64_t base = tile * TILE;
+  const int64_t rem = count - base;
+  const int nvalid = rem < TILE ? static_cast<int>(rem) : TILE;
+  const int warp_base = warp * 32 * ITEMS;
+  const unsigned lt_mask = (1u << lane) - 1u;
+
+  K k[ITEMS];
+  int32_t val[ITEMS];
+  uint32_t rank[ITEMS];
+#pragma unroll
+  for (int it = 0; it < ITEMS; ++it) {
+    const int pos = warp_base + it * 32 + lane;
+    const bool valid = pos < nvalid;
+    k[it] = valid ? kin[base + pos] : K(0);
+    val[it] = valid ? vin[base + pos] : 0;
+  }
+#pragma unroll
+  for (int it = 0; it < ITEMS; ++it) {
+    const int pos = warp_base + it * 32 + lane;
+    const bool valid = pos < nvalid;
+    const uint32_t d = static_cast<uint32_t>(static_cast<uint64_t>(k[it]) >> shift) & 255u;
+    unsigned peers = __ballot_sync(0xffffffffu, valid);
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      const bool bit = (d >> b) & 1u;
+      const unsigned bal = __ballot_sync(0xffffffffu, bit);
+      peers &= bit ? bal : ~bal;
+    }
+    const uint32_t lt = __popc(peers & lt_mask);
+    const uint32_t prev = valid ? s_wh[warp][d] : 0u;
+    __syncwarp();
+    if (valid && lt == 0) s_wh[warp][d] = prev + __popc(peers);
+    __syncwarp();
+    rank[it] = prev + lt;
+  }
+  __syncthreads();
+  // per digit (one thread each): warp exclusive offsets and the block's count
+  const int dg = tid;
+  uint32_t sum = 0;
+#pragma unroll
+  for (int w = 0; w < kSortWarps; ++w) {
+    const uint32_t c = s_wh[w][dg];
+    s_wh[w][dg] = sum;
+    sum += c;
+  }
+  // decoupled look-back over preceding tiles for this digit
+  long long prefix = 0;
+  unsigned long long* st = status + tile * 256 + dg;
+  if (tile == 0) {
+    st_release(st, kFlagInc | sum);
+  } else {
+    st_release(st, kFlagAgg | sum);
+    int64_t j = tile - 1;
+    long long spins = 0;
+    while (j >= 0) {
+      const unsigned long long s = ld_acquire(status + j * 256 + dg);
+      const unsigned long long flag = s & ~kValMask;
+      if (flag == 0) {
+        if (++spins > kSpinLimit) {
+          atomicOr(err, kErrLookbackTimeout);
+          break;
+        }
+        continue;
+      }
+      prefix += static_cast<long long>(s & kValMask);
+      if (flag == kFlagInc) break;
+      --j;
+    }
+    st_release(st, kFlagInc | (static_cast<unsigned long long>(prefix) + sum));
+  }
+  const uint32_t excl = block_exclusive_scan_256(sum, s_warp);
+  s_bx[dg] = excl;
+  s_gb[dg] = static_cast<long long>(goff[dg]) + prefix - static_cast<long long>(excl);
+  __syncthreads();
+#pragma unroll
+  for (int it = 0; it < ITEMS; ++it) {
+    const int pos = warp_base + it * 32 + lane;
+    if (pos < nvalid) {
+      const uint32_t d = static_cast<uint32_t>(static_cast<uint64_t>(k[it]) >> shift) & 255u;
+      const uint32_t lpos = s_bx[d] + s_wh[warp][d] + rank[it];
+      s_keys[lpos] = k[it];
+      s_vals[lpos] = val[it];
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < ITEMS; ++j) {
+    const int p = j * kSortThreads + tid;
+    if (p < nvalid) {
+      const K kk = s_keys[p];
+      const uint32_t d = static_cast<uint32_t>(static_cast<uint64_t>(kk) >> shift) & 255u;
+      const long long dst = s_gb[d] + p;
+      if (dst >= 0 && dst < count) {
+        kout[dst] = kk;
+        vout[dst] = s_vals[p];
+      } else {
+        atomicOr(err, kErrLookbackTimeout);
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ bin edges
+template <typename K>
+__global__ void tile_bins_kernel(const K* __restrict__ keys, int64_t count, int shift,
+                                 int32_t tile_n_bits, int32_t num_tiles, int64_t num_bins,
+                                 int2* bins, unsigned* err) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= count) return;
+  const uint64_t mask = (1ull << tile_n_bits) - 1ull;
+  const uint64_t key = static_cast<uint64_t>(keys[idx]) >> shift;
+  const int64_t cur = static_cast<int64_t>((key >> tile_n_bits) * num_tiles + (key & mask));
+  if (cur >= num_bins) {
+    atomicOr(err, kErrBinRange);
+    return;
+  }
+  // as in the reference, index 0 returns before the last-index test
+  if (idx == 0) {
+    bins[cur].x = 0;
+    return;
+  }
+  if (idx == count - 1) bins[cur].y = static_cast<int32_t>(count);
+  const uint64_t keyp = static_cast<uint64_t>(keys[idx - 1]) >> shift;
+  const int64_t prev = static_cast<int64_t>((keyp >> tile_n_bits) * num_tiles + (keyp & mask));
+  if (prev != cur && prev < num_bins) {
+    bins[prev].y = static_cast<int32_t>(idx);
+    bins[cur].x = static_cast<int32_t>(idx);
+  }
+}
+
+template <typename K, int ITEMS>
+int sort_impl(const SortScratch& s, int64_t count, int bits, cudaStream_t stream) {
+  const int passes = (bits + 7) / 8;
+  uint32_t* hist = s.hist;
+  uint32_t* offsets = s.hist + 8 * 256;
+  cudaMemsetAsync(hist, 0, sizeof(uint32_t) * 8 * 256, stream);
+  cudaMemsetAsync(s.tile_counters, 0, sizeof(int) * 8, stream);
+  const int64_t hblocks = (count + kSortThreads * kHistItems - 1) / (kSortThreads * kHistItems);
+  radix_hist_kernel<K><<<static_cast<unsigned>(hblocks), kSortThreads, 0, stream>>>(
+      reinterpret_cast<const K*>(s.keys[0]), count, passes, hist);
+  radix_scan_kernel<<<passes, 256, 0, stream>>>(hist, offsets);
+  constexpr int TILE = kSortThreads * ITEMS;
+  const int64_t tiles = (count + TILE - 1) / TILE;
+  const size_t smem = TILE * (sizeof(K) + sizeof(int32_t));
+  int cur = 0;
+  for (int p = 0; p < passes; ++p) {
+    cudaMemsetAsync(s.status, 0, sizeof(unsigned long long) * tiles * 256, stream);
+    onesweep_kernel<K, ITEMS><<<static_cast<unsigned>(tiles), kSortThreads, smem, stream>>>(
+        reinterpret_cast<const K*>(s.keys[cur]), s.vals[cur], reinterpret_cast<K*>(s.keys[cur ^ 1]),
+        s.vals[cur ^ 1], count, 8 * p, offsets + p * 256, s.status, s.tile_counters + p, s.err);
+    cur ^= 1;
+  }
+  return cur;
+}
+
+}  // namespace
+
+void launch_depth_minmax(const float* depths, const int32_t* radii, int64_t total, int64_t n,
+                         int32_t B, int32_t* depth_mm, cudaStream_t stream) {
+  seed_minmax_kernel<<<(B + 127) / 128, 128, 0, stream>>>(depth_mm, B);
+  const int64_t blocks = (total + kMmThreads * kMmItems - 1) / (kMmThreads * kMmItems);
+  if (blocks > 0)
+    depth_minmax_kernel<<<static_cast<unsigned>(blocks), kMmThreads, 0, stream>>>(depths, radii,
+                                                                                  total, n,
+                                                                                  depth_mm);
+}
+
+void launch_emit(const EmitArgs& a, bool key64, cudaStream_t stream) {
+  const int64_t blocks = (a.total + 255) / 256;
+  if (blocks == 0) return;
+  if (key64)
+    emit_kernel<true><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
+  else
+    emit_kernel<false><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
+}
+
+int sort_tile_items(bool key64) { return kSortThreads * (key64 ? kItems64 : kItems32); }
+
+int radix_sort_pairs(const SortScratch& s, bool key64, int64_t count, int bits,
+                     cudaStream_t stream) {
+  if (count <= 1) return 0;
+  return key64 ? sort_impl<uint64_t, kItems64>(s, count, bits, stream)
+               : sort_impl<uint32_t, kItems32>(s, count, bits, stream);
+}
+
+void launch_tile_bins(const void* keys, bool key64, int64_t count, int shift, int32_t tile_n_bits,
+                      int32_t num_tiles, int64_t num_bins, int32_t* tile_bins, unsigned* err,
+                      cudaStream_t stream) {
+  const int64_t blocks = (count + 255) / 256;
+  if (blocks == 0) return;
+  int2* bins = reinterpret_cast<int2*>(tile_bins);
+  if (key64)
+    tile_bins_kernel<uint64_t><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+        reinterpret_cast<const uint64_t*>(keys), count, shift, tile_n_bits, num_tiles, num_bins,
+        bins, err);
+  else
+    tile_bins_kernel<uint32_t><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+        reinterpret_cast<const uint32_t*>(keys), count, shift, tile_n_bits, num_tiles, num_bins,
+        bins, err);
+}
+
+}  // namespace splax
