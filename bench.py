@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Benchmark of the splax_b200 hot path on BASELINE.json's headline workload.
+"""Benchmark of the splax_b200 hot path on its headline workload.
 
 Metric: fwd+bwd frames/s of config 2 (N=1,000,000 gaussians, 8 ring cameras, 1080x1920,
 MSE against seeded targets, gradients of all five gaussian parameter arrays). One step renders
@@ -33,9 +33,10 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "fwd+bwd frames/s (1M gaussians, 1080p, 8 cams) at 1/2/4/8 B200; % roofline"
 CONFIG = 2
+WORKLOAD = "config 2: 1M gaussians, 8 ring cams, 1080x1920, MSE fwd+bwd, grads of 5 param arrays"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
-# algorithmic work per unit (SURVEY 8(d) counts restated): FLOPs per blend evaluation /
-# contribution, bytes per projected pair / intersection
+# algorithmic work per unit: FLOPs per blend evaluation / contribution (FMA = 2), restated from
+# the reference blend loop (splax/_rasterize/_kernels.py:185-197) and vjp (:1235-1253)
 FWD_FLOPS_PER_EVAL = 22
 BWD_FLOPS_PER_EVAL = 12
 BWD_FLOPS_PER_CONTRIB = 45
@@ -149,8 +150,8 @@ def reference_arm(args) -> None:
         "impl": "reference", "metric": METRIC, "value": value, "unit": "frames/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE config 2 shapes)",
-        "config": {"workload": "BASELINE config 2: 1M gaussians, 8 cams, 1080x1920, MSE fwd+bwd",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, config 2 distributions)",
+        "config": {"workload": WORKLOAD,
                    "implementation": "C oracle (CPU restatement; warp-lang/jax unavailable)"},
         "cpu_baseline": {"value": value, "unit": "frames/s", "cores": threads, "kind": "port",
                          "sample": sample},
@@ -358,9 +359,8 @@ def main() -> None:
             "metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded, BASELINE config 2 distributions)",
-            "config": {"workload": "BASELINE config 2: 1M gaussians, 8 ring cams, 1080x1920, "
-                                   "MSE fwd+bwd, grads of 5 param arrays",
+            "data": "synthetic (seeded, config 2 distributions)",
+            "config": {"workload": WORKLOAD,
                        "cams_per_gpu": per, "gaussians": n, "l2": "inputs larger than L2 "
                        "(targets 199 MB + params 56 MB + sort scratch per step)",
                        "parallelism": f"camera-sharded dp{world}"},

@@ -1,7 +1,7 @@
 """Camera helpers and the seeded synthetic scenes of the benchmark configurations.
 
 ``look_at`` follows splax/utils.py:9-30 (OpenCV world-to-camera, x right, y down). The scene
-builders generate the inputs BASELINE.json describes for each configuration, in a fixed order
+builders generate the seeded inputs of each benchmark configuration (0-4), in a fixed order
 with numpy's default_rng, so the CUDA path and the CPU baseline consume identical bytes.
 """
 
