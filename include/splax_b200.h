@@ -62,6 +62,24 @@ int splax_project(const float *means3d, int64_t means3d_rows, const float *scale
                   int64_t total, float *xys, float *depths, int32_t *radii, float *conics,
                   int32_t *num_tiles_hit, int32_t *cum_tiles_hit, void *stream);
 
+/* Projection forward that allocates nothing. No counterpart in the reference: same arguments
+ * and outputs as splax_project, for callers that cannot let a library call cudaMalloc (an XLA
+ * custom call under a preallocating JAX allocator, a stream being captured into a CUDA graph,
+ * a fixed device-memory budget). Its scan scratch is a 512 KiB file-scope __device__ array,
+ * so total = B*n is limited to 16,777,216 pairs (larger calls fail with
+ * SPLAX_ERR_INVALID_ARGUMENT). The first call on a device resolves the array's address; make
+ * it before any stream capture. Calls share the array: calls overlapping on the GPU race. */
+int splax_project_noalloc(const float *means3d, int64_t means3d_rows, const float *scales,
+                          int64_t scales_rows, const float *quats_xyzw, int64_t quats_rows,
+                          const float *viewmat, int64_t viewmat_rows, const float *opacities,
+                          int64_t opacities_rows, const float *gaussian_transforms,
+                          int64_t transforms_rows, const int32_t *transform_ids,
+                          int32_t num_gaussians, int32_t num_transforms, int32_t has_transforms,
+                          int32_t img_h, int32_t img_w, float fx, float fy, float cx, float cy,
+                          float glob_scale, float clip_thresh, int64_t total, float *xys,
+                          float *depths, int32_t *radii, float *conics, int32_t *num_tiles_hit,
+                          int32_t *cum_tiles_hit, void *stream);
+
 /* FFI target "project_bwd": _project_bwd_warp, splax/_project/_kernels.py:257-341 (:344-353).
  * B = out_rows / num_gaussians images; outputs v_mean3d (B*n,3), v_scale (B*n,3),
  * v_quat (B*n,4) xyzw, v_viewmat (4B,4), v_transforms (B*K,4,4), all overwritten. */

@@ -30,6 +30,7 @@ SOURCES = {
     "raster_fwd.cu": [],
     "raster_bwd.cu": [],
     "capi.cu": [],
+    "project_noalloc.cu": [],
 }
 
 

@@ -28,6 +28,8 @@ P, I64, I32, F32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_flo
 SIGNATURES: dict[str, list] = {
     "splax_project": [P, I64, P, I64, P, I64, P, I64, P, I64, P, I64, P, I32, I32, I32, I32, I32,
                       F32, F32, F32, F32, F32, F32, I64, P, P, P, P, P, P, P],
+    "splax_project_noalloc": [P, I64, P, I64, P, I64, P, I64, P, I64, P, I64, P, I32, I32, I32,
+                              I32, I32, F32, F32, F32, F32, F32, F32, I64, P, P, P, P, P, P, P],
     "splax_project_bwd": [P, I64, P, I64, P, I64, P, I64, P, I64, P, I64, P, I64, P, I64, P, I64,
                           P, I64, P, I32, I32, I32, F32, F32, F32, I64, P, P, P, P, P, P],
     "splax_rasterize": [P, I64, P, I64, P, I64, P, I64, P, P, P, P, P, I64, I32, I32, I32, I64,

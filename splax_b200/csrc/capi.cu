@@ -588,6 +588,9 @@ int rasterize_bwd_common(const float* colors, int64_t colors_rows, const float* 
 }
 
 }  // namespace
+
+int record_error(int code, const char* msg) { return fail(code, msg); }
+
 }  // namespace splax
 
 using namespace splax;

@@ -147,4 +147,7 @@ struct RasterBwdArgs {
 };
 void launch_raster_bwd(const RasterBwdArgs& a, cudaStream_t stream);
 
+// capi.cu: set the calling thread's splax_last_error() message and return `code`
+int record_error(int code, const char* msg);
+
 }  // namespace splax
