@@ -152,6 +152,17 @@ int splax_rasterize_bwd_depth(const float *colors, int64_t colors_rows, const fl
                               float *v_opacity, float *v_xy, float *v_conic, float *v_depths,
                               void *stream);
 
+/* Reuse of the forward's sort by its backward (the reference re-sorts in every backward,
+ * splax/_rasterize/_kernels.py:422-424; the sort is deterministic, so reusing it gives identical
+ * results). splax_last_sort_token() returns the token of the sort done by the calling thread's
+ * last splax_rasterize / splax_rasterize_depth call (-1 if none). splax_reuse_sort(token) arms
+ * it for the calling thread's next backward call, which then skips its sort_and_bin when the
+ * token is still the device's most recent sort and every geometry / opacity / colour pointer,
+ * length and static is identical; otherwise it sorts as usual. Arm it only when the forward's
+ * input buffers are unchanged since the forward. */
+int64_t splax_last_sort_token(void);
+void splax_reuse_sort(int64_t token);
+
 /* sort_and_bin, splax/_rasterize/_sort/_sort.py:29-171, exposed for parity tests: copies
  * the sorted flat gaussian ids (capacity gaussian_ids_cap) and the (B*T) int2 tile bins into
  * caller buffers, and optionally the sorted keys (as int64, NULL to skip). Writes the

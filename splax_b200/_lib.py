@@ -45,6 +45,8 @@ SIGNATURES: dict[str, list] = {
     "splax_scratch_info": [P, I32],
     "splax_check_device_errors": [P],
     "splax_debug_fail_alloc_after": [I64],
+    "splax_last_sort_token": [],
+    "splax_reuse_sort": [I64],
     "splax_profile_enable": [I32, I32],
     "splax_profile_reset": [],
     "splax_profile_report": [P, I32],
@@ -78,6 +80,8 @@ def load() -> ctypes.CDLL:
     lib.splax_clear_cache.restype = None
     lib.splax_debug_fail_alloc_after.restype = None
     lib.splax_profile_enable.restype = None
+    lib.splax_last_sort_token.restype = ctypes.c_int64
+    lib.splax_reuse_sort.restype = None
     _lib = lib
     return lib
 

@@ -49,6 +49,9 @@ class _RasterizeFn(torch.autograd.Function):
             else:
                 rc = lib.splax_rasterize(*args, _lib.stream_of(col))
         _lib.check(rc)
+        # the backward reuses this sort: autograd's version counters guarantee that the saved
+        # inputs are unchanged when it runs
+        ctx.sort_token = lib.splax_last_sort_token()
         ctx.save_for_backward(col, op, mo, bg, xy, dp, rd, cn, cum, final_Ts, final_idx)
         ctx.statics = (n, img_h, img_w, B, with_depth, key_bits)
         ctx.shapes = (colors.shape, opacities.shape, xys.shape, depths.shape, conics.shape)
@@ -79,6 +82,7 @@ class _RasterizeFn(torch.autograd.Function):
                   p(final_idx), p(vo), vo.numel() // (3 * img_w)]
         v_depths = None
         with torch.cuda.device(dev):
+            lib.splax_reuse_sort(ctx.sort_token)
             if with_depth:
                 v_dimg = rest[0]
                 vd = (_f32(v_dimg) if v_dimg is not None

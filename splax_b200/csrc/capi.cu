@@ -150,6 +150,34 @@ struct WorkUnits {
   int64_t visible = 0;         // not tracked on the host (device counters below)
   int64_t pixels_fwd = 0, pixels_bwd = 0;
   int64_t bins = 0;
+  int64_t sort_reuses = 0;   // backward passes that reused the forward's sort
+};
+
+struct SortOut {
+  const int32_t* gids = nullptr;
+  const void* keys = nullptr;
+  const int32_t* bins = nullptr;
+  const float4* records = nullptr;
+  int64_t count = 0;
+  int32_t tbx = 0, tby = 0, num_tiles = 0;
+  int key_bits = 0;
+};
+
+struct SortIn {
+  const float* xys;
+  const float* depths;
+  const int32_t* radii;
+  const float* conics;
+  const float* map_opacities;
+  int64_t map_rows;
+  const float* opacities;
+  int64_t opac_rows;
+  const float* colors;
+  int64_t color_rows;
+  const int32_t* cum;
+  int64_t n, B;
+  int32_t img_h, img_w;
+  int key_req;
 };
 
 struct DeviceState {
@@ -169,6 +197,12 @@ struct DeviceState {
   DevBuf work;                // device work counters: fwd evals, fwd contribs, bwd evals, bwd contribs
   KernelTimer timer;
   WorkUnits units;
+  // the most recent sort_and_bin result, reusable by a backward over the same inputs
+  uint64_t sort_gen = 0;
+  bool last_valid = false;
+  uint64_t last_gen = 0;
+  SortIn last_in{};
+  SortOut last_out{};
 
   unsigned long long* work_fwd() {
     return g_count_work.load() ? static_cast<unsigned long long*>(work.p) : nullptr;
@@ -189,6 +223,8 @@ struct DeviceState {
   }
 
   void drop_entry() {
+    last_valid = false;
+    ++sort_gen;
     for (DevBuf* b : {&keys[0], &keys[1], &vals[0], &vals[1], &records, &tile_bins, &depth_mm,
                       &status})
       buf_free(*b);
@@ -255,37 +291,12 @@ int report_device_error(DeviceState& st, unsigned w, cudaStream_t stream) {
   return fail(code, std::string("device check failed: ") + describe_device_error(w));
 }
 
-struct SortOut {
-  const int32_t* gids = nullptr;
-  const void* keys = nullptr;
-  const int32_t* bins = nullptr;
-  const float4* records = nullptr;
-  int64_t count = 0;
-  int32_t tbx = 0, tby = 0, num_tiles = 0;
-  int key_bits = 0;
-};
-
-struct SortIn {
-  const float* xys;
-  const float* depths;
-  const int32_t* radii;
-  const float* conics;
-  const float* map_opacities;
-  int64_t map_rows;
-  const float* opacities;
-  int64_t opac_rows;
-  const float* colors;
-  int64_t color_rows;
-  const int32_t* cum;
-  int64_t n, B;
-  int32_t img_h, img_w;
-  int key_req;
-};
-
 // sort_and_bin (splax/_rasterize/_sort/_sort.py:29-171) plus the record packing.
 int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut& out) {
   int rc = st.init();
   if (rc) return rc;
+  st.last_valid = false;  // the scratch is about to be rewritten
+  ++st.sort_gen;
   const int32_t tbx = (in.img_w + kBlockWidth - 1) / kBlockWidth;
   const int32_t tby = (in.img_h + kBlockWidth - 1) / kBlockWidth;
   const int64_t num_tiles = static_cast<int64_t>(tbx) * tby;
@@ -378,7 +389,13 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
   out.records = static_cast<const float4*>(st.records.p);
   out.gids = static_cast<const int32_t*>(st.vals[0].p);
   out.keys = st.keys[0].p;
-  if (count == 0) return SPLAX_OK;
+  if (count == 0) {
+    st.last_valid = true;
+    st.last_gen = st.sort_gen;
+    st.last_in = in;
+    st.last_out = out;
+    return SPLAX_OK;
+  }
 
   EmitArgs ea;
   ea.xys = in.xys;
@@ -434,8 +451,26 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
   st.units.key_bytes += count * static_cast<int64_t>(key_size);
   st.units.sort_passes += count > 1 ? count * passes : 0;
   st.units.bins += bins_len;
+  st.last_valid = true;
+  st.last_gen = st.sort_gen;
+  st.last_in = in;
+  st.last_out = out;
   SPLAX_CUDA(cudaGetLastError());
   return SPLAX_OK;
+}
+
+// Sort reuse between a forward and its backward: the forward leaves its sort's token in the
+// calling thread; the caller re-arms it before the backward, which then skips sort_and_bin when
+// the token is still the device's latest sort and every input pointer and size is identical.
+thread_local int64_t g_last_sort_token = -1;
+thread_local int64_t g_armed_sort_token = -1;
+
+bool same_sort_inputs(const SortIn& a, const SortIn& b) {
+  return a.xys == b.xys && a.depths == b.depths && a.radii == b.radii && a.conics == b.conics &&
+         a.map_opacities == b.map_opacities && a.map_rows == b.map_rows &&
+         a.opacities == b.opacities && a.opac_rows == b.opac_rows && a.colors == b.colors &&
+         a.color_rows == b.color_rows && a.cum == b.cum && a.n == b.n && a.B == b.B &&
+         a.img_h == b.img_h && a.img_w == b.img_w && a.key_req == b.key_req;
 }
 
 bool sync_check_enabled() {
@@ -488,8 +523,10 @@ int rasterize_common(const float* colors, int64_t colors_rows, const float* opac
   SortIn in{xys, depths, radii, conics, map_opacities, map_rows, opacities, opacities_rows,
             colors, colors_rows, cum, n, B, img_h, img_w, key_bits};
   SortOut so;
+  g_last_sort_token = -1;
   rc = sort_and_bin(*st, in, stream, so);
   if (rc) return rc;
+  g_last_sort_token = static_cast<int64_t>(st->sort_gen);
   RasterFwdArgs ra;
   ra.img_h = img_h;
   ra.img_w = img_w;
@@ -551,8 +588,16 @@ int rasterize_bwd_common(const float* colors, int64_t colors_rows, const float* 
   SortIn in{xys, depths, radii, conics, map_opacities, map_rows, opacities, opacities_rows,
             colors, colors_rows, cum, n, B_geom, img_h, img_w, key_bits};
   SortOut so;
-  rc = sort_and_bin(*st, in, stream, so);
-  if (rc) return rc;
+  const int64_t armed = g_armed_sort_token;
+  g_armed_sort_token = -1;
+  if (armed >= 0 && st->last_valid && static_cast<uint64_t>(armed) == st->last_gen &&
+      same_sort_inputs(st->last_in, in)) {
+    so = st->last_out;
+    st->units.sort_reuses += 1;
+  } else {
+    rc = sort_and_bin(*st, in, stream, so);
+    if (rc) return rc;
+  }
   if (so.count == 0) return finish(*st, stream);
   RasterBwdArgs ba;
   ba.img_h = img_h;
@@ -910,6 +955,10 @@ int splax_check_device_errors(void* stream_) {
 
 void splax_debug_fail_alloc_after(int64_t successes) { g_fail_after.store(successes); }
 
+int64_t splax_last_sort_token(void) { return g_last_sort_token; }
+
+void splax_reuse_sort(int64_t token) { g_armed_sort_token = token; }
+
 void splax_profile_enable(int32_t timing, int32_t count_work) {
   g_timing.store(timing != 0);
   g_count_work.store(count_work != 0);
@@ -955,8 +1004,10 @@ int splax_profile_report(char* buf, int32_t len) {
   js += tmp;
   snprintf(tmp, sizeof tmp,
            "\"pixels_fwd\": %lld, \"pixels_bwd\": %lld, \"fwd_evals\": %llu, "
-           "\"fwd_contribs\": %llu, \"bwd_evals\": %llu, \"bwd_contribs\": %llu}}",
-           (long long)u.pixels_fwd, (long long)u.pixels_bwd, w[0], w[1], w[2], w[3]);
+           "\"fwd_contribs\": %llu, \"bwd_evals\": %llu, \"bwd_contribs\": %llu, "
+           "\"sort_reuses\": %lld}}",
+           (long long)u.pixels_fwd, (long long)u.pixels_bwd, w[0], w[1], w[2], w[3],
+           (long long)u.sort_reuses);
   js += tmp;
   if (static_cast<int32_t>(js.size()) + 1 > len) return -SPLAX_ERR_INVALID_ARGUMENT;
   memcpy(buf, js.c_str(), js.size() + 1);

@@ -178,6 +178,17 @@ __device__ __forceinline__ int32_t ellipse_tile_count(const Ellipse& s) {
   return count;
 }
 
+// Hardware base-2 exponential (MUFU): the blend kernels' exponent is pre-scaled by log2(e).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// log2(e) / 2 and log2(e), the scales of the staged conic q = -(log2 e / 2) * (a, 2b, c)
+constexpr float kHalfLog2e = 0.721347520444482f;
+constexpr float kLog2e = 1.442695040888963f;
+
 // Ordered-integer image of a float, so atomicMin / atomicMax on int32 order like floats.
 __device__ __forceinline__ int32_t float_to_ordered(float f) {
   int32_t i = __float_as_int(f);
@@ -185,6 +196,17 @@ __device__ __forceinline__ int32_t float_to_ordered(float f) {
 }
 __device__ __forceinline__ float ordered_to_float(int32_t i) {
   return __int_as_float(i >= 0 ? i : i ^ 0x7fffffff);
+}
+
+// Relaxed gpu-scope accesses for look-back status words: the flag and the value share one
+// 64-bit word, so a reader that sees the flag sees its value and no fence is needed.
+__device__ __forceinline__ void st_relaxed(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
 
 // Release / acquire accesses for look-back status words.

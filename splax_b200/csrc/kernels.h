@@ -53,7 +53,8 @@ struct ProjectBwdArgs {
 };
 
 // Per-gaussian record staged by the blend kernels: 3 x float4 =
-// (x, y, conic_a, conic_b), (conic_c, opacity, r, g), (b, depth, 0, 0).
+// (x, y, qa, qb), (qc, opacity, r, g), (b, depth, 0, 0), with the conic pre-scaled for a
+// base-2 exponent: (qa, qb, qc) = -log2(e)/2 * (a, 2b, c).
 constexpr int kRecordFloat4 = 3;
 
 struct EmitArgs {

@@ -223,13 +223,13 @@ project_fwd_kernel(ProjectArgs a, unsigned long long* status, int* ticket, unsig
     unsigned long long agg = static_cast<unsigned long long>(s_warp[kProjThreads / 32 - 1]);
     long long prefix = 0;
     if (tile == 0) {
-      st_release(&status[0], kFlagInc | agg);
+      st_relaxed(&status[0], kFlagInc | agg);
     } else {
-      st_release(&status[tile], kFlagAgg | agg);
+      st_relaxed(&status[tile], kFlagAgg | agg);
       int j = tile - 1;
       long long spins = 0;
       while (j >= 0) {
-        unsigned long long s = ld_acquire(&status[j]);
+        unsigned long long s = ld_relaxed(&status[j]);
         unsigned long long flag = s & ~kValMask;
         if (flag == 0) {
           if (++spins > kSpinLimit) {
@@ -242,7 +242,7 @@ project_fwd_kernel(ProjectArgs a, unsigned long long* status, int* ticket, unsig
         if (flag == kFlagInc) break;
         --j;
       }
-      st_release(&status[tile], kFlagInc | (static_cast<unsigned long long>(prefix) + agg));
+      st_relaxed(&status[tile], kFlagInc | (static_cast<unsigned long long>(prefix) + agg));
     }
     s_prefix = prefix;
     if (static_cast<int64_t>(tile + 1) * kProjThreads >= a.total &&

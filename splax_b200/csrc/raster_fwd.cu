@@ -1,12 +1,16 @@
 // Forward blend: _rasterize_kernel and _rasterize_depth_kernel
 // (splax/_rasterize/_kernels.py:102-205, 277-380).
 //
-// One 256-thread CTA per (image, 16x16 tile), one pixel per thread. The tile's sorted list is
-// walked in batches of 256: each thread gathers one packed 48-byte gaussian record (three
-// 16-byte loads from the record array the emission pass wrote) into shared memory, then every
-// thread blends the batch front to back from shared memory (broadcast reads). A block vote
-// (__syncthreads_count) ends the walk once every pixel's transmittance has saturated.
-// Pixel semantics match the reference exactly: a gaussian is skipped when sigma < 0 or
+// One 128-thread CTA per (image, 16x16 tile); each thread owns two pixels of one column,
+// rows li and li + 8, so every shared-memory record read and the x-terms of the Gaussian
+// exponent serve two evaluations. The tile's sorted list is walked in batches of 256: the CTA
+// gathers the packed 48-byte records (three 16-byte loads each, written by the emission pass)
+// into shared memory, then blends the batch front to back from shared memory with broadcast
+// reads. Records carry the conic pre-scaled by -log2(e)/2, so the exponent is a quadratic form
+// evaluated with FMAs and one ex2. A block vote (__syncthreads_count) ends the walk once every
+// pixel has saturated.
+//
+// Pixel semantics are the reference's: a gaussian is skipped when sigma < 0 (exponent > 0) or
 // alpha < 1/255, and the walk stops before the gaussian that would take T to <= 1e-4.
 #include "common.cuh"
 #include "kernels.h"
@@ -14,8 +18,40 @@
 namespace splax {
 namespace {
 
+constexpr int kFwdThreads = 128;
+
+struct PixelState {
+  float T = 1.0f, c0 = 0.0f, c1 = 0.0f, c2 = 0.0f, dep = 0.0f;
+  int32_t cur_idx = 0;
+  bool done;
+};
+
 template <bool DEPTH, bool COUNT>
-__global__ void __launch_bounds__(kBlockSize)
+__device__ __forceinline__ void blend_one(PixelState& s, float p, float opac, float r, float g,
+                                          float b, float depth, int32_t idx,
+                                          unsigned long long& evals,
+                                          unsigned long long& contribs) {
+  if (s.done) return;
+  if constexpr (COUNT) ++evals;
+  const float alpha = fminf(kAlphaMax, opac * ex2_approx(p));
+  if (p > 0.0f || alpha < kAlphaThreshold) return;
+  const float next_T = s.T * (1.0f - alpha);
+  if (next_T <= kTransmittanceMin) {
+    s.done = true;
+    return;
+  }
+  const float vis = alpha * s.T;
+  s.c0 += r * vis;
+  s.c1 += g * vis;
+  s.c2 += b * vis;
+  if constexpr (DEPTH) s.dep += depth * vis;
+  s.T = next_T;
+  s.cur_idx = idx;
+  if constexpr (COUNT) ++contribs;
+}
+
+template <bool DEPTH, bool COUNT>
+__global__ void __launch_bounds__(kFwdThreads)
 raster_fwd_kernel(RasterFwdArgs a) {
   unsigned long long evals = 0, contribs = 0;
   __shared__ float4 s_r0[kBlockSize];
@@ -26,61 +62,57 @@ raster_fwd_kernel(RasterFwdArgs a) {
   const int32_t tile_local = static_cast<int32_t>(tile_g % a.num_tiles);
   const int32_t tile_x = tile_local % a.tbx, tile_y = tile_local / a.tbx;
   const int tr = threadIdx.x;
-  const int32_t i = tile_y * kBlockWidth + tr / kBlockWidth;
-  const int32_t j = tile_x * kBlockWidth + tr % kBlockWidth;
-  const float px = static_cast<float>(j) + 0.5f, py = static_cast<float>(i) + 0.5f;
-  const bool inside = i < a.img_h && j < a.img_w;
-  bool done = !inside;
+  const int32_t j = tile_x * kBlockWidth + (tr & 15);
+  const int32_t i0 = tile_y * kBlockWidth + (tr >> 4), i1 = i0 + 8;
+  const float px = static_cast<float>(j) + 0.5f;
+  const float py0 = static_cast<float>(i0) + 0.5f;
+  const bool inside0 = i0 < a.img_h && j < a.img_w;
+  const bool inside1 = i1 < a.img_h && j < a.img_w;
+  PixelState s0, s1;
+  s0.done = !inside0;
+  s1.done = !inside1;
   const int2 range = reinterpret_cast<const int2*>(a.tile_bins)[tile_g];
   const int32_t range_start = range.x, range_end = range.y;
   const int32_t num_batches = (range_end - range_start + kBlockSize - 1) / kBlockSize;
-  float T = 1.0f;
-  int32_t cur_idx = 0;
-  float c0 = 0.0f, c1 = 0.0f, c2 = 0.0f, dep = 0.0f;
   for (int32_t b = 0; b < num_batches; ++b) {
     // block vote doubles as the barrier protecting the previous batch's shared reads
-    if (__syncthreads_count(done) >= kBlockSize) break;
+    if (__syncthreads_count(s0.done && s1.done) >= kFwdThreads) break;
     const int32_t batch_start = range_start + b * kBlockSize;
-    const int32_t src = batch_start + tr;
-    if (src < range_end) {
-      const int64_t g = a.gids[src];
-      if (g >= 0 && g < a.num_records) {
-        const float4* rec = a.records + kRecordFloat4 * g;
-        s_r0[tr] = rec[0];
-        s_r1[tr] = rec[1];
-        const float4 r2 = rec[2];
-        s_r2[tr] = make_float2(r2.x, r2.y);
-      } else {  // only after a reported emission error: stage a transparent record
-        s_r0[tr] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        s_r1[tr] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        s_r2[tr] = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int h = 0; h < kBlockSize / kFwdThreads; ++h) {
+      const int slot = tr + h * kFwdThreads;
+      const int32_t src = batch_start + slot;
+      if (src < range_end) {
+        const int64_t g = a.gids[src];
+        if (g >= 0 && g < a.num_records) {
+          const float4* rec = a.records + kRecordFloat4 * g;
+          s_r0[slot] = rec[0];
+          s_r1[slot] = rec[1];
+          const float4 r2 = rec[2];
+          s_r2[slot] = make_float2(r2.x, r2.y);
+        } else {  // only after a reported emission error: stage a transparent record
+          s_r0[slot] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          s_r1[slot] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          s_r2[slot] = make_float2(0.0f, 0.0f);
+        }
       }
     }
     __syncthreads();
     const int32_t batch_size = min(kBlockSize, range_end - batch_start);
-    if (!done) {
+    if (!(s0.done && s1.done)) {
       for (int32_t t = 0; t < batch_size; ++t) {
-        const float4 r0 = s_r0[t];
-        const float4 r1 = s_r1[t];
-        const float dx = r0.x - px, dy = r0.y - py;
-        const float sigma = 0.5f * (r0.z * dx * dx + r1.x * dy * dy) + r0.w * dx * dy;
-        const float alpha = fminf(kAlphaMax, r1.y * __expf(-sigma));
-        if constexpr (COUNT) ++evals;
-        if (sigma < 0.0f || alpha < kAlphaThreshold) continue;
-        const float next_T = T * (1.0f - alpha);
-        if (next_T <= kTransmittanceMin) {
-          done = true;
-          break;
-        }
-        const float vis = alpha * T;
-        const float2 r2 = s_r2[t];
-        c0 += r1.z * vis;
-        c1 += r1.w * vis;
-        c2 += r2.x * vis;
-        if constexpr (DEPTH) dep += r2.y * vis;
-        T = next_T;
-        cur_idx = batch_start + t;
-        if constexpr (COUNT) ++contribs;
+        const float4 r0 = s_r0[t];  // x, y, qa, qb  (q = -log2(e)/2 * (a, 2b, c))
+        const float4 r1 = s_r1[t];  // qc, opacity, r, g
+        const float2 r2 = s_r2[t];  // b, depth
+        const float dx = r0.x - px;
+        const float dy0 = r0.y - py0, dy1 = dy0 - 8.0f;
+        const float qxx = r0.z * dx * dx, qbx = r0.w * dx;
+        const float p0 = fmaf(fmaf(r1.x, dy0, qbx), dy0, qxx);
+        const float p1 = fmaf(fmaf(r1.x, dy1, qbx), dy1, qxx);
+        const int32_t idx = batch_start + t;
+        blend_one<DEPTH, COUNT>(s0, p0, r1.y, r1.z, r1.w, r2.x, r2.y, idx, evals, contribs);
+        blend_one<DEPTH, COUNT>(s1, p1, r1.y, r1.z, r1.w, r2.x, r2.y, idx, evals, contribs);
+        if (s0.done && s1.done) break;
       }
     }
   }
@@ -92,15 +124,20 @@ raster_fwd_kernel(RasterFwdArgs a) {
       atomicAdd(&a.work[1], contribs);
     }
   }
-  if (inside) {
-    const float* bg = a.background + 3 * (a.sel_bg ? image_id : 0);
+  const float* bg = a.background + 3 * (a.sel_bg ? image_id : 0);
+  const float bg0 = bg[0], bg1 = bg[1], bg2 = bg[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const PixelState& s = k ? s1 : s0;
+    if (!(k ? inside1 : inside0)) continue;
+    const int32_t i = k ? i1 : i0;
     const int64_t pix = (image_id * a.img_h + i) * static_cast<int64_t>(a.img_w) + j;
-    a.final_Ts[pix] = T;
-    a.final_idx[pix] = cur_idx;
-    a.out_img[3 * pix] = c0 + T * bg[0];
-    a.out_img[3 * pix + 1] = c1 + T * bg[1];
-    a.out_img[3 * pix + 2] = c2 + T * bg[2];
-    if constexpr (DEPTH) a.out_depth[pix] = dep;
+    a.final_Ts[pix] = s.T;
+    a.final_idx[pix] = s.cur_idx;
+    a.out_img[3 * pix] = s.c0 + s.T * bg0;
+    a.out_img[3 * pix + 1] = s.c1 + s.T * bg1;
+    a.out_img[3 * pix + 2] = s.c2 + s.T * bg2;
+    if constexpr (DEPTH) a.out_depth[pix] = s.dep;
   }
 }
 
@@ -111,11 +148,11 @@ void launch_raster_fwd(const RasterFwdArgs& a, cudaStream_t stream) {
   if (blocks == 0) return;
   const unsigned g = static_cast<unsigned>(blocks);
   if (a.out_depth) {
-    if (a.work) raster_fwd_kernel<true, true><<<g, kBlockSize, 0, stream>>>(a);
-    else raster_fwd_kernel<true, false><<<g, kBlockSize, 0, stream>>>(a);
+    if (a.work) raster_fwd_kernel<true, true><<<g, kFwdThreads, 0, stream>>>(a);
+    else raster_fwd_kernel<true, false><<<g, kFwdThreads, 0, stream>>>(a);
   } else {
-    if (a.work) raster_fwd_kernel<false, true><<<g, kBlockSize, 0, stream>>>(a);
-    else raster_fwd_kernel<false, false><<<g, kBlockSize, 0, stream>>>(a);
+    if (a.work) raster_fwd_kernel<false, true><<<g, kFwdThreads, 0, stream>>>(a);
+    else raster_fwd_kernel<false, false><<<g, kFwdThreads, 0, stream>>>(a);
   }
 }
 

@@ -96,8 +96,9 @@ __global__ void __launch_bounds__(256) emit_kernel(EmitArgs a) {
     const int64_t ci = idx % a.color_rows;
     const float op = a.opacities[idx % a.opac_rows];
     float4* rec = a.records + kRecordFloat4 * idx;
-    rec[0] = make_float4(x, y, ca, cb);
-    rec[1] = make_float4(cc, op, a.colors[3 * ci], a.colors[3 * ci + 1]);
+    // conic pre-scaled for the blends' base-2 exponent: q = -log2(e)/2 * (a, 2b, c)
+    rec[0] = make_float4(x, y, -kHalfLog2e * ca, -kLog2e * cb);
+    rec[1] = make_float4(-kHalfLog2e * cc, op, a.colors[3 * ci], a.colors[3 * ci + 1]);
     rec[2] = make_float4(a.colors[3 * ci + 2], depth, 0.0f, 0.0f);
   }
   uint64_t enc;
@@ -150,25 +151,26 @@ __global__ void __launch_bounds__(256) emit_kernel(EmitArgs a) {
 }
 
 // ------------------------------------------------------------------ onesweep radix sort
-constexpr int kSortThreads = 256;
+constexpr int kSortThreads = 512;
 constexpr int kSortWarps = kSortThreads / 32;
-constexpr int kItems32 = 16;  // 4096 keys per tile for 32-bit keys
-constexpr int kItems64 = 12;  // 3072 keys per tile for 64-bit keys
+constexpr int kItems32 = 8;  // 4096 keys per tile for 32-bit keys
+constexpr int kItems64 = 6;  // 3072 keys per tile for 64-bit keys
+constexpr int kHistThreads = 256;
 constexpr int kHistItems = 32;
 constexpr unsigned long long kFlagAgg = 1ull << 62;
 constexpr unsigned long long kFlagInc = 2ull << 62;
 constexpr unsigned long long kValMask = (1ull << 62) - 1;
 
 template <typename K>
-__global__ void __launch_bounds__(kSortThreads)
+__global__ void __launch_bounds__(kHistThreads)
 radix_hist_kernel(const K* __restrict__ keys, int64_t count, int passes, uint32_t* hist) {
   __shared__ uint32_t s[8][256];
-  for (int i = threadIdx.x; i < 8 * 256; i += kSortThreads) (&s[0][0])[i] = 0;
+  for (int i = threadIdx.x; i < 8 * 256; i += kHistThreads) (&s[0][0])[i] = 0;
   __syncthreads();
-  const int64_t base = static_cast<int64_t>(blockIdx.x) * kSortThreads * kHistItems;
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kHistThreads * kHistItems;
 #pragma unroll 4
   for (int k = 0; k < kHistItems; ++k) {
-    const int64_t i = base + k * kSortThreads + threadIdx.x;
+    const int64_t i = base + k * kHistThreads + threadIdx.x;
     if (i >= count) break;
     const uint64_t key = static_cast<uint64_t>(keys[i]);
     for (int p = 0; p < passes; ++p) atomicAdd(&s[p][(key >> (8 * p)) & 255u], 1u);
@@ -180,7 +182,9 @@ radix_hist_kernel(const K* __restrict__ keys, int64_t count, int passes, uint32_
   }
 }
 
-__device__ __forceinline__ uint32_t block_exclusive_scan_256(uint32_t v, uint32_t* s_warp) {
+// Exclusive scan over the block (NT threads); s_warp holds NT/32 words.
+template <int NT>
+__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* s_warp) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   uint32_t inc = v;
 #pragma unroll
@@ -197,10 +201,10 @@ __device__ __forceinline__ uint32_t block_exclusive_scan_256(uint32_t v, uint32_
 
 // exclusive scan of each pass's 256-digit histogram: offsets[p][d]
 __global__ void radix_scan_kernel(const uint32_t* hist, uint32_t* offsets) {
-  __shared__ uint32_t s_warp[kSortWarps];
+  __shared__ uint32_t s_warp[8];
   const int p = blockIdx.x;
   const uint32_t v = hist[p * 256 + threadIdx.x];
-  offsets[p * 256 + threadIdx.x] = block_exclusive_scan_256(v, s_warp);
+  offsets[p * 256 + threadIdx.x] = block_exclusive_scan<256>(v, s_warp);
 }
 
 template <typename K, int ITEMS>
@@ -240,18 +244,13 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
     k[it] = valid ? kin[base + pos] : K(0);
     val[it] = valid ? vin[base + pos] : 0;
   }
+  // stable warp-level ranking: keys of one digit keep their input order (iteration, lane)
 #pragma unroll
   for (int it = 0; it < ITEMS; ++it) {
     const int pos = warp_base + it * 32 + lane;
     const bool valid = pos < nvalid;
     const uint32_t d = static_cast<uint32_t>(static_cast<uint64_t>(k[it]) >> shift) & 255u;
-    unsigned peers = __ballot_sync(0xffffffffu, valid);
-#pragma unroll
-    for (int b = 0; b < 8; ++b) {
-      const bool bit = (d >> b) & 1u;
-      const unsigned bal = __ballot_sync(0xffffffffu, bit);
-      peers &= bit ? bal : ~bal;
-    }
+    const unsigned peers = __match_any_sync(0xffffffffu, valid ? d : 256u + lane);
     const uint32_t lt = __popc(peers & lt_mask);
     const uint32_t prev = valid ? s_wh[warp][d] : 0u;
     __syncwarp();
@@ -260,43 +259,46 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
     rank[it] = prev + lt;
   }
   __syncthreads();
-  // per digit (one thread each): warp exclusive offsets and the block's count
-  const int dg = tid;
+  // per digit (threads 0..255): warp exclusive offsets, the block's count, the look-back
   uint32_t sum = 0;
-#pragma unroll
-  for (int w = 0; w < kSortWarps; ++w) {
-    const uint32_t c = s_wh[w][dg];
-    s_wh[w][dg] = sum;
-    sum += c;
-  }
-  // decoupled look-back over preceding tiles for this digit
   long long prefix = 0;
-  unsigned long long* st = status + tile * 256 + dg;
-  if (tile == 0) {
-    st_release(st, kFlagInc | sum);
-  } else {
-    st_release(st, kFlagAgg | sum);
-    int64_t j = tile - 1;
-    long long spins = 0;
-    while (j >= 0) {
-      const unsigned long long s = ld_acquire(status + j * 256 + dg);
-      const unsigned long long flag = s & ~kValMask;
-      if (flag == 0) {
-        if (++spins > kSpinLimit) {
-          atomicOr(err, kErrLookbackTimeout);
-          break;
-        }
-        continue;
-      }
-      prefix += static_cast<long long>(s & kValMask);
-      if (flag == kFlagInc) break;
-      --j;
+  if (tid < 256) {
+    const int dg = tid;
+#pragma unroll
+    for (int w = 0; w < kSortWarps; ++w) {
+      const uint32_t c = s_wh[w][dg];
+      s_wh[w][dg] = sum;
+      sum += c;
     }
-    st_release(st, kFlagInc | (static_cast<unsigned long long>(prefix) + sum));
+    unsigned long long* st = status + tile * 256 + dg;
+    if (tile == 0) {
+      st_relaxed(st, kFlagInc | sum);
+    } else {
+      st_relaxed(st, kFlagAgg | sum);
+      int64_t j = tile - 1;
+      long long spins = 0;
+      while (j >= 0) {
+        const unsigned long long s = ld_relaxed(status + j * 256 + dg);
+        const unsigned long long flag = s & ~kValMask;
+        if (flag == 0) {
+          if (++spins > kSpinLimit) {
+            atomicOr(err, kErrLookbackTimeout);
+            break;
+          }
+          continue;
+        }
+        prefix += static_cast<long long>(s & kValMask);
+        if (flag == kFlagInc) break;
+        --j;
+      }
+      st_relaxed(st, kFlagInc | (static_cast<unsigned long long>(prefix) + sum));
+    }
   }
-  const uint32_t excl = block_exclusive_scan_256(sum, s_warp);
-  s_bx[dg] = excl;
-  s_gb[dg] = static_cast<long long>(goff[dg]) + prefix - static_cast<long long>(excl);
+  const uint32_t excl = block_exclusive_scan<kSortThreads>(sum, s_warp);
+  if (tid < 256) {
+    s_bx[tid] = excl;
+    s_gb[tid] = static_cast<long long>(goff[tid]) + prefix - static_cast<long long>(excl);
+  }
   __syncthreads();
 #pragma unroll
   for (int it = 0; it < ITEMS; ++it) {
@@ -361,13 +363,19 @@ int sort_impl(const SortScratch& s, int64_t count, int bits, cudaStream_t stream
   uint32_t* offsets = s.hist + 8 * 256;
   cudaMemsetAsync(hist, 0, sizeof(uint32_t) * 8 * 256, stream);
   cudaMemsetAsync(s.tile_counters, 0, sizeof(int) * 8, stream);
-  const int64_t hblocks = (count + kSortThreads * kHistItems - 1) / (kSortThreads * kHistItems);
-  radix_hist_kernel<K><<<static_cast<unsigned>(hblocks), kSortThreads, 0, stream>>>(
+  const int64_t hblocks = (count + kHistThreads * kHistItems - 1) / (kHistThreads * kHistItems);
+  radix_hist_kernel<K><<<static_cast<unsigned>(hblocks), kHistThreads, 0, stream>>>(
       reinterpret_cast<const K*>(s.keys[0]), count, passes, hist);
   radix_scan_kernel<<<passes, 256, 0, stream>>>(hist, offsets);
   constexpr int TILE = kSortThreads * ITEMS;
   const int64_t tiles = (count + TILE - 1) / TILE;
   const size_t smem = TILE * (sizeof(K) + sizeof(int32_t));
+  static bool attr_set = false;  // per instantiation: static + dynamic exceeds 48 KiB
+  if (!attr_set) {
+    cudaFuncSetAttribute(onesweep_kernel<K, ITEMS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    attr_set = true;
+  }
   int cur = 0;
   for (int p = 0; p < passes; ++p) {
     cudaMemsetAsync(s.status, 0, sizeof(unsigned long long) * tiles * 256, stream);

@@ -286,3 +286,33 @@ def test_key_overflow_raises(sx):
 
     with pytest.raises(ValueError, match="key overflow"):
         srt.key_bits_for(1 << 20, 4096, 8192)
+
+
+def test_backward_reuses_forward_sort(sx):
+    """The backward skips its re-sort when the forward's sort is still the device's latest one,
+    and re-sorts (same gradients) when another render ran in between."""
+    from splax_b200 import _lib
+
+    n, H, W = 20_000, 200, 240
+    m, s, q, c, op, bg = random_scene(n, 12)
+    w = T(np.random.default_rng(5).uniform(size=(H, W, 3)))
+    other = random_scene(5000, 13)
+
+    def grads(intervene):
+        params = [T(x).requires_grad_() for x in (m, s, q, c, op)]
+        img, _ = sx.render(*params, viewmat=T(viewmat()), background=T(bg), **cam(H, W))
+        if intervene:
+            sx.render(*(T(x) for x in other[:5]), viewmat=T(viewmat()), background=T(bg),
+                      **cam(H, W))
+        (img * w).sum().backward()
+        return [N(p.grad) for p in params]
+
+    _lib.profile_reset()
+    g_reuse = grads(False)
+    reused = _lib.profile_report()["units"]["sort_reuses"]
+    _lib.profile_reset()
+    g_fresh = grads(True)
+    fresh = _lib.profile_report()["units"]["sort_reuses"]
+    assert reused == 1 and fresh == 0
+    for a, b in zip(g_reuse, g_fresh):
+        assert rel_l2(a, b) <= 1e-5
