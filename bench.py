@@ -329,6 +329,12 @@ def main() -> None:
             "radix_sort": per_launch("intersections", "radix_sort") * kb
             + 2 * passes * per_launch("intersections", "radix_sort") * (kb + 4),
             "tile_bins": per_launch("key_bytes", "tile_bins") + 8 * per_launch("bins", "tile_bins"),
+            # depth-order sort of the B*n pairs and the scan of their counts in that order
+            "pair_sort": per_launch("pair_key_bytes", "pair_sort")
+            + 2 * per_launch("pair_pass_keys", "pair_sort")
+            * (work["pair_key_bytes"] / max(work["pairs_sorted"], 1) + 4),
+            "pair_keys": 12 * per_launch("pairs_sorted", "pair_keys"),
+            "pair_scan": 12 * per_launch("pairs_sorted", "pair_scan"),
             "project_bwd": 120 * per_launch("pairs_bwd", "project_bwd"),
             "depth_minmax": 8 * pairs,
         }

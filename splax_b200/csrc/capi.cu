@@ -79,10 +79,11 @@ constexpr double kScratchHeadroom = 1.25;  // splax/_cache.py:149
 std::atomic<bool> g_timing{false};
 std::atomic<bool> g_count_work{false};
 
-enum Kind { kProjectFwd, kProjectBwd, kDepthMinmax, kEmit, kRadixSort, kTileBins, kRasterFwd,
-            kRasterBwd, kNumKinds };
-const char* kKindNames[kNumKinds] = {"project_fwd", "project_bwd", "depth_minmax", "emit_keys",
-                                     "radix_sort", "tile_bins", "raster_fwd", "raster_bwd"};
+enum Kind { kProjectFwd, kProjectBwd, kDepthMinmax, kPairKeys, kPairSort, kPairScan, kEmit,
+            kRadixSort, kTileBins, kRasterFwd, kRasterBwd, kNumKinds };
+const char* kKindNames[kNumKinds] = {"project_fwd", "project_bwd", "depth_minmax", "pair_keys",
+                                     "pair_sort", "pair_scan", "emit_keys", "radix_sort",
+                                     "tile_bins", "raster_fwd", "raster_bwd"};
 
 // CUDA-event timing of each launch sequence on the stream it runs on, resolved lazily.
 struct KernelTimer {
@@ -151,16 +152,21 @@ struct WorkUnits {
   int64_t pixels_fwd = 0, pixels_bwd = 0;
   int64_t bins = 0;
   int64_t sort_reuses = 0;   // backward passes that reused the forward's sort
+  int64_t pairs_sorted = 0;  // (camera, gaussian) pairs through the depth-order sort
+  int64_t pair_key_bytes = 0;
+  int64_t pair_pass_keys = 0;
 };
 
 struct SortOut {
   const int32_t* gids = nullptr;
-  const void* keys = nullptr;
+  const uint32_t* keys = nullptr;  // sorted (image | tile) bin keys
   const int32_t* bins = nullptr;
   const float4* records = nullptr;
   int64_t count = 0;
   int32_t tbx = 0, tby = 0, num_tiles = 0;
-  int key_bits = 0;
+  int key_bits = 0;  // the reference's key width for this call (32 packed, 64 wide)
+  int32_t tile_n_bits = 0, depth_bits = 0;
+  const int32_t* depth_mm = nullptr;
 };
 
 struct SortIn {
@@ -188,8 +194,9 @@ struct DeviceState {
   int key_bits = 0;
   int64_t isect_cap = 0;
   DevBuf keys[2], vals[2], records, tile_bins, depth_mm, status;
+  DevBuf pkeys[2], pvals[2], poffs, scan_status;  // depth-order sort of the B*n pairs
   // signature-independent pieces
-  DevBuf misc;        // [0] error word, [1] project ticket, [2..9] sort tile counters
+  DevBuf misc;  // [0] error word, [2..9] sort tile counters, [10] depth span, [11] scan ticket
   DevBuf hist;        // radix histograms and offsets
   DevBuf proj_status; // projection scan look-back words
   int32_t* pinned = nullptr;  // [0] count, [1] error word
@@ -213,11 +220,14 @@ struct DeviceState {
 
   unsigned* err_word() { return static_cast<unsigned*>(misc.p); }
   int* sort_counters() { return static_cast<int*>(misc.p) + 2; }
+  unsigned* span_word() { return static_cast<unsigned*>(misc.p) + 10; }
+  int* scan_ticket() { return static_cast<int*>(misc.p) + 11; }
 
   size_t bytes_held() const {
     size_t s = 0;
     for (const DevBuf* b : {&keys[0], &keys[1], &vals[0], &vals[1], &records, &tile_bins,
-                            &depth_mm, &status, &misc, &hist, &proj_status})
+                            &depth_mm, &status, &pkeys[0], &pkeys[1], &pvals[0], &pvals[1],
+                            &poffs, &scan_status, &misc, &hist, &proj_status})
       s += b->bytes;
     return s;
   }
@@ -226,7 +236,7 @@ struct DeviceState {
     last_valid = false;
     ++sort_gen;
     for (DevBuf* b : {&keys[0], &keys[1], &vals[0], &vals[1], &records, &tile_bins, &depth_mm,
-                      &status})
+                      &status, &pkeys[0], &pkeys[1], &pvals[0], &pvals[1], &poffs, &scan_status})
       buf_free(*b);
     sig_B = sig_n = sig_T = -1;
     key_bits = 0;
@@ -240,7 +250,7 @@ struct DeviceState {
     SPLAX_CUDA(buf_reserve(hist, sizeof(uint32_t) * 2 * 8 * 256));
     SPLAX_CUDA(buf_reserve(work, 4 * sizeof(unsigned long long)));
     SPLAX_CUDA(cudaMemset(work.p, 0, 4 * sizeof(unsigned long long)));
-    SPLAX_CUDA(cudaMallocHost(&pinned, 2 * sizeof(int32_t)));
+    SPLAX_CUDA(cudaMallocHost(&pinned, 4 * sizeof(int32_t)));
     SPLAX_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
     return SPLAX_OK;
   }
@@ -291,7 +301,10 @@ int report_device_error(DeviceState& st, unsigned w, cudaStream_t stream) {
   return fail(code, std::string("device check failed: ") + describe_device_error(w));
 }
 
-// sort_and_bin (splax/_rasterize/_sort/_sort.py:29-171) plus the record packing.
+// sort_and_bin (splax/_rasterize/_sort/_sort.py:29-171) plus the record packing. The sorted
+// order equals the reference's stable sort of (image | tile | depth key) keys, produced as a
+// stable depth-order sort of the B*n pairs followed by a stable sort of the intersections by
+// their (image | tile) field alone.
 int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut& out) {
   int rc = st.init();
   if (rc) return rc;
@@ -323,35 +336,40 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
   if (st.sig_B != in.B || st.sig_n != in.n || st.sig_T != num_tiles) {
     SPLAX_CUDA(cudaStreamSynchronize(stream));
     st.drop_entry();
-    rc = 0;
     cudaError_t e;
+    const int64_t ptiles = sorted_offsets_tiles(total);
     if ((e = buf_reserve(st.tile_bins, sizeof(int2) * bins_len)) != cudaSuccess ||
-        (e = buf_reserve(st.depth_mm, sizeof(int32_t) * 2 * (in.B > 0 ? in.B : 1))) !=
-            cudaSuccess ||
-        (e = buf_reserve(st.records, sizeof(float4) * kRecordFloat4 * (total > 0 ? total : 1))) !=
-            cudaSuccess) {
+        (e = buf_reserve(st.depth_mm, sizeof(int32_t) * 2 * in.B)) != cudaSuccess ||
+        (e = buf_reserve(st.records, sizeof(float4) * kRecordFloat4 * total)) != cudaSuccess ||
+        (e = buf_reserve(st.pkeys[0], sizeof(uint64_t) * total)) != cudaSuccess ||
+        (e = buf_reserve(st.pkeys[1], sizeof(uint64_t) * total)) != cudaSuccess ||
+        (e = buf_reserve(st.pvals[0], sizeof(int32_t) * total)) != cudaSuccess ||
+        (e = buf_reserve(st.pvals[1], sizeof(int32_t) * total)) != cudaSuccess ||
+        (e = buf_reserve(st.poffs, sizeof(int32_t) * total)) != cudaSuccess ||
+        (e = buf_reserve(st.scan_status, sizeof(unsigned long long) * ptiles)) != cudaSuccess) {
       st.drop_entry();
-      return cuda_fail(e, "scratch allocation (tile bins, depth ranges, records)");
+      return cuda_fail(e, "scratch allocation (tile bins, depth ranges, records, pair order)");
     }
     st.sig_B = in.B;
     st.sig_n = in.n;
     st.sig_T = num_tiles;
   }
-  // the one device-to-host sync: intersection count and the device error word
+  // count-independent work first, then the one device-to-host sync: intersection count,
+  // device error word and (wide keys) the largest per-image depth-bit span
+  int32_t* depth_mm = static_cast<int32_t*>(st.depth_mm.p);
+  st.timer.begin(kDepthMinmax, packed ? 2 : 3, stream);
+  launch_depth_minmax(in.depths, in.radii, total, in.n, static_cast<int32_t>(in.B), depth_mm,
+                      stream);
+  if (!packed) launch_depth_span(depth_mm, static_cast<int32_t>(in.B), st.span_word(), stream);
+  st.timer.end(stream);
   SPLAX_CUDA(cudaMemcpyAsync(&st.pinned[0], in.cum + (total - 1), sizeof(int32_t),
                              cudaMemcpyDeviceToHost, stream));
   SPLAX_CUDA(cudaMemcpyAsync(&st.pinned[1], st.err_word(), sizeof(int32_t),
                              cudaMemcpyDeviceToHost, stream));
+  SPLAX_CUDA(cudaMemcpyAsync(&st.pinned[2], st.span_word(), sizeof(int32_t),
+                             cudaMemcpyDeviceToHost, stream));
   SPLAX_CUDA(cudaEventRecord(st.ev, stream));
-  // count-independent work runs inside the sync bubble
   SPLAX_CUDA(cudaMemsetAsync(st.tile_bins.p, 0, sizeof(int2) * bins_len, stream));
-  int32_t* depth_mm = static_cast<int32_t*>(st.depth_mm.p);
-  if (packed) {
-    st.timer.begin(kDepthMinmax, 2, stream);
-    launch_depth_minmax(in.depths, in.radii, total, in.n, static_cast<int32_t>(in.B), depth_mm,
-                        stream);
-    st.timer.end(stream);
-  }
   SPLAX_CUDA(cudaEventSynchronize(st.ev));
   const unsigned werr = static_cast<unsigned>(st.pinned[1]);
   if (werr) return report_device_error(st, werr, stream);
@@ -360,35 +378,54 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
     return fail(SPLAX_ERR_COUNT_OVERFLOW,
                 "cum_tiles_hit[-1] is negative: the intersection count overflowed int32");
   const int kb = packed ? 32 : 64;
-  const size_t key_size = packed ? 4 : 8;
-  if (st.isect_cap < count || st.key_bits != kb) {
+  // pair key: image id above the depth key
+  const int key_shift = packed ? depth_bits : bit_length(static_cast<uint32_t>(st.pinned[2]));
+  const int pair_bits = image_n_bits + key_shift;
+  const bool pair64 = pair_bits > 32;
+  const int bin_bits = upper;
+  if (st.isect_cap < count) {
     const int64_t cap = std::max<int64_t>(static_cast<int64_t>(count * kScratchHeadroom) + 1,
-                                          st.key_bits == kb ? st.isect_cap : 0);
+                                          st.isect_cap);
     SPLAX_CUDA(cudaStreamSynchronize(stream));
-    for (DevBuf* b : {&st.keys[0], &st.keys[1], &st.vals[0], &st.vals[1], &st.status}) buf_free(*b);
+    for (DevBuf* b : {&st.keys[0], &st.keys[1], &st.vals[0], &st.vals[1]}) buf_free(*b);
     st.isect_cap = 0;
-    const int64_t tiles = (cap + sort_tile_items(!packed) - 1) / sort_tile_items(!packed);
     cudaError_t e;
-    if ((e = buf_reserve(st.keys[0], key_size * cap)) != cudaSuccess ||
-        (e = buf_reserve(st.keys[1], key_size * cap)) != cudaSuccess ||
+    if ((e = buf_reserve(st.keys[0], sizeof(uint32_t) * cap)) != cudaSuccess ||
+        (e = buf_reserve(st.keys[1], sizeof(uint32_t) * cap)) != cudaSuccess ||
         (e = buf_reserve(st.vals[0], sizeof(int32_t) * cap)) != cudaSuccess ||
-        (e = buf_reserve(st.vals[1], sizeof(int32_t) * cap)) != cudaSuccess ||
-        (e = buf_reserve(st.status, sizeof(unsigned long long) * 256 * tiles)) != cudaSuccess) {
+        (e = buf_reserve(st.vals[1], sizeof(int32_t) * cap)) != cudaSuccess) {
       st.drop_entry();
       return cuda_fail(e, "sort scratch allocation");
     }
     st.isect_cap = cap;
+  }
+  {
+    // look-back words for the larger of the two sorts
+    const int64_t t_pairs = (total + sort_tile_items(pair64) - 1) / sort_tile_items(pair64);
+    const int64_t t_bins = (st.isect_cap + sort_tile_items(false) - 1) / sort_tile_items(false);
+    const size_t need = sizeof(unsigned long long) * 256 * std::max(t_pairs, t_bins);
+    if (st.status.bytes < need) {
+      SPLAX_CUDA(cudaStreamSynchronize(stream));
+      cudaError_t e = buf_reserve(st.status, need);
+      if (e != cudaSuccess) {
+        st.drop_entry();
+        return cuda_fail(e, "sort look-back allocation");
+      }
+    }
   }
   st.key_bits = kb;
   out.tbx = tbx;
   out.tby = tby;
   out.num_tiles = static_cast<int32_t>(num_tiles);
   out.key_bits = kb;
+  out.tile_n_bits = tile_n_bits;
+  out.depth_bits = depth_bits;
+  out.depth_mm = depth_mm;
   out.count = count;
   out.bins = static_cast<const int32_t*>(st.tile_bins.p);
   out.records = static_cast<const float4*>(st.records.p);
   out.gids = static_cast<const int32_t*>(st.vals[0].p);
-  out.keys = st.keys[0].p;
+  out.keys = static_cast<const uint32_t*>(st.keys[0].p);
   if (count == 0) {
     st.last_valid = true;
     st.last_gen = st.sort_gen;
@@ -397,6 +434,44 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
     return SPLAX_OK;
   }
 
+  SortScratch ss;
+  ss.hist = static_cast<uint32_t*>(st.hist.p);
+  ss.status = static_cast<unsigned long long*>(st.status.p);
+  ss.status_words = static_cast<int64_t>(st.status.bytes / sizeof(unsigned long long));
+  ss.tile_counters = st.sort_counters();
+  ss.err = st.err_word();
+
+  // 1. pairs in (image, depth key) order
+  PairKeyArgs pa;
+  pa.depths = in.depths;
+  pa.radii = in.radii;
+  pa.depth_mm = depth_mm;
+  pa.n = in.n;
+  pa.total = total;
+  pa.packed = packed;
+  pa.depth_bits = depth_bits;
+  pa.key_shift = key_shift;
+  pa.err = st.err_word();
+  st.timer.begin(kPairKeys, 1, stream);
+  launch_pair_keys(pa, pair64, st.pkeys[0].p, static_cast<int32_t*>(st.pvals[0].p), stream);
+  st.timer.end(stream);
+  ss.keys[0] = st.pkeys[0].p;
+  ss.keys[1] = st.pkeys[1].p;
+  ss.vals[0] = static_cast<int32_t*>(st.pvals[0].p);
+  ss.vals[1] = static_cast<int32_t*>(st.pvals[1].p);
+  const int pair_passes = (pair_bits + 7) / 8;
+  st.timer.begin(kPairSort, total > 1 && pair_passes ? 2 + pair_passes : 0, stream);
+  const int pfin = radix_sort_pairs(ss, pair64, total, pair_bits, stream);
+  st.timer.end(stream);
+  const int32_t* perm = ss.vals[pfin];
+  int32_t* offsets = static_cast<int32_t*>(st.poffs.p);
+  st.timer.begin(kPairScan, 1, stream);
+  launch_sorted_offsets(perm, in.cum, total, offsets,
+                        static_cast<unsigned long long*>(st.scan_status.p), st.scan_ticket(),
+                        st.err_word(), stream);
+  st.timer.end(stream);
+
+  // 2. emission in pair order: (image | tile) keys, flat ids, blend records
   EmitArgs ea;
   ea.xys = in.xys;
   ea.depths = in.depths;
@@ -409,53 +484,49 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
   ea.colors = in.colors;
   ea.color_rows = in.color_rows;
   ea.cum = in.cum;
+  ea.perm = perm;
+  ea.offsets = offsets;
   ea.n = in.n;
   ea.total = total;
   ea.count = count;
   ea.tile_n_bits = tile_n_bits;
-  ea.depth_bits = depth_bits;
   ea.tbx = tbx;
   ea.tby = tby;
-  ea.depth_mm = depth_mm;
-  ea.keys = st.keys[0].p;
+  ea.keys = static_cast<uint32_t*>(st.keys[0].p);
   ea.vals = static_cast<int32_t*>(st.vals[0].p);
   ea.records = in.colors ? static_cast<float4*>(st.records.p) : nullptr;
   ea.err = st.err_word();
   st.timer.begin(kEmit, 1, stream);
-  launch_emit(ea, !packed, stream);
+  launch_emit(ea, stream);
   st.timer.end(stream);
 
-  SortScratch ss;
+  // 3. stable sort of the intersections by (image | tile)
   ss.keys[0] = st.keys[0].p;
   ss.keys[1] = st.keys[1].p;
   ss.vals[0] = static_cast<int32_t*>(st.vals[0].p);
   ss.vals[1] = static_cast<int32_t*>(st.vals[1].p);
-  ss.hist = static_cast<uint32_t*>(st.hist.p);
-  ss.status = static_cast<unsigned long long*>(st.status.p);
-  ss.status_words = static_cast<int64_t>(st.status.bytes / sizeof(unsigned long long));
-  ss.tile_counters = st.sort_counters();
-  ss.err = st.err_word();
-  const int bits = packed ? 31 : 32 + upper;
-  const int passes = (bits + 7) / 8;
-  st.timer.begin(kRadixSort, count > 1 ? 2 + passes : 0, stream);
-  const int fin = radix_sort_pairs(ss, !packed, count, bits, stream);
+  const int passes = (bin_bits + 7) / 8;
+  st.timer.begin(kRadixSort, count > 1 && passes ? 2 + passes : 0, stream);
+  const int fin = radix_sort_pairs(ss, false, count, bin_bits, stream);
   st.timer.end(stream);
   out.gids = ss.vals[fin];
-  out.keys = ss.keys[fin];
+  out.keys = static_cast<const uint32_t*>(ss.keys[fin]);
   st.timer.begin(kTileBins, 1, stream);
-  launch_tile_bins(out.keys, !packed, count, packed ? depth_bits : 32, tile_n_bits,
-                   static_cast<int32_t>(num_tiles), bins_len, static_cast<int32_t*>(st.tile_bins.p),
-                   st.err_word(), stream);
+  launch_tile_bins(out.keys, false, count, 0, tile_n_bits, static_cast<int32_t>(num_tiles),
+                   bins_len, static_cast<int32_t*>(st.tile_bins.p), st.err_word(), stream);
   st.timer.end(stream);
+  SPLAX_CUDA(cudaGetLastError());
   st.units.intersections += count;
-  st.units.key_bytes += count * static_cast<int64_t>(key_size);
+  st.units.key_bytes += count * static_cast<int64_t>(sizeof(uint32_t));
   st.units.sort_passes += count > 1 ? count * passes : 0;
   st.units.bins += bins_len;
+  st.units.pairs_sorted += total;
+  st.units.pair_key_bytes += total * (pair64 ? 8 : 4);
+  st.units.pair_pass_keys += total > 1 ? total * pair_passes : 0;
   st.last_valid = true;
   st.last_gen = st.sort_gen;
   st.last_in = in;
   st.last_out = out;
-  SPLAX_CUDA(cudaGetLastError());
   return SPLAX_OK;
 }
 
@@ -897,16 +968,18 @@ int splax_sort_and_bin(const float* xys, const float* depths, const int32_t* rad
                              sizeof(int2) * static_cast<int64_t>(num_images) * so.num_tiles,
                              cudaMemcpyDeviceToDevice, stream));
   if (sorted_keys && so.count > 0) {
-    // widen to int64 on the host side of the caller's buffer: copy raw, then expand
-    if (so.key_bits == 64) {
-      SPLAX_CUDA(cudaMemcpyAsync(sorted_keys, so.keys, sizeof(int64_t) * so.count,
-                                 cudaMemcpyDeviceToDevice, stream));
-    } else {
-      SPLAX_CUDA(cudaMemcpy2DAsync(sorted_keys, sizeof(int64_t), so.keys, sizeof(int32_t),
-                                   sizeof(int32_t), so.count, cudaMemcpyDeviceToDevice, stream));
-      SPLAX_CUDA(cudaMemset2DAsync(reinterpret_cast<char*>(sorted_keys) + 4, sizeof(int64_t), 0,
-                                   sizeof(int32_t), so.count, stream));
-    }
+    // the reference's own key for each sorted intersection
+    PairKeyArgs pa;
+    pa.depths = depths;
+    pa.radii = radii;
+    pa.depth_mm = so.depth_mm;
+    pa.n = num_gaussians;
+    pa.total = total;
+    pa.packed = so.key_bits == 32;
+    pa.depth_bits = so.depth_bits;
+    pa.key_shift = 0;
+    pa.err = st->err_word();
+    launch_reference_keys(so.keys, so.gids, so.count, pa, sorted_keys, stream);
   }
   *num_intersects = so.count;
   *used_key_bits = so.key_bits;
@@ -1005,9 +1078,13 @@ int splax_profile_report(char* buf, int32_t len) {
   snprintf(tmp, sizeof tmp,
            "\"pixels_fwd\": %lld, \"pixels_bwd\": %lld, \"fwd_evals\": %llu, "
            "\"fwd_contribs\": %llu, \"bwd_evals\": %llu, \"bwd_contribs\": %llu, "
-           "\"sort_reuses\": %lld}}",
+           "\"sort_reuses\": %lld, ",
            (long long)u.pixels_fwd, (long long)u.pixels_bwd, w[0], w[1], w[2], w[3],
            (long long)u.sort_reuses);
+  js += tmp;
+  snprintf(tmp, sizeof tmp,
+           "\"pairs_sorted\": %lld, \"pair_key_bytes\": %lld, \"pair_pass_keys\": %lld}}",
+           (long long)u.pairs_sorted, (long long)u.pair_key_bytes, (long long)u.pair_pass_keys);
   js += tmp;
   if (static_cast<int32_t>(js.size()) + 1 > len) return -SPLAX_ERR_INVALID_ARGUMENT;
   memcpy(buf, js.c_str(), js.size() + 1);

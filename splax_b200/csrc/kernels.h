@@ -69,13 +69,25 @@ struct EmitArgs {
   const float* colors;
   int64_t color_rows;
   const int32_t* cum;
+  const int32_t* perm;     // pairs in (image, depth key) order
+  const int32_t* offsets;  // exclusive scan of their tile counts in that order
   int64_t n, total;
   int64_t count;  // intersections (cum[total-1]); emission never writes past it
-  int32_t tile_n_bits, depth_bits, tbx, tby;
-  const int32_t* depth_mm;  // ordered-int per-image [min, max] (32-bit keys only)
-  void* keys;               // uint32 or uint64 keys
+  int32_t tile_n_bits, tbx, tby;
+  uint32_t* keys;  // (image | tile) bin keys
   int32_t* vals;
-  float4* records;
+  float4* records;  // nullptr: no record packing
+  unsigned* err;
+};
+
+struct PairKeyArgs {
+  const float* depths;
+  const int32_t* radii;
+  const int32_t* depth_mm;  // ordered-int per-image [min, max] of visible depths
+  int64_t n, total;
+  bool packed;         // quantised depth (32-bit reference keys) or float bits (64-bit)
+  int32_t depth_bits;  // packed: the reference's depth field width
+  int32_t key_shift;   // bits below the image id in the pair key
   unsigned* err;
 };
 
@@ -87,7 +99,17 @@ void launch_project_bwd(const ProjectBwdArgs& a, cudaStream_t stream);
 // sort.cu
 void launch_depth_minmax(const float* depths, const int32_t* radii, int64_t total, int64_t n,
                          int32_t B, int32_t* depth_mm, cudaStream_t stream);
-void launch_emit(const EmitArgs& a, bool key64, cudaStream_t stream);
+void launch_depth_span(const int32_t* depth_mm, int32_t B, unsigned* span_out,
+                       cudaStream_t stream);
+void launch_pair_keys(const PairKeyArgs& a, bool key64, void* keys, int32_t* vals,
+                      cudaStream_t stream);
+int64_t sorted_offsets_tiles(int64_t total);
+void launch_sorted_offsets(const int32_t* perm, const int32_t* cum, int64_t total,
+                           int32_t* offsets, unsigned long long* status, int* ticket,
+                           unsigned* err, cudaStream_t stream);
+void launch_emit(const EmitArgs& a, cudaStream_t stream);
+void launch_reference_keys(const uint32_t* bin_keys, const int32_t* gids, int64_t count,
+                           const PairKeyArgs& a, int64_t* out, cudaStream_t stream);
 // Onesweep radix sort of (key, value) pairs over `bits` low key bits, ping-ponging between
 // the two buffers; returns the index (0 or 1) of the buffer holding the result.
 struct SortScratch {

@@ -3,10 +3,12 @@
 //
 //  depth min/max   per-image [dmin, dmax] of visible depths (_sort/_kernels.py:31-73), a
 //                  warp-reduced atomic min/max on order-preserving integers.
-//  emission        the ellipse tile walk once more per visible gaussian (_kernels.py:76-211),
-//                  writing keys and flat ids at the cum offsets, and packing the gaussian's
-//                  blend record (xy, conic, opacity, colour, depth) for the blend kernels.
-//  radix sort      stable LSD onesweep: one upfront histogram pass over all digits, then one
+//  pair order     the B*n pairs sorted stably by (image, depth key), and the exclusive scan
+//                  of their tile counts in that order.
+//  emission        the ellipse tile walk once more per visible pair, in sorted pair order
+//                  (_kernels.py:76-211), writing (image | tile) bin keys and flat ids, and
+//                  packing the pair's blend record (xy, conic, opacity, colour, depth).
+//  radix sort      stable LSD onesweep (used for both sorts): one upfront histogram pass, then one
 //                  kernel per 8-bit digit that ranks keys with warp ballots, resolves the
 //                  tile's global digit offsets by a decoupled look-back (bounded spin) and
 //                  scatters through shared memory so the global writes coalesce per digit.
@@ -75,15 +77,161 @@ depth_minmax_kernel(const float* __restrict__ depths, const int32_t* __restrict_
   }
 }
 
-// ------------------------------------------------------------------ key emission
-template <bool K64>
-__global__ void __launch_bounds__(256) emit_kernel(EmitArgs a) {
+// ------------------------------------------------------------------ depth-first ordering
+// The reference sorts every intersection by the key (image | tile | depth) (_sort/_kernels.py
+// :76-211), stably over emission order (ascending flat id). Within one (image, tile) bin that
+// order is (depth key, flat id). The same order arises from two stable sorts: the B*n pairs by
+// (image, depth key), then -- after emitting each pair's tiles in that order -- the
+// intersections by their (image | tile) field alone. The first sort touches B*n pairs, the
+// second only the image and tile bits, instead of every depth bit of every intersection.
+
+// Largest per-image span of visible depth bit patterns (64-bit key mode): the pair key stores
+// depth bits relative to the image's minimum, which orders positive floats like their values.
+__global__ void depth_span_kernel(const int32_t* mm, int32_t B, unsigned* span_out) {
+  unsigned span = 0;
+  for (int b = threadIdx.x; b < B; b += blockDim.x) {
+    const int32_t lo = mm[2 * b], hi = mm[2 * b + 1];
+    if (lo <= hi) span = max(span, static_cast<unsigned>(hi - lo));
+  }
+  span = __reduce_max_sync(0xffffffffu, span);
+  __shared__ unsigned s_span[32];
+  if ((threadIdx.x & 31) == 0) s_span[threadIdx.x >> 5] = span;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned m = 0;
+    for (int w = 0; w < (blockDim.x + 31) / 32; ++w) m = max(m, s_span[w]);
+    *span_out = m;
+  }
+}
+
+// Pair key (image | depth key) and value (flat id) for every pair.
+//  packed keys: depth key = the reference's quantised depth (_sort/_kernels.py:116-124)
+//  wide keys:   depth key = float bits - the image's minimum visible float bits
+template <typename K>
+__global__ void __launch_bounds__(256)
+pair_key_kernel(PairKeyArgs a, K* keys, int32_t* vals) {
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= a.total) return;
-  if (a.radii[idx] <= 0) return;
   const int64_t bid = idx / a.n;
-  int64_t cur = idx > 0 ? static_cast<int64_t>(static_cast<uint32_t>(a.cum[idx - 1])) : 0;
-  int64_t end = static_cast<int64_t>(static_cast<uint32_t>(a.cum[idx]));
+  uint64_t dk = 0;
+  if (a.radii[idx] > 0) {
+    const float depth = a.depths[idx];
+    if (a.packed) {
+      const float dmin = ordered_to_float(a.depth_mm[2 * bid]);
+      const float drange = ordered_to_float(a.depth_mm[2 * bid + 1]) - dmin;
+      const int32_t qmax = static_cast<int32_t>((1u << a.depth_bits) - 1u);
+      const float maxq = static_cast<float>(qmax);
+      if (drange > 0.0f) {
+        const float f = (depth - dmin) / drange;
+        dk = static_cast<uint64_t>(imin(imax(f2i(f * maxq), 0), qmax));
+      }
+    } else {
+      const int32_t dbits = __float_as_int(depth);
+      // the reference sign-extends a negative depth into the image and tile fields
+      if (dbits < 0) atomicOr(a.err, kErrNegativeDepthKey);
+      dk = static_cast<uint32_t>(dbits - a.depth_mm[2 * bid]);
+    }
+  }
+  keys[idx] = static_cast<K>((static_cast<uint64_t>(bid) << a.key_shift) | dk);
+  vals[idx] = static_cast<int32_t>(idx);
+}
+
+// Exclusive scan of the tile counts in sorted pair order (count = cum[g] - cum[g-1]), one
+// pass with a decoupled look-back (bounded spin); also writes the total to *total_out.
+constexpr int kScanThreads = 256;
+constexpr int kScanItems = 8;
+constexpr unsigned long long kScanAgg = 1ull << 62;
+constexpr unsigned long long kScanInc = 2ull << 62;
+constexpr unsigned long long kScanMask = (1ull << 62) - 1;
+
+__global__ void __launch_bounds__(kScanThreads)
+sorted_offsets_kernel(const int32_t* __restrict__ perm, const int32_t* __restrict__ cum,
+                      int64_t total, int32_t* __restrict__ offsets, unsigned long long* status,
+                      int* ticket, unsigned* err) {
+  __shared__ int s_tile;
+  __shared__ long long s_warp[kScanThreads / 32];
+  __shared__ long long s_prefix;
+  if (threadIdx.x == 0) s_tile = atomicAdd(ticket, 1);
+  __syncthreads();
+  const int64_t tile = s_tile;
+  const int64_t base = tile * kScanThreads * kScanItems + static_cast<int64_t>(threadIdx.x) * kScanItems;
+  long long c[kScanItems];
+  long long tsum = 0;
+#pragma unroll
+  for (int k = 0; k < kScanItems; ++k) {
+    const int64_t i = base + k;
+    long long v = 0;
+    if (i < total) {
+      const int64_t g = perm[i];
+      const long long hi = static_cast<uint32_t>(cum[g]);
+      const long long lo = g > 0 ? static_cast<long long>(static_cast<uint32_t>(cum[g - 1])) : 0;
+      v = hi - lo;
+    }
+    c[k] = v;
+    tsum += v;
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  long long inc = tsum;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const long long o = __shfl_up_sync(0xffffffffu, inc, off);
+    if (lane >= off) inc += o;
+  }
+  if (lane == 31) s_warp[warp] = inc;
+  __syncthreads();
+  long long wpre = 0;
+  for (int w = 0; w < warp; ++w) wpre += s_warp[w];
+  if (threadIdx.x == 0) {
+    long long agg = 0;
+    for (int w = 0; w < kScanThreads / 32; ++w) agg += s_warp[w];
+    long long prefix = 0;
+    if (tile == 0) {
+      st_relaxed(&status[0], kScanInc | static_cast<unsigned long long>(agg));
+    } else {
+      st_relaxed(&status[tile], kScanAgg | static_cast<unsigned long long>(agg));
+      int64_t j = tile - 1;
+      long long spins = 0;
+      while (j >= 0) {
+        const unsigned long long s = ld_relaxed(&status[j]);
+        const unsigned long long flag = s & ~kScanMask;
+        if (flag == 0) {
+          if (++spins > kSpinLimit) {
+            atomicOr(err, kErrLookbackTimeout);
+            break;
+          }
+          continue;
+        }
+        prefix += static_cast<long long>(s & kScanMask);
+        if (flag == kScanInc) break;
+        --j;
+      }
+      st_relaxed(&status[tile], kScanInc | static_cast<unsigned long long>(prefix + agg));
+    }
+    s_prefix = prefix;
+  }
+  __syncthreads();
+  long long run = s_prefix + wpre + inc - tsum;
+#pragma unroll
+  for (int k = 0; k < kScanItems; ++k) {
+    const int64_t i = base + k;
+    if (i < total) offsets[i] = static_cast<int32_t>(run);
+    run += c[k];
+  }
+}
+
+// Emission in sorted pair order: the ellipse walk once more per visible pair (the count
+// projection made), writing the (image | tile) bin key and the flat id at the pair's offset,
+// and packing the pair's blend record.
+__global__ void __launch_bounds__(256) emit_sorted_kernel(EmitArgs a) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= a.total) return;
+  const int64_t idx = a.perm[i];
+  if (idx < 0 || idx >= a.total || a.radii[idx] <= 0) return;
+  const int64_t bid = idx / a.n;
+  const int64_t hi = static_cast<uint32_t>(a.cum[idx]);
+  const int64_t lo = idx > 0 ? static_cast<int64_t>(static_cast<uint32_t>(a.cum[idx - 1])) : 0;
+  int64_t cur = a.offsets[i];
+  int64_t end = cur + (hi - lo);
   if (end > a.count || cur > end) {  // cum_tiles_hit does not describe this geometry
     atomicOr(a.err, kErrEmitCount);
     end = min(end, a.count);
@@ -91,7 +239,6 @@ __global__ void __launch_bounds__(256) emit_kernel(EmitArgs a) {
   }
   const float x = a.xys[2 * idx], y = a.xys[2 * idx + 1];
   const float ca = a.conics[3 * idx], cb = a.conics[3 * idx + 1], cc = a.conics[3 * idx + 2];
-  const float depth = a.depths[idx];
   if (a.records) {
     const int64_t ci = idx % a.color_rows;
     const float op = a.opacities[idx % a.opac_rows];
@@ -99,26 +246,9 @@ __global__ void __launch_bounds__(256) emit_kernel(EmitArgs a) {
     // conic pre-scaled for the blends' base-2 exponent: q = -log2(e)/2 * (a, 2b, c)
     rec[0] = make_float4(x, y, -kHalfLog2e * ca, -kLog2e * cb);
     rec[1] = make_float4(-kHalfLog2e * cc, op, a.colors[3 * ci], a.colors[3 * ci + 1]);
-    rec[2] = make_float4(a.colors[3 * ci + 2], depth, 0.0f, 0.0f);
+    rec[2] = make_float4(a.colors[3 * ci + 2], a.depths[idx], 0.0f, 0.0f);
   }
-  uint64_t enc;
-  uint32_t depth_q = 0;
-  if constexpr (K64) {
-    const int32_t dbits = __float_as_int(depth);
-    // the reference sign-extends a negative depth into the image and tile fields
-    if (dbits < 0) atomicOr(a.err, kErrNegativeDepthKey);
-    enc = (static_cast<uint64_t>(bid) << (32 + a.tile_n_bits)) | static_cast<uint32_t>(dbits);
-  } else {
-    const float dmin = ordered_to_float(a.depth_mm[2 * bid]);
-    const float drange = ordered_to_float(a.depth_mm[2 * bid + 1]) - dmin;
-    const int32_t qmax = static_cast<int32_t>((1u << a.depth_bits) - 1u);
-    const float maxq = static_cast<float>(qmax);
-    if (drange > 0.0f) {
-      const float f = (depth - dmin) / drange;
-      depth_q = static_cast<uint32_t>(imin(imax(f2i(f * maxq), 0), qmax));
-    }
-    enc = static_cast<uint64_t>(bid) << (a.depth_bits + a.tile_n_bits);
-  }
+  const uint32_t img_enc = static_cast<uint32_t>(bid) << a.tile_n_bits;
   const float t = iso_level(a.map_opacities[idx % a.map_opac_rows]);
   Ellipse e;
   ellipse_init(ca, cb, cc, t, x, y, a.tbx, a.tby, e);
@@ -134,20 +264,42 @@ __global__ void __launch_bounds__(256) emit_kernel(EmitArgs a) {
           bad = true;
           break;
         }
-        const uint64_t tile =
-            static_cast<uint64_t>(e.isY ? u * a.tbx + v : v * a.tbx + u);
-        if constexpr (K64) {
-          reinterpret_cast<uint64_t*>(a.keys)[cur] = enc | (tile << 32);
-        } else {
-          reinterpret_cast<uint32_t*>(a.keys)[cur] =
-              static_cast<uint32_t>(enc | (tile << a.depth_bits) | depth_q);
-        }
+        const uint32_t tile = static_cast<uint32_t>(e.isY ? u * a.tbx + v : v * a.tbx + u);
+        a.keys[cur] = img_enc | tile;
         a.vals[cur] = static_cast<int32_t>(idx);
         ++cur;
       }
     }
   }
   if (bad || cur != end) atomicOr(a.err, kErrEmitCount);
+}
+
+// The reference's own sort keys for the sorted order (for the parity entry point only):
+// packed (bin << depth_bits) | quantised depth, wide (bin << 32) | depth bits.
+__global__ void reference_keys_kernel(const uint32_t* __restrict__ bin_keys,
+                                      const int32_t* __restrict__ gids, int64_t count,
+                                      PairKeyArgs a, int64_t* out) {
+  const int64_t p = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (p >= count) return;
+  const int64_t idx = gids[p];
+  const int64_t bid = idx / a.n;
+  const float depth = a.depths[idx];
+  uint64_t key;
+  if (a.packed) {
+    uint32_t q = 0;
+    const float dmin = ordered_to_float(a.depth_mm[2 * bid]);
+    const float drange = ordered_to_float(a.depth_mm[2 * bid + 1]) - dmin;
+    const int32_t qmax = static_cast<int32_t>((1u << a.depth_bits) - 1u);
+    if (drange > 0.0f) {
+      const float f = (depth - dmin) / drange;
+      q = static_cast<uint32_t>(imin(imax(f2i(f * static_cast<float>(qmax)), 0), qmax));
+    }
+    key = (static_cast<uint64_t>(bin_keys[p]) << a.depth_bits) | q;
+  } else {
+    key = (static_cast<uint64_t>(bin_keys[p]) << 32) |
+          static_cast<uint64_t>(static_cast<int64_t>(__float_as_int(depth)));
+  }
+  out[p] = static_cast<int64_t>(key);
 }
 
 // ------------------------------------------------------------------ onesweep radix sort
@@ -399,13 +551,50 @@ void launch_depth_minmax(const float* depths, const int32_t* radii, int64_t tota
                                                                                   depth_mm);
 }
 
-void launch_emit(const EmitArgs& a, bool key64, cudaStream_t stream) {
+void launch_depth_span(const int32_t* depth_mm, int32_t B, unsigned* span_out,
+                       cudaStream_t stream) {
+  depth_span_kernel<<<1, 256, 0, stream>>>(depth_mm, B, span_out);
+}
+
+void launch_pair_keys(const PairKeyArgs& a, bool key64, void* keys, int32_t* vals,
+                      cudaStream_t stream) {
   const int64_t blocks = (a.total + 255) / 256;
   if (blocks == 0) return;
   if (key64)
-    emit_kernel<true><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
+    pair_key_kernel<uint64_t><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+        a, static_cast<uint64_t*>(keys), vals);
   else
-    emit_kernel<false><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
+    pair_key_kernel<uint32_t><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+        a, static_cast<uint32_t*>(keys), vals);
+}
+
+int64_t sorted_offsets_tiles(int64_t total) {
+  return (total + kScanThreads * kScanItems - 1) / (kScanThreads * kScanItems);
+}
+
+void launch_sorted_offsets(const int32_t* perm, const int32_t* cum, int64_t total,
+                           int32_t* offsets, unsigned long long* status, int* ticket,
+                           unsigned* err, cudaStream_t stream) {
+  const int64_t tiles = sorted_offsets_tiles(total);
+  if (tiles == 0) return;
+  cudaMemsetAsync(ticket, 0, sizeof(int), stream);
+  cudaMemsetAsync(status, 0, sizeof(unsigned long long) * tiles, stream);
+  sorted_offsets_kernel<<<static_cast<unsigned>(tiles), kScanThreads, 0, stream>>>(
+      perm, cum, total, offsets, status, ticket, err);
+}
+
+void launch_emit(const EmitArgs& a, cudaStream_t stream) {
+  const int64_t blocks = (a.total + 255) / 256;
+  if (blocks == 0) return;
+  emit_sorted_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
+}
+
+void launch_reference_keys(const uint32_t* bin_keys, const int32_t* gids, int64_t count,
+                           const PairKeyArgs& a, int64_t* out, cudaStream_t stream) {
+  const int64_t blocks = (count + 255) / 256;
+  if (blocks == 0) return;
+  reference_keys_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(bin_keys, gids,
+                                                                            count, a, out);
 }
 
 int sort_tile_items(bool key64) { return kSortThreads * (key64 ? kItems64 : kItems32); }
