@@ -195,6 +195,7 @@ struct DeviceState {
   int64_t isect_cap = 0;
   DevBuf keys[2], vals[2], records, tile_bins, depth_mm, status;
   DevBuf pkeys[2], pvals[2], poffs, scan_status;  // depth-order sort of the B*n pairs
+  DevBuf walk, counts;                             // per-pair walk records and tile counts
   // signature-independent pieces
   DevBuf misc;  // [0] error word, [2..9] sort tile counters, [10] depth span, [11] scan ticket
   DevBuf hist;        // radix histograms and offsets
@@ -227,7 +228,8 @@ struct DeviceState {
     size_t s = 0;
     for (const DevBuf* b : {&keys[0], &keys[1], &vals[0], &vals[1], &records, &tile_bins,
                             &depth_mm, &status, &pkeys[0], &pkeys[1], &pvals[0], &pvals[1],
-                            &poffs, &scan_status, &misc, &hist, &proj_status})
+                            &poffs, &scan_status, &walk, &counts, &misc, &hist,
+                            &proj_status})
       s += b->bytes;
     return s;
   }
@@ -236,7 +238,8 @@ struct DeviceState {
     last_valid = false;
     ++sort_gen;
     for (DevBuf* b : {&keys[0], &keys[1], &vals[0], &vals[1], &records, &tile_bins, &depth_mm,
-                      &status, &pkeys[0], &pkeys[1], &pvals[0], &pvals[1], &poffs, &scan_status})
+                      &status, &pkeys[0], &pkeys[1], &pvals[0], &pvals[1], &poffs, &scan_status,
+                      &walk, &counts})
       buf_free(*b);
     sig_B = sig_n = sig_T = -1;
     key_bits = 0;
@@ -346,7 +349,9 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
         (e = buf_reserve(st.pvals[0], sizeof(int32_t) * total)) != cudaSuccess ||
         (e = buf_reserve(st.pvals[1], sizeof(int32_t) * total)) != cudaSuccess ||
         (e = buf_reserve(st.poffs, sizeof(int32_t) * total)) != cudaSuccess ||
-        (e = buf_reserve(st.scan_status, sizeof(unsigned long long) * ptiles)) != cudaSuccess) {
+        (e = buf_reserve(st.scan_status, sizeof(unsigned long long) * ptiles)) != cudaSuccess ||
+        (e = buf_reserve(st.walk, 2 * sizeof(float4) * total)) != cudaSuccess ||
+        (e = buf_reserve(st.counts, sizeof(int32_t) * total)) != cudaSuccess) {
       st.drop_entry();
       return cuda_fail(e, "scratch allocation (tile bins, depth ranges, records, pair order)");
     }
@@ -452,6 +457,18 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
   pa.depth_bits = depth_bits;
   pa.key_shift = key_shift;
   pa.err = st.err_word();
+  pa.xys = in.xys;
+  pa.conics = in.conics;
+  pa.cum = in.cum;
+  pa.map_opacities = in.map_opacities;
+  pa.map_opac_rows = in.map_rows;
+  pa.opacities = in.opacities;
+  pa.opac_rows = in.opac_rows;
+  pa.colors = in.colors;
+  pa.color_rows = in.color_rows;
+  pa.counts = static_cast<int32_t*>(st.counts.p);
+  pa.walk = static_cast<float4*>(st.walk.p);
+  pa.records = in.colors ? static_cast<float4*>(st.records.p) : nullptr;
   st.timer.begin(kPairKeys, 1, stream);
   launch_pair_keys(pa, pair64, st.pkeys[0].p, static_cast<int32_t*>(st.pvals[0].p), stream);
   st.timer.end(stream);
@@ -466,27 +483,17 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
   const int32_t* perm = ss.vals[pfin];
   int32_t* offsets = static_cast<int32_t*>(st.poffs.p);
   st.timer.begin(kPairScan, 1, stream);
-  launch_sorted_offsets(perm, in.cum, total, offsets,
+  launch_sorted_offsets(perm, static_cast<const int32_t*>(st.counts.p), total, offsets,
                         static_cast<unsigned long long*>(st.scan_status.p), st.scan_ticket(),
                         st.err_word(), stream);
   st.timer.end(stream);
 
   // 2. emission in pair order: (image | tile) keys, flat ids, blend records
   EmitArgs ea;
-  ea.xys = in.xys;
-  ea.depths = in.depths;
-  ea.radii = in.radii;
-  ea.conics = in.conics;
-  ea.map_opacities = in.map_opacities;
-  ea.map_opac_rows = in.map_rows;
-  ea.opacities = in.opacities;
-  ea.opac_rows = in.opac_rows;
-  ea.colors = in.colors;
-  ea.color_rows = in.color_rows;
-  ea.cum = in.cum;
   ea.perm = perm;
   ea.offsets = offsets;
-  ea.n = in.n;
+  ea.counts = static_cast<const int32_t*>(st.counts.p);
+  ea.walk = static_cast<const float4*>(st.walk.p);
   ea.total = total;
   ea.count = count;
   ea.tile_n_bits = tile_n_bits;
@@ -494,7 +501,6 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
   ea.tby = tby;
   ea.keys = static_cast<uint32_t*>(st.keys[0].p);
   ea.vals = static_cast<int32_t*>(st.vals[0].p);
-  ea.records = in.colors ? static_cast<float4*>(st.records.p) : nullptr;
   ea.err = st.err_word();
   st.timer.begin(kEmit, 1, stream);
   launch_emit(ea, stream);
@@ -979,6 +985,8 @@ int splax_sort_and_bin(const float* xys, const float* depths, const int32_t* rad
     pa.depth_bits = so.depth_bits;
     pa.key_shift = 0;
     pa.err = st->err_word();
+    pa.walk = nullptr;
+    pa.records = nullptr;
     launch_reference_keys(so.keys, so.gids, so.count, pa, sorted_keys, stream);
   }
   *num_intersects = so.count;

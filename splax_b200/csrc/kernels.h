@@ -53,30 +53,21 @@ struct ProjectBwdArgs {
 };
 
 // Per-gaussian record staged by the blend kernels: 3 x float4 =
-// (x, y, qa, qb), (qc, opacity, r, g), (b, depth, 0, 0), with the conic pre-scaled for a
-// base-2 exponent: (qa, qb, qc) = -log2(e)/2 * (a, 2b, c).
+// (x, y, qa, qb), (qc, opacity, r, g), (b, depth, ex, ey), with the conic pre-scaled for a
+// base-2 exponent, (qa, qb, qc) = -log2(e)/2 * (a, 2b, c), and (ex, ey) the half-extents of
+// the ellipse outside which alpha < 1/255.
 constexpr int kRecordFloat4 = 3;
 
 struct EmitArgs {
-  const float* xys;
-  const float* depths;
-  const int32_t* radii;
-  const float* conics;
-  const float* map_opacities;
-  int64_t map_opac_rows;
-  const float* opacities;  // blend opacities, packed into the record
-  int64_t opac_rows;
-  const float* colors;
-  int64_t color_rows;
-  const int32_t* cum;
   const int32_t* perm;     // pairs in (image, depth key) order
   const int32_t* offsets;  // exclusive scan of their tile counts in that order
-  int64_t n, total;
+  const int32_t* counts;   // tile count per pair (flat order)
+  const float4* walk;      // walk record per pair (flat order)
+  int64_t total;
   int64_t count;  // intersections (cum[total-1]); emission never writes past it
   int32_t tile_n_bits, tbx, tby;
   uint32_t* keys;  // (image | tile) bin keys
   int32_t* vals;
-  float4* records;  // nullptr: no record packing
   unsigned* err;
 };
 
@@ -89,6 +80,19 @@ struct PairKeyArgs {
   int32_t depth_bits;  // packed: the reference's depth field width
   int32_t key_shift;   // bits below the image id in the pair key
   unsigned* err;
+  // per-pair records (flat order); walk == nullptr skips them
+  const float* xys;
+  const float* conics;
+  const int32_t* cum;
+  const float* map_opacities;
+  int64_t map_opac_rows;
+  const float* opacities;
+  int64_t opac_rows;
+  const float* colors;
+  int64_t color_rows;
+  int32_t* counts;
+  float4* walk;     // (x, y, a, b), (c, iso level, image id bits, count bits)
+  float4* records;  // blend records, nullptr without colours
 };
 
 void launch_project_fwd(const ProjectArgs& a, unsigned long long* status, int* ticket,
@@ -104,7 +108,7 @@ void launch_depth_span(const int32_t* depth_mm, int32_t B, unsigned* span_out,
 void launch_pair_keys(const PairKeyArgs& a, bool key64, void* keys, int32_t* vals,
                       cudaStream_t stream);
 int64_t sorted_offsets_tiles(int64_t total);
-void launch_sorted_offsets(const int32_t* perm, const int32_t* cum, int64_t total,
+void launch_sorted_offsets(const int32_t* perm, const int32_t* counts, int64_t total,
                            int32_t* offsets, unsigned long long* status, int* ticket,
                            unsigned* err, cudaStream_t stream);
 void launch_emit(const EmitArgs& a, cudaStream_t stream);

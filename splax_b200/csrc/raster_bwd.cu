@@ -2,8 +2,9 @@
 // (splax/_rasterize/_kernels.py:530-794, 935-1209) with _blend_color_vjp / _blend_depth_vjp
 // (:1212-1302).
 //
-// Recompute-style: one 128-thread CTA per (output image, tile); each thread owns two pixels of
-// one column (rows li and li + 8). The walk runs back to front from the block's largest
+// Recompute-style: one 128-thread CTA per (output image, tile); each warp owns a 16x4 block and
+// each thread two vertically adjacent pixels. A warp skips every gaussian whose alpha >= 1/255
+// ellipse misses its block (those evaluations are all rejected). The walk runs back to front from the block's largest
 // final_idx over batches of 256 records staged in shared memory (plus the flat ids that
 // address the gradients). Each pixel rebuilds T by dividing out (1 - alpha), and only entries
 // at or below its own final_idx count. All lanes of a warp visit the same entry together, so
@@ -24,47 +25,47 @@ constexpr float kLn2 = 0.693147180559945f;
 
 struct BwdPixel {
   int32_t bin_final;
-  float T, t_final, vo0, vo1, vo2, vod, bgdot;
-  float buf0 = 0.0f, buf1 = 0.0f, buf2 = 0.0f, dbuf = 0.0f;
+  float T, vo0, vo1, vo2, vod;
+  float tb;            // t_final * (background . v_out): the background's share of v_alpha
+  float bufdot = 0.0f; // (colour, depth) accumulated behind this gaussian, dotted with v_out
 };
 
-template <bool DEPTH, int K>
-__device__ __forceinline__ bool vjp_one(BwdPixel& s, int32_t idx, float p, float dx, float dy,
-                                        float qa, float qb, float qc, float opac, float r,
-                                        float g, float b, float depth, float (&v)[K]) {
+// Accumulators of one thread for the current gaussian, over its two pixels:
+// [0..2] colour, [3] sum v_sigma, [4] sum v_sigma dy, [5] sum v_sigma dy^2, [6] opacity,
+// [7] depth. The xy and conic cotangents are formed from these once per thread.
+//
+// _blend_color_vjp (splax/_rasterize/_kernels.py:1212-1254) restated with the colour buffer
+// kept as its dot product with v_out: v_alpha = T (c . v_out) - ra (buf . v_out + t_final
+// bg . v_out), and buf . v_out grows by (c . v_out) fac.
+template <bool DEPTH>
+__device__ __forceinline__ bool vjp_one(BwdPixel& s, int32_t idx, float p, float dy, float opac,
+                                        float r, float g, float b, float depth, float* acc) {
   if (idx > s.bin_final || p > 0.0f) return false;
   const float vis = ex2_approx(p);
   const float ov = opac * vis;
   const float alpha = fminf(kAlphaMax, ov);
   if (alpha < kAlphaThreshold) return false;
-  const float ra = 1.0f / (1.0f - alpha);
+  const float ra = __fdividef(1.0f, 1.0f - alpha);
   s.T = s.T * ra;
   const float fac = alpha * s.T;
-  v[0] += s.vo0 * fac;
-  v[1] += s.vo1 * fac;
-  v[2] += s.vo2 * fac;
-  float v_alpha = (r * s.T - s.buf0 * ra) * s.vo0 + (g * s.T - s.buf1 * ra) * s.vo1 +
-                  (b * s.T - s.buf2 * ra) * s.vo2 - s.t_final * ra * s.bgdot;
-  s.buf0 += r * fac;
-  s.buf1 += g * fac;
-  s.buf2 += b * fac;
+  acc[0] += s.vo0 * fac;
+  acc[1] += s.vo1 * fac;
+  acc[2] += s.vo2 * fac;
+  float cv = r * s.vo0 + g * s.vo1 + b * s.vo2;
   if constexpr (DEPTH) {
-    v_alpha += (depth * s.T - s.dbuf * ra) * s.vod;
-    s.dbuf += depth * fac;
-    v[9] += s.vod * fac;
+    cv += depth * s.vod;
+    acc[7] += s.vod * fac;
   }
-  if (ov <= kAlphaMax) {
-    const float v_sigma = -ov * v_alpha;
-    const float hv = 0.5f * v_sigma;
-    v[3] += hv * dx * dx;
-    v[4] += v_sigma * dx * dy;
-    v[5] += hv * dy * dy;
-    // (a dx + b dy, b dx + c dy) = -ln2 * (2 qa dx + qb dy, qb dx + 2 qc dy)
-    const float ks = -kLn2 * v_sigma;
-    v[6] += ks * fmaf(2.0f * qa, dx, qb * dy);
-    v[7] += ks * fmaf(2.0f * qc, dy, qb * dx);
-    v[8] += vis * v_alpha;
-  }
+  const float v_alpha = s.T * cv - ra * (s.bufdot + s.tb);
+  s.bufdot += cv * fac;
+  // where the 0.999 clamp is active alpha is constant: no sigma or opacity cotangent
+  const bool live = ov <= kAlphaMax;
+  const float vs = live ? -ov * v_alpha : 0.0f;
+  acc[6] += live ? vis * v_alpha : 0.0f;
+  acc[3] += vs;
+  const float vsy = vs * dy;
+  acc[4] += vsy;
+  acc[5] += vsy * dy;
   return true;
 }
 
@@ -75,7 +76,7 @@ raster_bwd_kernel(RasterBwdArgs a) {
   unsigned long long evals = 0, contribs = 0;
   __shared__ float4 s_r0[kBlockSize];
   __shared__ float4 s_r1[kBlockSize];
-  __shared__ float2 s_r2[kBlockSize];
+  __shared__ float4 s_r2[kBlockSize];
   __shared__ int32_t s_id[kBlockSize];
   __shared__ int32_t s_wmax[kBwdThreads / 32];
 
@@ -91,26 +92,27 @@ raster_bwd_kernel(RasterBwdArgs a) {
 
   const int tr = threadIdx.x, lane = tr & 31, warp = tr >> 5;
   const int32_t tile_x = tile_local % a.tbx, tile_y = tile_local / a.tbx;
-  const int32_t j = tile_x * kBlockWidth + (tr & 15);
-  const int32_t i0 = tile_y * kBlockWidth + (tr >> 4);
+  const int32_t j = tile_x * kBlockWidth + (lane & 15);
+  const int32_t i0 = tile_y * kBlockWidth + 4 * warp + 2 * (lane >> 4);
   const float px = static_cast<float>(j) + 0.5f;
   const float py0 = static_cast<float>(i0) + 0.5f;
+  const float wcx = static_cast<float>(tile_x * kBlockWidth) + 8.0f;
+  const float wcy = static_cast<float>(tile_y * kBlockWidth + 4 * warp) + 2.0f;
 
   BwdPixel px_s[2];
   const float* bg = a.background + 3 * (a.sel_bg ? image_id : 0);
 #pragma unroll
   for (int k = 0; k < 2; ++k) {
     BwdPixel& s = px_s[k];
-    const int32_t i = i0 + 8 * k;
+    const int32_t i = i0 + k;
     s.bin_final = range_start - 1;
     s.T = 1.0f;
-    s.t_final = 1.0f;
-    s.vo0 = s.vo1 = s.vo2 = s.vod = s.bgdot = 0.0f;
+    s.vo0 = s.vo1 = s.vo2 = s.vod = s.tb = 0.0f;
     if (i < a.img_h && j < a.img_w) {
       const int64_t fpix = (geom_image * a.img_h + i) * static_cast<int64_t>(a.img_w) + j;
       s.bin_final = min(a.final_idx[fpix], range_end - 1);
-      s.t_final = a.final_Ts[fpix];
-      s.T = s.t_final;
+      const float t_final = a.final_Ts[fpix];
+      s.T = t_final;
       const int64_t vrow = (image_id * a.img_h + i) % a.vout_rows;
       const float* vo = a.v_out_img + 3 * (vrow * a.img_w + j);
       s.vo0 = vo[0];
@@ -120,7 +122,7 @@ raster_bwd_kernel(RasterBwdArgs a) {
         const int64_t drow = (image_id * a.img_h + i) % a.vdepth_rows;
         s.vod = a.v_out_depth[drow * a.img_w + j];
       }
-      s.bgdot = bg[0] * s.vo0 + bg[1] * s.vo1 + bg[2] * s.vo2;
+      s.tb = t_final * (bg[0] * s.vo0 + bg[1] * s.vo1 + bg[2] * s.vo2);
     }
   }
 
@@ -164,13 +166,12 @@ raster_bwd_kernel(RasterBwdArgs a) {
           const float4* rec = a.records + kRecordFloat4 * static_cast<int64_t>(g);
           s_r0[slot] = rec[0];
           s_r1[slot] = rec[1];
-          const float4 r2 = rec[2];
-          s_r2[slot] = make_float2(r2.x, r2.y);
+          s_r2[slot] = rec[2];
           s_id[slot] = g;
         } else {  // only after a reported emission error: a transparent record, id 0
           s_r0[slot] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
           s_r1[slot] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-          s_r2[slot] = make_float2(0.0f, 0.0f);
+          s_r2[slot] = make_float4(0.0f, 0.0f, -1.0e30f, -1.0e30f);
           s_id[slot] = 0;
         }
       }
@@ -182,23 +183,37 @@ raster_bwd_kernel(RasterBwdArgs a) {
     for (int32_t t = t_begin; t < batch_size; ++t) {
       const int32_t idx = batch_end - t;
       const float4 r0 = s_r0[t];
+      const float4 r2 = s_r2[t];
+      if constexpr (COUNT) evals += (idx <= px_s[0].bin_final) + (idx <= px_s[1].bin_final);
+      if (fabsf(r0.x - wcx) > r2.z + 7.5f || fabsf(r0.y - wcy) > r2.w + 1.5f) continue;
       const float4 r1 = s_r1[t];
-      const float2 r2 = s_r2[t];
       const float dx = r0.x - px;
-      const float dy0 = r0.y - py0, dy1 = dy0 - 8.0f;
+      const float dy0 = r0.y - py0, dy1 = dy0 - 1.0f;
       const float qxx = r0.z * dx * dx, qbx = r0.w * dx;
       const float p0 = fmaf(fmaf(r1.x, dy0, qbx), dy0, qxx);
       const float p1 = fmaf(fmaf(r1.x, dy1, qbx), dy1, qxx);
-      float v[K];
+      float acc[8];
 #pragma unroll
-      for (int k = 0; k < K; ++k) v[k] = 0.0f;
-      if constexpr (COUNT) evals += (idx <= px_s[0].bin_final) + (idx <= px_s[1].bin_final);
-      const bool c0 = vjp_one<DEPTH, K>(px_s[0], idx, p0, dx, dy0, r0.z, r0.w, r1.x, r1.y, r1.z,
-                                        r1.w, r2.x, r2.y, v);
-      const bool c1 = vjp_one<DEPTH, K>(px_s[1], idx, p1, dx, dy1, r0.z, r0.w, r1.x, r1.y, r1.z,
-                                        r1.w, r2.x, r2.y, v);
+      for (int k = 0; k < 8; ++k) acc[k] = 0.0f;
+      const bool c0 = vjp_one<DEPTH>(px_s[0], idx, p0, dy0, r1.y, r1.z, r1.w, r2.x, r2.y, acc);
+      const bool c1 = vjp_one<DEPTH>(px_s[1], idx, p1, dy1, r1.y, r1.z, r1.w, r2.x, r2.y, acc);
       if constexpr (COUNT) contribs += c0 + c1;
       if (__ballot_sync(0xffffffffu, c0 || c1) == 0u) continue;
+      // per-thread cotangents: sum_px v_sigma (dx, dy) and the second moments give the conic
+      // and xy terms; (a, b, c) = -ln2 (2 qa, qb, 2 qc) recovers the unscaled conic
+      const float sx = acc[3] * dx, sy = acc[4];
+      const float a2 = -2.0f * kLn2 * r0.z, bq = -kLn2 * r0.w, c2 = -2.0f * kLn2 * r1.x;
+      float v[K];
+      v[0] = acc[0];
+      v[1] = acc[1];
+      v[2] = acc[2];
+      v[3] = 0.5f * sx * dx;
+      v[4] = sy * dx;
+      v[5] = 0.5f * acc[5];
+      v[6] = fmaf(a2, sx, bq * sy);
+      v[7] = fmaf(bq, sx, c2 * sy);
+      v[8] = acc[6];
+      if constexpr (DEPTH) v[9] = acc[7];
       warp_reduce_scatter<K>(v, lane);
       if (my_base != nullptr && v[0] != 0.0f) {
         const int64_t og = og_base + s_id[t];

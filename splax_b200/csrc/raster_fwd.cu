@@ -1,9 +1,10 @@
 // Forward blend: _rasterize_kernel and _rasterize_depth_kernel
 // (splax/_rasterize/_kernels.py:102-205, 277-380).
 //
-// One 128-thread CTA per (image, 16x16 tile); each thread owns two pixels of one column,
-// rows li and li + 8, so every shared-memory record read and the x-terms of the Gaussian
-// exponent serve two evaluations. The tile's sorted list is walked in batches of 256: the CTA
+// One 128-thread CTA per (image, 16x16 tile); each warp owns a 16x4 block of the tile and each
+// thread two vertically adjacent pixels, so every shared-memory record read and the x-terms of
+// the Gaussian exponent serve two evaluations. The tile's sorted list is walked in batches of
+// 256: the CTA
 // gathers the packed 48-byte records (three 16-byte loads each, written by the emission pass)
 // into shared memory, then blends the batch front to back from shared memory with broadcast
 // reads. Records carry the conic pre-scaled by -log2(e)/2, so the exponent is a quadratic form
@@ -32,7 +33,6 @@ __device__ __forceinline__ void blend_one(PixelState& s, float p, float opac, fl
                                           unsigned long long& evals,
                                           unsigned long long& contribs) {
   if (s.done) return;
-  if constexpr (COUNT) ++evals;
   const float alpha = fminf(kAlphaMax, opac * ex2_approx(p));
   if (p > 0.0f || alpha < kAlphaThreshold) return;
   const float next_T = s.T * (1.0f - alpha);
@@ -61,9 +61,9 @@ raster_fwd_kernel(RasterFwdArgs a) {
   const int64_t image_id = tile_g / a.num_tiles;
   const int32_t tile_local = static_cast<int32_t>(tile_g % a.num_tiles);
   const int32_t tile_x = tile_local % a.tbx, tile_y = tile_local / a.tbx;
-  const int tr = threadIdx.x;
-  const int32_t j = tile_x * kBlockWidth + (tr & 15);
-  const int32_t i0 = tile_y * kBlockWidth + (tr >> 4), i1 = i0 + 8;
+  const int tr = threadIdx.x, lane = tr & 31, warp = tr >> 5;
+  const int32_t j = tile_x * kBlockWidth + (lane & 15);
+  const int32_t i0 = tile_y * kBlockWidth + 4 * warp + 2 * (lane >> 4), i1 = i0 + 1;
   const float px = static_cast<float>(j) + 0.5f;
   const float py0 = static_cast<float>(i0) + 0.5f;
   const bool inside0 = i0 < a.img_h && j < a.img_w;
@@ -104,8 +104,9 @@ raster_fwd_kernel(RasterFwdArgs a) {
         const float4 r0 = s_r0[t];  // x, y, qa, qb  (q = -log2(e)/2 * (a, 2b, c))
         const float4 r1 = s_r1[t];  // qc, opacity, r, g
         const float2 r2 = s_r2[t];  // b, depth
+        if constexpr (COUNT) evals += !s0.done + !s1.done;
         const float dx = r0.x - px;
-        const float dy0 = r0.y - py0, dy1 = dy0 - 8.0f;
+        const float dy0 = r0.y - py0, dy1 = dy0 - 1.0f;
         const float qxx = r0.z * dx * dx, qbx = r0.w * dx;
         const float p0 = fmaf(fmaf(r1.x, dy0, qbx), dy0, qxx);
         const float p1 = fmaf(fmaf(r1.x, dy1, qbx), dy1, qxx);
@@ -130,7 +131,7 @@ raster_fwd_kernel(RasterFwdArgs a) {
   for (int k = 0; k < 2; ++k) {
     const PixelState& s = k ? s1 : s0;
     if (!(k ? inside1 : inside0)) continue;
-    const int32_t i = k ? i1 : i0;
+    const int32_t i = k ? i1 : i0;  // rows i0 and i0 + 1
     const int64_t pix = (image_id * a.img_h + i) * static_cast<int64_t>(a.img_w) + j;
     a.final_Ts[pix] = s.T;
     a.final_idx[pix] = s.cur_idx;

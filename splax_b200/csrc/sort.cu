@@ -104,18 +104,21 @@ __global__ void depth_span_kernel(const int32_t* mm, int32_t B, unsigned* span_o
   }
 }
 
-// Pair key (image | depth key) and value (flat id) for every pair.
-//  packed keys: depth key = the reference's quantised depth (_sort/_kernels.py:116-124)
-//  wide keys:   depth key = float bits - the image's minimum visible float bits
+// Per pair, in flat order (coalesced): the pair key (image | depth key) and value (flat id),
+// the pair's tile count, its 32-byte walk record for the emission, and (when blending) its
+// 48-byte blend record. Depth keys:
+//  packed keys: the reference's quantised depth (_sort/_kernels.py:116-124)
+//  wide keys:   float bits - the image's minimum visible float bits (orders like the value)
 template <typename K>
 __global__ void __launch_bounds__(256)
-pair_key_kernel(PairKeyArgs a, K* keys, int32_t* vals) {
+pair_prep_kernel(PairKeyArgs a, K* keys, int32_t* vals) {
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= a.total) return;
   const int64_t bid = idx / a.n;
+  const bool live = a.radii[idx] > 0;
   uint64_t dk = 0;
-  if (a.radii[idx] > 0) {
-    const float depth = a.depths[idx];
+  const float depth = a.depths[idx];
+  if (live) {
     if (a.packed) {
       const float dmin = ordered_to_float(a.depth_mm[2 * bid]);
       const float drange = ordered_to_float(a.depth_mm[2 * bid + 1]) - dmin;
@@ -134,10 +137,43 @@ pair_key_kernel(PairKeyArgs a, K* keys, int32_t* vals) {
   }
   keys[idx] = static_cast<K>((static_cast<uint64_t>(bid) << a.key_shift) | dk);
   vals[idx] = static_cast<int32_t>(idx);
+  if (!a.walk) return;  // the parity key reconstruction reuses this struct without records
+  const int64_t hi = static_cast<uint32_t>(a.cum[idx]);
+  const int64_t lo = idx > 0 ? static_cast<int64_t>(static_cast<uint32_t>(a.cum[idx - 1])) : 0;
+  int64_t count = hi - lo;
+  if (!live) {
+    // the reference emits nothing for a culled pair; its cum range must then be empty
+    if (count != 0) atomicOr(a.err, kErrEmitCount);
+    count = 0;
+  }
+  a.counts[idx] = static_cast<int32_t>(count);
+  if (!live) return;
+  const float x = a.xys[2 * idx], y = a.xys[2 * idx + 1];
+  const float ca = a.conics[3 * idx], cb = a.conics[3 * idx + 1], cc = a.conics[3 * idx + 2];
+  const float mop = a.map_opacities[idx % a.map_opac_rows];
+  float4* w = a.walk + 2 * idx;
+  w[0] = make_float4(x, y, ca, cb);
+  w[1] = make_float4(cc, iso_level(mop), __int_as_float(static_cast<int32_t>(bid)),
+                     __int_as_float(static_cast<int32_t>(count)));
+  if (a.records) {
+    const int64_t ci = idx % a.color_rows;
+    const float op = a.opacities[idx % a.opac_rows];
+    // half-extents of the region where either opacity can reach alpha >= 1/255 (the larger
+    // isocontour), widened against rounding: the blends skip a warp's block outside it
+    const float tc = iso_level(fmax_w(mop, op));
+    const float nt = -tc / (cb * cb - ca * cc);
+    const float ex = sqrtf(nt * cc) * 1.001f + 0.01f;
+    const float ey = sqrtf(nt * ca) * 1.001f + 0.01f;
+    float4* rec = a.records + kRecordFloat4 * idx;
+    // conic pre-scaled for the blends' base-2 exponent: q = -log2(e)/2 * (a, 2b, c)
+    rec[0] = make_float4(x, y, -kHalfLog2e * ca, -kLog2e * cb);
+    rec[1] = make_float4(-kHalfLog2e * cc, op, a.colors[3 * ci], a.colors[3 * ci + 1]);
+    rec[2] = make_float4(a.colors[3 * ci + 2], depth, ex, ey);
+  }
 }
 
-// Exclusive scan of the tile counts in sorted pair order (count = cum[g] - cum[g-1]), one
-// pass with a decoupled look-back (bounded spin); also writes the total to *total_out.
+// Exclusive scan of the tile counts in sorted pair order, one pass with a decoupled look-back
+// (bounded spin).
 constexpr int kScanThreads = 256;
 constexpr int kScanItems = 8;
 constexpr unsigned long long kScanAgg = 1ull << 62;
@@ -145,7 +181,7 @@ constexpr unsigned long long kScanInc = 2ull << 62;
 constexpr unsigned long long kScanMask = (1ull << 62) - 1;
 
 __global__ void __launch_bounds__(kScanThreads)
-sorted_offsets_kernel(const int32_t* __restrict__ perm, const int32_t* __restrict__ cum,
+sorted_offsets_kernel(const int32_t* __restrict__ perm, const int32_t* __restrict__ counts,
                       int64_t total, int32_t* __restrict__ offsets, unsigned long long* status,
                       int* ticket, unsigned* err) {
   __shared__ int s_tile;
@@ -161,12 +197,7 @@ sorted_offsets_kernel(const int32_t* __restrict__ perm, const int32_t* __restric
   for (int k = 0; k < kScanItems; ++k) {
     const int64_t i = base + k;
     long long v = 0;
-    if (i < total) {
-      const int64_t g = perm[i];
-      const long long hi = static_cast<uint32_t>(cum[g]);
-      const long long lo = g > 0 ? static_cast<long long>(static_cast<uint32_t>(cum[g - 1])) : 0;
-      v = hi - lo;
-    }
+    if (i < total) v = counts[perm[i]];
     c[k] = v;
     tsum += v;
   }
@@ -220,38 +251,25 @@ sorted_offsets_kernel(const int32_t* __restrict__ perm, const int32_t* __restric
 }
 
 // Emission in sorted pair order: the ellipse walk once more per visible pair (the count
-// projection made), writing the (image | tile) bin key and the flat id at the pair's offset,
-// and packing the pair's blend record.
+// projection made), from the pair's walk record, writing the (image | tile) bin key and the
+// flat id at the pair's offset -- adjacent threads write adjacent runs.
 __global__ void __launch_bounds__(256) emit_sorted_kernel(EmitArgs a) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= a.total) return;
   const int64_t idx = a.perm[i];
-  if (idx < 0 || idx >= a.total || a.radii[idx] <= 0) return;
-  const int64_t bid = idx / a.n;
-  const int64_t hi = static_cast<uint32_t>(a.cum[idx]);
-  const int64_t lo = idx > 0 ? static_cast<int64_t>(static_cast<uint32_t>(a.cum[idx - 1])) : 0;
+  if (idx < 0 || idx >= a.total || a.counts[idx] == 0) return;
+  const float4 w0 = a.walk[2 * idx], w1 = a.walk[2 * idx + 1];
+  const int64_t bid = __float_as_int(w1.z);
   int64_t cur = a.offsets[i];
-  int64_t end = cur + (hi - lo);
+  int64_t end = cur + __float_as_int(w1.w);
   if (end > a.count || cur > end) {  // cum_tiles_hit does not describe this geometry
     atomicOr(a.err, kErrEmitCount);
     end = min(end, a.count);
     cur = min(cur, end);
   }
-  const float x = a.xys[2 * idx], y = a.xys[2 * idx + 1];
-  const float ca = a.conics[3 * idx], cb = a.conics[3 * idx + 1], cc = a.conics[3 * idx + 2];
-  if (a.records) {
-    const int64_t ci = idx % a.color_rows;
-    const float op = a.opacities[idx % a.opac_rows];
-    float4* rec = a.records + kRecordFloat4 * idx;
-    // conic pre-scaled for the blends' base-2 exponent: q = -log2(e)/2 * (a, 2b, c)
-    rec[0] = make_float4(x, y, -kHalfLog2e * ca, -kLog2e * cb);
-    rec[1] = make_float4(-kHalfLog2e * cc, op, a.colors[3 * ci], a.colors[3 * ci + 1]);
-    rec[2] = make_float4(a.colors[3 * ci + 2], a.depths[idx], 0.0f, 0.0f);
-  }
   const uint32_t img_enc = static_cast<uint32_t>(bid) << a.tile_n_bits;
-  const float t = iso_level(a.map_opacities[idx % a.map_opac_rows]);
   Ellipse e;
-  ellipse_init(ca, cb, cc, t, x, y, a.tbx, a.tby, e);
+  ellipse_init(w0.z, w0.w, w1.x, w1.y, w0.x, w0.y, a.tbx, a.tby, e);
   bool bad = false;
   if (e.valid) {
     float i0, i1;
@@ -561,10 +579,10 @@ void launch_pair_keys(const PairKeyArgs& a, bool key64, void* keys, int32_t* val
   const int64_t blocks = (a.total + 255) / 256;
   if (blocks == 0) return;
   if (key64)
-    pair_key_kernel<uint64_t><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+    pair_prep_kernel<uint64_t><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
         a, static_cast<uint64_t*>(keys), vals);
   else
-    pair_key_kernel<uint32_t><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+    pair_prep_kernel<uint32_t><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
         a, static_cast<uint32_t*>(keys), vals);
 }
 
@@ -572,7 +590,7 @@ int64_t sorted_offsets_tiles(int64_t total) {
   return (total + kScanThreads * kScanItems - 1) / (kScanThreads * kScanItems);
 }
 
-void launch_sorted_offsets(const int32_t* perm, const int32_t* cum, int64_t total,
+void launch_sorted_offsets(const int32_t* perm, const int32_t* counts, int64_t total,
                            int32_t* offsets, unsigned long long* status, int* ticket,
                            unsigned* err, cudaStream_t stream) {
   const int64_t tiles = sorted_offsets_tiles(total);
@@ -580,7 +598,7 @@ void launch_sorted_offsets(const int32_t* perm, const int32_t* cum, int64_t tota
   cudaMemsetAsync(ticket, 0, sizeof(int), stream);
   cudaMemsetAsync(status, 0, sizeof(unsigned long long) * tiles, stream);
   sorted_offsets_kernel<<<static_cast<unsigned>(tiles), kScanThreads, 0, stream>>>(
-      perm, cum, total, offsets, status, ticket, err);
+      perm, counts, total, offsets, status, ticket, err);
 }
 
 void launch_emit(const EmitArgs& a, cudaStream_t stream) {
