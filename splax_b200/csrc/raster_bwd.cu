@@ -2,8 +2,8 @@
 // (splax/_rasterize/_kernels.py:530-794, 935-1209) with _blend_color_vjp / _blend_depth_vjp
 // (:1212-1302).
 //
-// Recompute-style: one 128-thread CTA per (output image, tile); each warp owns a 16x4 block and
-// each thread two vertically adjacent pixels. A warp skips every gaussian whose alpha >= 1/255
+// Recompute-style: one 64-thread CTA per (output image, tile); each warp owns a 16x8 block and
+// each thread four vertically adjacent pixels. A warp skips every gaussian whose alpha >= 1/255
 // ellipse misses its block (those evaluations are all rejected). The walk runs back to front from the block's largest
 // final_idx over batches of 256 records staged in shared memory (plus the flat ids that
 // address the gradients). Each pixel rebuilds T by dividing out (1 - alpha), and only entries
@@ -20,7 +20,6 @@
 namespace splax {
 namespace {
 
-constexpr int kBwdThreads = 128;
 constexpr float kLn2 = 0.693147180559945f;
 
 struct BwdPixel {
@@ -69,9 +68,15 @@ __device__ __forceinline__ bool vjp_one(BwdPixel& s, int32_t idx, float p, float
   return true;
 }
 
-template <bool DEPTH, bool COUNT>
-__global__ void __launch_bounds__(kBwdThreads)
+// PIX vertically adjacent pixels per thread; a warp owns a 16 x (2 PIX) block of the tile and
+// the CTA (256 / PIX threads) the whole tile. Four pixels per thread amortise the per-gaussian
+// warp reduction over 128 pixels.
+constexpr int kPixels = 4;
+
+template <bool DEPTH, bool COUNT, int PIX>
+__global__ void __launch_bounds__(kBlockSize / PIX)
 raster_bwd_kernel(RasterBwdArgs a) {
+  constexpr int kBwdThreads = kBlockSize / PIX;
   constexpr int K = DEPTH ? 10 : 9;
   unsigned long long evals = 0, contribs = 0;
   __shared__ float4 s_r0[kBlockSize];
@@ -93,16 +98,18 @@ raster_bwd_kernel(RasterBwdArgs a) {
   const int tr = threadIdx.x, lane = tr & 31, warp = tr >> 5;
   const int32_t tile_x = tile_local % a.tbx, tile_y = tile_local / a.tbx;
   const int32_t j = tile_x * kBlockWidth + (lane & 15);
-  const int32_t i0 = tile_y * kBlockWidth + 4 * warp + 2 * (lane >> 4);
+  const int32_t i0 = tile_y * kBlockWidth + 2 * PIX * warp + PIX * (lane >> 4);
   const float px = static_cast<float>(j) + 0.5f;
   const float py0 = static_cast<float>(i0) + 0.5f;
+  // centre of the warp's block of pixel centres (half-extents 7.5 and PIX - 0.5)
   const float wcx = static_cast<float>(tile_x * kBlockWidth) + 8.0f;
-  const float wcy = static_cast<float>(tile_y * kBlockWidth + 4 * warp) + 2.0f;
+  const float wcy = static_cast<float>(tile_y * kBlockWidth + 2 * PIX * warp + PIX);
+  constexpr float kHalfY = PIX - 0.5f;
 
-  BwdPixel px_s[2];
+  BwdPixel px_s[PIX];
   const float* bg = a.background + 3 * (a.sel_bg ? image_id : 0);
 #pragma unroll
-  for (int k = 0; k < 2; ++k) {
+  for (int k = 0; k < PIX; ++k) {
     BwdPixel& s = px_s[k];
     const int32_t i = i0 + k;
     s.bin_final = range_start - 1;
@@ -144,8 +151,10 @@ raster_bwd_kernel(RasterBwdArgs a) {
   }
 
   // walk starts at the block maximum of final_idx
-  const int32_t wmax =
-      __reduce_max_sync(0xffffffffu, max(px_s[0].bin_final, px_s[1].bin_final));
+  int32_t tmax = px_s[0].bin_final;
+#pragma unroll
+  for (int k = 1; k < PIX; ++k) tmax = max(tmax, px_s[k].bin_final);
+  const int32_t wmax = __reduce_max_sync(0xffffffffu, tmax);
   if (lane == 0) s_wmax[warp] = wmax;
   __syncthreads();
   int32_t start_idx = s_wmax[0];
@@ -184,21 +193,28 @@ raster_bwd_kernel(RasterBwdArgs a) {
       const int32_t idx = batch_end - t;
       const float4 r0 = s_r0[t];
       const float4 r2 = s_r2[t];
-      if constexpr (COUNT) evals += (idx <= px_s[0].bin_final) + (idx <= px_s[1].bin_final);
-      if (fabsf(r0.x - wcx) > r2.z + 7.5f || fabsf(r0.y - wcy) > r2.w + 1.5f) continue;
+      if constexpr (COUNT) {
+#pragma unroll
+        for (int k = 0; k < PIX; ++k) evals += idx <= px_s[k].bin_final;
+      }
+      if (fabsf(r0.x - wcx) > r2.z + 7.5f || fabsf(r0.y - wcy) > r2.w + kHalfY) continue;
       const float4 r1 = s_r1[t];
       const float dx = r0.x - px;
-      const float dy0 = r0.y - py0, dy1 = dy0 - 1.0f;
+      const float dy0 = r0.y - py0;
       const float qxx = r0.z * dx * dx, qbx = r0.w * dx;
-      const float p0 = fmaf(fmaf(r1.x, dy0, qbx), dy0, qxx);
-      const float p1 = fmaf(fmaf(r1.x, dy1, qbx), dy1, qxx);
       float acc[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) acc[k] = 0.0f;
-      const bool c0 = vjp_one<DEPTH>(px_s[0], idx, p0, dy0, r1.y, r1.z, r1.w, r2.x, r2.y, acc);
-      const bool c1 = vjp_one<DEPTH>(px_s[1], idx, p1, dy1, r1.y, r1.z, r1.w, r2.x, r2.y, acc);
-      if constexpr (COUNT) contribs += c0 + c1;
-      if (__ballot_sync(0xffffffffu, c0 || c1) == 0u) continue;
+      bool any = false;
+#pragma unroll
+      for (int k = 0; k < PIX; ++k) {
+        const float dy = dy0 - static_cast<float>(k);
+        const float p = fmaf(fmaf(r1.x, dy, qbx), dy, qxx);
+        const bool c = vjp_one<DEPTH>(px_s[k], idx, p, dy, r1.y, r1.z, r1.w, r2.x, r2.y, acc);
+        if constexpr (COUNT) contribs += c;
+        any |= c;
+      }
+      if (__ballot_sync(0xffffffffu, any) == 0u) continue;
       // per-thread cotangents: sum_px v_sigma (dx, dy) and the second moments give the conic
       // and xy terms; (a, b, c) = -ln2 (2 qa, qb, 2 qc) recovers the unscaled conic
       const float sx = acc[3] * dx, sy = acc[4];
@@ -231,19 +247,25 @@ raster_bwd_kernel(RasterBwdArgs a) {
   }
 }
 
+template <int PIX>
+void launch_bwd(const RasterBwdArgs& a, unsigned g, cudaStream_t stream) {
+  constexpr int nt = kBlockSize / PIX;
+  if (a.v_out_depth) {
+    if (a.work) raster_bwd_kernel<true, true, PIX><<<g, nt, 0, stream>>>(a);
+    else raster_bwd_kernel<true, false, PIX><<<g, nt, 0, stream>>>(a);
+  } else {
+    if (a.work) raster_bwd_kernel<false, true, PIX><<<g, nt, 0, stream>>>(a);
+    else raster_bwd_kernel<false, false, PIX><<<g, nt, 0, stream>>>(a);
+  }
+}
+
 }  // namespace
 
 void launch_raster_bwd(const RasterBwdArgs& a, cudaStream_t stream) {
   const int64_t blocks = a.B_out * a.num_tiles;
   if (blocks == 0) return;
   const unsigned g = static_cast<unsigned>(blocks);
-  if (a.v_out_depth) {
-    if (a.work) raster_bwd_kernel<true, true><<<g, kBwdThreads, 0, stream>>>(a);
-    else raster_bwd_kernel<true, false><<<g, kBwdThreads, 0, stream>>>(a);
-  } else {
-    if (a.work) raster_bwd_kernel<false, true><<<g, kBwdThreads, 0, stream>>>(a);
-    else raster_bwd_kernel<false, false><<<g, kBwdThreads, 0, stream>>>(a);
-  }
+  launch_bwd<kPixels>(a, g, stream);
 }
 
 }  // namespace splax

@@ -1,9 +1,9 @@
 // Forward blend: _rasterize_kernel and _rasterize_depth_kernel
 // (splax/_rasterize/_kernels.py:102-205, 277-380).
 //
-// One 128-thread CTA per (image, 16x16 tile); each warp owns a 16x4 block of the tile and each
-// thread two vertically adjacent pixels, so every shared-memory record read and the x-terms of
-// the Gaussian exponent serve two evaluations. The tile's sorted list is walked in batches of
+// One 64-thread CTA per (image, 16x16 tile); each warp owns a 16x8 block of the tile and each
+// thread four vertically adjacent pixels, so every shared-memory record read and the x-terms of
+// the Gaussian exponent serve four evaluations. The tile's sorted list is walked in batches of
 // 256: the CTA
 // gathers the packed 48-byte records (three 16-byte loads each, written by the emission pass)
 // into shared memory, then blends the batch front to back from shared memory with broadcast
@@ -19,7 +19,6 @@
 namespace splax {
 namespace {
 
-constexpr int kFwdThreads = 128;
 
 struct PixelState {
   float T = 1.0f, c0 = 0.0f, c1 = 0.0f, c2 = 0.0f, dep = 0.0f;
@@ -30,7 +29,6 @@ struct PixelState {
 template <bool DEPTH, bool COUNT>
 __device__ __forceinline__ void blend_one(PixelState& s, float p, float opac, float r, float g,
                                           float b, float depth, int32_t idx,
-                                          unsigned long long& evals,
                                           unsigned long long& contribs) {
   if (s.done) return;
   const float alpha = fminf(kAlphaMax, opac * ex2_approx(p));
@@ -50,9 +48,14 @@ __device__ __forceinline__ void blend_one(PixelState& s, float p, float opac, fl
   if constexpr (COUNT) ++contribs;
 }
 
-template <bool DEPTH, bool COUNT>
-__global__ void __launch_bounds__(kFwdThreads)
+// PIX vertically adjacent pixels per thread; a warp owns a 16 x (2 PIX) block of the tile and
+// the CTA (256 / PIX threads) the whole tile.
+constexpr int kPixels = 4;  // pixels per thread: 64 threads per tile
+
+template <bool DEPTH, bool COUNT, int PIX>
+__global__ void __launch_bounds__(kBlockSize / PIX)
 raster_fwd_kernel(RasterFwdArgs a) {
+  constexpr int kFwdThreads = kBlockSize / PIX;
   unsigned long long evals = 0, contribs = 0;
   __shared__ float4 s_r0[kBlockSize];
   __shared__ float4 s_r1[kBlockSize];
@@ -63,20 +66,22 @@ raster_fwd_kernel(RasterFwdArgs a) {
   const int32_t tile_x = tile_local % a.tbx, tile_y = tile_local / a.tbx;
   const int tr = threadIdx.x, lane = tr & 31, warp = tr >> 5;
   const int32_t j = tile_x * kBlockWidth + (lane & 15);
-  const int32_t i0 = tile_y * kBlockWidth + 4 * warp + 2 * (lane >> 4), i1 = i0 + 1;
+  const int32_t i0 = tile_y * kBlockWidth + 2 * PIX * warp + PIX * (lane >> 4);
   const float px = static_cast<float>(j) + 0.5f;
   const float py0 = static_cast<float>(i0) + 0.5f;
-  const bool inside0 = i0 < a.img_h && j < a.img_w;
-  const bool inside1 = i1 < a.img_h && j < a.img_w;
-  PixelState s0, s1;
-  s0.done = !inside0;
-  s1.done = !inside1;
+  PixelState st[PIX];
+  bool all_done = true;
+#pragma unroll
+  for (int k = 0; k < PIX; ++k) {
+    st[k].done = !(i0 + k < a.img_h && j < a.img_w);
+    all_done &= st[k].done;
+  }
   const int2 range = reinterpret_cast<const int2*>(a.tile_bins)[tile_g];
   const int32_t range_start = range.x, range_end = range.y;
   const int32_t num_batches = (range_end - range_start + kBlockSize - 1) / kBlockSize;
   for (int32_t b = 0; b < num_batches; ++b) {
     // block vote doubles as the barrier protecting the previous batch's shared reads
-    if (__syncthreads_count(s0.done && s1.done) >= kFwdThreads) break;
+    if (__syncthreads_count(all_done) >= kFwdThreads) break;
     const int32_t batch_start = range_start + b * kBlockSize;
 #pragma unroll
     for (int h = 0; h < kBlockSize / kFwdThreads; ++h) {
@@ -99,21 +104,25 @@ raster_fwd_kernel(RasterFwdArgs a) {
     }
     __syncthreads();
     const int32_t batch_size = min(kBlockSize, range_end - batch_start);
-    if (!(s0.done && s1.done)) {
+    if (!all_done) {
       for (int32_t t = 0; t < batch_size; ++t) {
         const float4 r0 = s_r0[t];  // x, y, qa, qb  (q = -log2(e)/2 * (a, 2b, c))
         const float4 r1 = s_r1[t];  // qc, opacity, r, g
         const float2 r2 = s_r2[t];  // b, depth
-        if constexpr (COUNT) evals += !s0.done + !s1.done;
         const float dx = r0.x - px;
-        const float dy0 = r0.y - py0, dy1 = dy0 - 1.0f;
+        const float dy0 = r0.y - py0;
         const float qxx = r0.z * dx * dx, qbx = r0.w * dx;
-        const float p0 = fmaf(fmaf(r1.x, dy0, qbx), dy0, qxx);
-        const float p1 = fmaf(fmaf(r1.x, dy1, qbx), dy1, qxx);
         const int32_t idx = batch_start + t;
-        blend_one<DEPTH, COUNT>(s0, p0, r1.y, r1.z, r1.w, r2.x, r2.y, idx, evals, contribs);
-        blend_one<DEPTH, COUNT>(s1, p1, r1.y, r1.z, r1.w, r2.x, r2.y, idx, evals, contribs);
-        if (s0.done && s1.done) break;
+        all_done = true;
+#pragma unroll
+        for (int k = 0; k < PIX; ++k) {
+          if constexpr (COUNT) evals += !st[k].done;
+          const float dy = dy0 - static_cast<float>(k);
+          const float p = fmaf(fmaf(r1.x, dy, qbx), dy, qxx);
+          blend_one<DEPTH, COUNT>(st[k], p, r1.y, r1.z, r1.w, r2.x, r2.y, idx, contribs);
+          all_done &= st[k].done;
+        }
+        if (all_done) break;
       }
     }
   }
@@ -128,10 +137,10 @@ raster_fwd_kernel(RasterFwdArgs a) {
   const float* bg = a.background + 3 * (a.sel_bg ? image_id : 0);
   const float bg0 = bg[0], bg1 = bg[1], bg2 = bg[2];
 #pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    const PixelState& s = k ? s1 : s0;
-    if (!(k ? inside1 : inside0)) continue;
-    const int32_t i = k ? i1 : i0;  // rows i0 and i0 + 1
+  for (int k = 0; k < PIX; ++k) {
+    const PixelState& s = st[k];
+    const int32_t i = i0 + k;
+    if (!(i < a.img_h && j < a.img_w)) continue;
     const int64_t pix = (image_id * a.img_h + i) * static_cast<int64_t>(a.img_w) + j;
     a.final_Ts[pix] = s.T;
     a.final_idx[pix] = s.cur_idx;
@@ -142,19 +151,25 @@ raster_fwd_kernel(RasterFwdArgs a) {
   }
 }
 
+template <int PIX>
+void launch_fwd(const RasterFwdArgs& a, unsigned g, cudaStream_t stream) {
+  constexpr int nt = kBlockSize / PIX;
+  if (a.out_depth) {
+    if (a.work) raster_fwd_kernel<true, true, PIX><<<g, nt, 0, stream>>>(a);
+    else raster_fwd_kernel<true, false, PIX><<<g, nt, 0, stream>>>(a);
+  } else {
+    if (a.work) raster_fwd_kernel<false, true, PIX><<<g, nt, 0, stream>>>(a);
+    else raster_fwd_kernel<false, false, PIX><<<g, nt, 0, stream>>>(a);
+  }
+}
+
 }  // namespace
 
 void launch_raster_fwd(const RasterFwdArgs& a, cudaStream_t stream) {
   const int64_t blocks = a.num_images * a.num_tiles;
   if (blocks == 0) return;
   const unsigned g = static_cast<unsigned>(blocks);
-  if (a.out_depth) {
-    if (a.work) raster_fwd_kernel<true, true><<<g, kFwdThreads, 0, stream>>>(a);
-    else raster_fwd_kernel<true, false><<<g, kFwdThreads, 0, stream>>>(a);
-  } else {
-    if (a.work) raster_fwd_kernel<false, true><<<g, kFwdThreads, 0, stream>>>(a);
-    else raster_fwd_kernel<false, false><<<g, kFwdThreads, 0, stream>>>(a);
-  }
+  launch_fwd<kPixels>(a, g, stream);
 }
 
 }  // namespace splax

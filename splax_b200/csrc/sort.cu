@@ -322,7 +322,6 @@ __global__ void reference_keys_kernel(const uint32_t* __restrict__ bin_keys,
 
 // ------------------------------------------------------------------ onesweep radix sort
 constexpr int kSortThreads = 512;
-constexpr int kSortWarps = kSortThreads / 32;
 constexpr int kItems32 = 8;  // 4096 keys per tile for 32-bit keys
 constexpr int kItems64 = 6;  // 3072 keys per tile for 64-bit keys
 constexpr int kHistThreads = 256;
@@ -377,13 +376,14 @@ __global__ void radix_scan_kernel(const uint32_t* hist, uint32_t* offsets) {
   offsets[p * 256 + threadIdx.x] = block_exclusive_scan<256>(v, s_warp);
 }
 
-template <typename K, int ITEMS>
-__global__ void __launch_bounds__(kSortThreads)
+template <typename K, int ITEMS, int NT>
+__global__ void __launch_bounds__(NT)
 onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* __restrict__ kout,
                 int32_t* __restrict__ vout, int64_t count, int shift,
                 const uint32_t* __restrict__ goff, unsigned long long* status, int* tile_counter,
                 unsigned* err) {
-  constexpr int TILE = kSortThreads * ITEMS;
+  constexpr int TILE = NT * ITEMS;
+  constexpr int kSortWarps = NT / 32;
   __shared__ uint32_t s_wh[kSortWarps][256];
   __shared__ uint32_t s_bx[256];
   __shared__ long long s_gb[256];
@@ -394,7 +394,7 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
   int32_t* s_vals = reinterpret_cast<int32_t*>(s_raw + TILE * sizeof(K));
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int i = tid; i < kSortWarps * 256; i += kSortThreads) (&s_wh[0][0])[i] = 0;
+  for (int i = tid; i < kSortWarps * 256; i += NT) (&s_wh[0][0])[i] = 0;
   if (tid == 0) s_tile = atomicAdd(tile_counter, 1);
   __syncthreads();
   const int64_t tile = s_tile;
@@ -464,7 +464,7 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
       st_relaxed(st, kFlagInc | (static_cast<unsigned long long>(prefix) + sum));
     }
   }
-  const uint32_t excl = block_exclusive_scan<kSortThreads>(sum, s_warp);
+  const uint32_t excl = block_exclusive_scan<NT>(sum, s_warp);
   if (tid < 256) {
     s_bx[tid] = excl;
     s_gb[tid] = static_cast<long long>(goff[tid]) + prefix - static_cast<long long>(excl);
@@ -483,7 +483,7 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
   __syncthreads();
 #pragma unroll
   for (int j = 0; j < ITEMS; ++j) {
-    const int p = j * kSortThreads + tid;
+    const int p = j * NT + tid;
     if (p < nvalid) {
       const K kk = s_keys[p];
       const uint32_t d = static_cast<uint32_t>(static_cast<uint64_t>(kk) >> shift) & 255u;
@@ -526,7 +526,7 @@ __global__ void tile_bins_kernel(const K* __restrict__ keys, int64_t count, int 
   }
 }
 
-template <typename K, int ITEMS>
+template <typename K, int ITEMS, int NT>
 int sort_impl(const SortScratch& s, int64_t count, int bits, cudaStream_t stream) {
   const int passes = (bits + 7) / 8;
   uint32_t* hist = s.hist;
@@ -537,19 +537,19 @@ int sort_impl(const SortScratch& s, int64_t count, int bits, cudaStream_t stream
   radix_hist_kernel<K><<<static_cast<unsigned>(hblocks), kHistThreads, 0, stream>>>(
       reinterpret_cast<const K*>(s.keys[0]), count, passes, hist);
   radix_scan_kernel<<<passes, 256, 0, stream>>>(hist, offsets);
-  constexpr int TILE = kSortThreads * ITEMS;
+  constexpr int TILE = NT * ITEMS;
   const int64_t tiles = (count + TILE - 1) / TILE;
   const size_t smem = TILE * (sizeof(K) + sizeof(int32_t));
   static bool attr_set = false;  // per instantiation: static + dynamic exceeds 48 KiB
   if (!attr_set) {
-    cudaFuncSetAttribute(onesweep_kernel<K, ITEMS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(onesweep_kernel<K, ITEMS, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(smem));
     attr_set = true;
   }
   int cur = 0;
   for (int p = 0; p < passes; ++p) {
     cudaMemsetAsync(s.status, 0, sizeof(unsigned long long) * tiles * 256, stream);
-    onesweep_kernel<K, ITEMS><<<static_cast<unsigned>(tiles), kSortThreads, smem, stream>>>(
+    onesweep_kernel<K, ITEMS, NT><<<static_cast<unsigned>(tiles), NT, smem, stream>>>(
         reinterpret_cast<const K*>(s.keys[cur]), s.vals[cur], reinterpret_cast<K*>(s.keys[cur ^ 1]),
         s.vals[cur ^ 1], count, 8 * p, offsets + p * 256, s.status, s.tile_counters + p, s.err);
     cur ^= 1;
@@ -620,8 +620,8 @@ int sort_tile_items(bool key64) { return kSortThreads * (key64 ? kItems64 : kIte
 int radix_sort_pairs(const SortScratch& s, bool key64, int64_t count, int bits,
                      cudaStream_t stream) {
   if (count <= 1) return 0;
-  return key64 ? sort_impl<uint64_t, kItems64>(s, count, bits, stream)
-               : sort_impl<uint32_t, kItems32>(s, count, bits, stream);
+  return key64 ? sort_impl<uint64_t, kItems64, kSortThreads>(s, count, bits, stream)
+               : sort_impl<uint32_t, kItems32, kSortThreads>(s, count, bits, stream);
 }
 
 void launch_tile_bins(const void* keys, bool key64, int64_t count, int shift, int32_t tile_n_bits,
