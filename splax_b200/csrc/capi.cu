@@ -78,6 +78,7 @@ constexpr double kScratchHeadroom = 1.25;  // splax/_cache.py:149
 // ------------------------------------------------------------------ profiling (opt-in)
 std::atomic<bool> g_timing{false};
 std::atomic<bool> g_count_work{false};
+constexpr int kWorkWords = 7;  // device work counters (see DeviceState::work)
 
 enum Kind { kProjectFwd, kProjectBwd, kDepthMinmax, kPairKeys, kPairSort, kPairScan, kEmit,
             kRadixSort, kTileBins, kRasterFwd, kRasterBwd, kNumKinds };
@@ -202,7 +203,9 @@ struct DeviceState {
   DevBuf proj_status; // projection scan look-back words
   int32_t* pinned = nullptr;  // [0] count, [1] error word
   cudaEvent_t ev = nullptr;
-  DevBuf work;                // device work counters: fwd evals, fwd contribs, bwd evals, bwd contribs
+  // device work counters: fwd evals, fwd contribs, bwd evals, bwd contribs, bwd warp steps,
+  // bwd warp steps past the ellipse cull, bwd warp steps with a contribution
+  DevBuf work;
   KernelTimer timer;
   WorkUnits units;
   // the most recent sort_and_bin result, reusable by a backward over the same inputs
@@ -251,8 +254,8 @@ struct DeviceState {
     SPLAX_CUDA(buf_reserve(misc, 64));
     SPLAX_CUDA(cudaMemset(misc.p, 0, 64));
     SPLAX_CUDA(buf_reserve(hist, sizeof(uint32_t) * 2 * 8 * 256));
-    SPLAX_CUDA(buf_reserve(work, 4 * sizeof(unsigned long long)));
-    SPLAX_CUDA(cudaMemset(work.p, 0, 4 * sizeof(unsigned long long)));
+    SPLAX_CUDA(buf_reserve(work, kWorkWords * sizeof(unsigned long long)));
+    SPLAX_CUDA(cudaMemset(work.p, 0, kWorkWords * sizeof(unsigned long long)));
     SPLAX_CUDA(cudaMallocHost(&pinned, 4 * sizeof(int32_t)));
     SPLAX_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
     return SPLAX_OK;
@@ -1054,7 +1057,7 @@ int splax_profile_reset(void) {
   if (rc) return rc;
   st->timer.reset();
   st->units = WorkUnits{};
-  SPLAX_CUDA(cudaMemset(st->work.p, 0, 4 * sizeof(unsigned long long)));
+  SPLAX_CUDA(cudaMemset(st->work.p, 0, kWorkWords * sizeof(unsigned long long)));
   return SPLAX_OK;
 }
 
@@ -1066,7 +1069,7 @@ int splax_profile_report(char* buf, int32_t len) {
   rc = st->init();
   if (rc) return -rc;
   st->timer.collect();
-  unsigned long long w[4] = {0, 0, 0, 0};
+  unsigned long long w[kWorkWords] = {};
   if (cudaMemcpy(w, st->work.p, sizeof(w), cudaMemcpyDeviceToHost) != cudaSuccess) return -SPLAX_ERR_CUDA;
   std::string js = "{\"kernels\": {";
   char tmp[256];
@@ -1091,8 +1094,13 @@ int splax_profile_report(char* buf, int32_t len) {
            (long long)u.sort_reuses);
   js += tmp;
   snprintf(tmp, sizeof tmp,
-           "\"pairs_sorted\": %lld, \"pair_key_bytes\": %lld, \"pair_pass_keys\": %lld}}",
+           "\"pairs_sorted\": %lld, \"pair_key_bytes\": %lld, \"pair_pass_keys\": %lld, ",
            (long long)u.pairs_sorted, (long long)u.pair_key_bytes, (long long)u.pair_pass_keys);
+  js += tmp;
+  snprintf(tmp, sizeof tmp,
+           "\"bwd_warp_steps\": %llu, \"bwd_warp_steps_uncull\": %llu, "
+           "\"bwd_warp_steps_active\": %llu}}",
+           w[4], w[5], w[6]);
   js += tmp;
   if (static_cast<int32_t>(js.size()) + 1 > len) return -SPLAX_ERR_INVALID_ARGUMENT;
   memcpy(buf, js.c_str(), js.size() + 1);

@@ -209,6 +209,46 @@ __device__ __forceinline__ unsigned long long ld_relaxed(const unsigned long lon
   return v;
 }
 
+// Decoupled look-back by one full warp over single-word tile states (2-bit flag: 1 aggregate,
+// 2 inclusive prefix, in the top bits; value below): the 32 lanes read 32 predecessors per
+// round trip, sum up to the nearest inclusive one, and repeat further back if there is none.
+// Returns the exclusive prefix of `tile`. Spins are bounded; on expiry sets kErrLookbackTimeout.
+constexpr unsigned long long kLookbackAgg = 1ull << 62;
+constexpr unsigned long long kLookbackInc = 2ull << 62;
+constexpr unsigned long long kLookbackMask = (1ull << 62) - 1;
+
+__device__ __forceinline__ long long warp_lookback(const unsigned long long* status, int64_t tile,
+                                                   unsigned* err) {
+  constexpr unsigned long long kInc = kLookbackInc, kMask = kLookbackMask;
+  const int lane = threadIdx.x & 31;
+  long long prefix = 0;
+  int64_t base = tile - 1;
+  long long spins = 0;
+  while (base >= 0) {
+    const int64_t j = base - lane;
+    const unsigned long long s = j >= 0 ? ld_relaxed(status + j) : kInc;  // before tile 0: 0
+    const unsigned long long flag = s & ~kMask;
+    const unsigned inc = __ballot_sync(0xffffffffu, flag == kInc);
+    const unsigned notready = __ballot_sync(0xffffffffu, flag == 0);
+    const int first = inc ? __ffs(inc) - 1 : 31;
+    const unsigned needed = first == 31 ? 0xffffffffu : ((2u << first) - 1u);
+    if (notready & needed) {
+      if (++spins > kSpinLimit) {
+        if (lane == 0) atomicOr(err, kErrLookbackTimeout);
+        break;
+      }
+      continue;
+    }
+    long long v = lane <= first ? static_cast<long long>(s & kMask) : 0;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    prefix += v;
+    if (inc) break;
+    base -= 32;
+  }
+  return prefix;
+}
+
 // Release / acquire accesses for look-back status words.
 __device__ __forceinline__ void st_release(unsigned long long* p, unsigned long long v) {
   asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");

@@ -97,6 +97,9 @@ struct PairKeyArgs {
 
 void launch_project_fwd(const ProjectArgs& a, unsigned long long* status, int* ticket,
                         unsigned* err, cudaStream_t stream);
+// The projection's fused scan covers kProjScanTile pairs per CTA and keeps one look-back word
+// per such tile.
+constexpr int64_t kProjScanTile = 1024;
 int64_t project_scan_tiles(int64_t total);
 void launch_project_bwd(const ProjectBwdArgs& a, cudaStream_t stream);
 

@@ -111,10 +111,6 @@ __device__ __forceinline__ void project_geom(const ProjectArgs& a, int64_t idx, 
   }
 }
 
-constexpr unsigned long long kFlagAgg = 1ull << 62;
-constexpr unsigned long long kFlagInc = 2ull << 62;
-constexpr unsigned long long kValMask = (1ull << 62) - 1;
-
 // Projection of one pair; returns its tile count (0 when culled), writing every output row.
 __device__ __forceinline__ int32_t project_one(const ProjectArgs& a, int64_t idx) {
   int64_t bid = idx / a.n, gid = idx % a.n;
@@ -186,71 +182,69 @@ __device__ __forceinline__ int32_t project_one(const ProjectArgs& a, int64_t idx
 }
 
 constexpr int kProjThreads = 256;
+constexpr int kProjItems = kProjScanTile / kProjThreads;  // pairs per thread
+constexpr int kProjTile = kProjScanTile;
 
 __global__ void __launch_bounds__(kProjThreads)
 project_fwd_kernel(ProjectArgs a, unsigned long long* status, int* ticket, unsigned* err) {
   __shared__ int s_tile;
+  __shared__ __align__(16) int32_t s_cnt[kProjTile];
   __shared__ long long s_warp[kProjThreads / 32];
   __shared__ long long s_prefix;
   if (threadIdx.x == 0) s_tile = atomicAdd(ticket, 1);
   __syncthreads();
-  const int tile = s_tile;
-  const int64_t idx = static_cast<int64_t>(tile) * kProjThreads + threadIdx.x;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  long long count = idx < a.total ? project_one(a, idx) : 0;
-  // block inclusive scan
-  long long v = count;
+  const int64_t tile = s_tile;
+  const int64_t base = tile * kProjTile;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+#pragma unroll
+  for (int k = 0; k < kProjItems; ++k) {
+    const int64_t idx = base + k * kProjThreads + tid;
+    s_cnt[k * kProjThreads + tid] = idx < a.total ? project_one(a, idx) : 0;
+  }
+  __syncthreads();
+  // each thread scans 4 consecutive pairs; a block scan of the thread sums places them
+  static_assert(kProjItems == 4, "the scan reads each thread's counts as one int4");
+  const int4 c4 = reinterpret_cast<const int4*>(s_cnt)[tid];
+  const int32_t c[kProjItems] = {c4.x, c4.y, c4.z, c4.w};
+  const long long tsum = static_cast<long long>(c4.x) + c4.y + c4.z + c4.w;
+  long long v = tsum;
 #pragma unroll
   for (int off = 1; off < 32; off <<= 1) {
-    long long o = __shfl_up_sync(0xffffffffu, v, off);
+    const long long o = __shfl_up_sync(0xffffffffu, v, off);
     if (lane >= off) v += o;
   }
   if (lane == 31) s_warp[warp] = v;
   __syncthreads();
-  if (warp == 0) {
-    long long w = lane < kProjThreads / 32 ? s_warp[lane] : 0;
+  long long wpre = 0, agg = 0;
 #pragma unroll
-    for (int off = 1; off < kProjThreads / 32; off <<= 1) {
-      long long o = __shfl_up_sync(0xffffffffu, w, off);
-      if (lane >= off) w += o;
-    }
-    if (lane < kProjThreads / 32) s_warp[lane] = w;  // inclusive warp totals
+  for (int w = 0; w < kProjThreads / 32; ++w) {
+    if (w < warp) wpre += s_warp[w];
+    agg += s_warp[w];
   }
-  __syncthreads();
-  if (warp > 0) v += s_warp[warp - 1];
-  // decoupled look-back on the block aggregate (thread 0), bounded spin
-  if (threadIdx.x == 0) {
-    unsigned long long agg = static_cast<unsigned long long>(s_warp[kProjThreads / 32 - 1]);
+  if (warp == 0) {
     long long prefix = 0;
     if (tile == 0) {
-      st_relaxed(&status[0], kFlagInc | agg);
+      if (lane == 0) st_relaxed(&status[0], kLookbackInc | static_cast<unsigned long long>(agg));
     } else {
-      st_relaxed(&status[tile], kFlagAgg | agg);
-      int j = tile - 1;
-      long long spins = 0;
-      while (j >= 0) {
-        unsigned long long s = ld_relaxed(&status[j]);
-        unsigned long long flag = s & ~kValMask;
-        if (flag == 0) {
-          if (++spins > kSpinLimit) {
-            atomicOr(err, kErrLookbackTimeout);
-            break;
-          }
-          continue;
-        }
-        prefix += static_cast<long long>(s & kValMask);
-        if (flag == kFlagInc) break;
-        --j;
-      }
-      st_relaxed(&status[tile], kFlagInc | (static_cast<unsigned long long>(prefix) + agg));
+      if (lane == 0) st_relaxed(&status[tile], kLookbackAgg | static_cast<unsigned long long>(agg));
+      prefix = warp_lookback(status, tile, err);
+      if (lane == 0)
+        st_relaxed(&status[tile], kLookbackInc | static_cast<unsigned long long>(prefix + agg));
     }
-    s_prefix = prefix;
-    if (static_cast<int64_t>(tile + 1) * kProjThreads >= a.total &&
-        prefix + static_cast<long long>(agg) > 0x7fffffffll)
-      atomicOr(err, kErrCountOverflow);
+    if (lane == 0) {
+      s_prefix = prefix;
+      if (base + kProjTile >= a.total && prefix + agg > 0x7fffffffll)
+        atomicOr(err, kErrCountOverflow);
+    }
   }
   __syncthreads();
-  if (idx < a.total) a.cum_tiles_hit[idx] = static_cast<int32_t>(static_cast<uint32_t>(s_prefix + v));
+  long long run = s_prefix + wpre + v - tsum;
+#pragma unroll
+  for (int m = 0; m < kProjItems; ++m) {
+    run += c[m];
+    const int64_t idx = base + tid * kProjItems + m;
+    if (idx < a.total) a.cum_tiles_hit[idx] = static_cast<int32_t>(static_cast<uint32_t>(run));
+  }
 }
 
 // ------------------------------------------------------------------ backward
@@ -450,13 +444,13 @@ __global__ void __launch_bounds__(kBwdThreads) project_bwd_kernel(ProjectBwdArgs
 
 void launch_project_fwd(const ProjectArgs& a, unsigned long long* status, int* ticket,
                         unsigned* err, cudaStream_t stream) {
-  const int64_t blocks = (a.total + kProjThreads - 1) / kProjThreads;
+  const int64_t blocks = project_scan_tiles(a.total);
   if (blocks == 0) return;
   project_fwd_kernel<<<static_cast<unsigned>(blocks), kProjThreads, 0, stream>>>(a, status, ticket,
                                                                                  err);
 }
 
-int64_t project_scan_tiles(int64_t total) { return (total + kProjThreads - 1) / kProjThreads; }
+int64_t project_scan_tiles(int64_t total) { return (total + kProjTile - 1) / kProjTile; }
 
 void launch_project_bwd(const ProjectBwdArgs& a, cudaStream_t stream) {
   const int64_t blocks_per_image = (a.n + kBwdThreads - 1) / kBwdThreads;

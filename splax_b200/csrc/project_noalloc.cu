@@ -35,8 +35,7 @@ namespace splax {
 namespace {
 
 constexpr int64_t kNoAllocMaxPairs = int64_t(1) << 24;
-constexpr int64_t kScanPairsPerTile = 256;  // project_scan_tiles granularity
-constexpr int64_t kNoAllocTiles = kNoAllocMaxPairs / kScanPairsPerTile;
+constexpr int64_t kNoAllocTiles = kNoAllocMaxPairs / kProjScanTile;
 // word 0: block ticket, word 1: device error word, words 2..: one look-back word per scan tile
 constexpr int64_t kNoAllocWords = kNoAllocTiles + 2;
 

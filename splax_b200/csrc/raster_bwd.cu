@@ -79,6 +79,7 @@ raster_bwd_kernel(RasterBwdArgs a) {
   constexpr int kBwdThreads = kBlockSize / PIX;
   constexpr int K = DEPTH ? 10 : 9;
   unsigned long long evals = 0, contribs = 0;
+  unsigned steps = 0, steps_uncull = 0, steps_active = 0;  // warp steps (COUNT builds only)
   __shared__ float4 s_r0[kBlockSize];
   __shared__ float4 s_r1[kBlockSize];
   __shared__ float4 s_r2[kBlockSize];
@@ -196,8 +197,10 @@ raster_bwd_kernel(RasterBwdArgs a) {
       if constexpr (COUNT) {
 #pragma unroll
         for (int k = 0; k < PIX; ++k) evals += idx <= px_s[k].bin_final;
+        ++steps;
       }
       if (fabsf(r0.x - wcx) > r2.z + 7.5f || fabsf(r0.y - wcy) > r2.w + kHalfY) continue;
+      if constexpr (COUNT) ++steps_uncull;
       const float4 r1 = s_r1[t];
       const float dx = r0.x - px;
       const float dy0 = r0.y - py0;
@@ -215,6 +218,7 @@ raster_bwd_kernel(RasterBwdArgs a) {
         any |= c;
       }
       if (__ballot_sync(0xffffffffu, any) == 0u) continue;
+      if constexpr (COUNT) ++steps_active;
       // per-thread cotangents: sum_px v_sigma (dx, dy) and the second moments give the conic
       // and xy terms; (a, b, c) = -ln2 (2 qa, qb, 2 qc) recovers the unscaled conic
       const float sx = acc[3] * dx, sy = acc[4];
@@ -243,6 +247,9 @@ raster_bwd_kernel(RasterBwdArgs a) {
     if (lane == 0) {
       atomicAdd(&a.work[0], evals);
       atomicAdd(&a.work[1], contribs);
+      atomicAdd(&a.work[2], static_cast<unsigned long long>(steps));
+      atomicAdd(&a.work[3], static_cast<unsigned long long>(steps_uncull));
+      atomicAdd(&a.work[4], static_cast<unsigned long long>(steps_active));
     }
   }
 }

@@ -176,9 +176,6 @@ pair_prep_kernel(PairKeyArgs a, K* keys, int32_t* vals) {
 // (bounded spin).
 constexpr int kScanThreads = 256;
 constexpr int kScanItems = 8;
-constexpr unsigned long long kScanAgg = 1ull << 62;
-constexpr unsigned long long kScanInc = 2ull << 62;
-constexpr unsigned long long kScanMask = (1ull << 62) - 1;
 
 __global__ void __launch_bounds__(kScanThreads)
 sorted_offsets_kernel(const int32_t* __restrict__ perm, const int32_t* __restrict__ counts,
@@ -212,33 +209,19 @@ sorted_offsets_kernel(const int32_t* __restrict__ perm, const int32_t* __restric
   __syncthreads();
   long long wpre = 0;
   for (int w = 0; w < warp; ++w) wpre += s_warp[w];
-  if (threadIdx.x == 0) {
+  if (warp == 0) {
     long long agg = 0;
     for (int w = 0; w < kScanThreads / 32; ++w) agg += s_warp[w];
     long long prefix = 0;
     if (tile == 0) {
-      st_relaxed(&status[0], kScanInc | static_cast<unsigned long long>(agg));
+      if (lane == 0) st_relaxed(&status[0], kLookbackInc | static_cast<unsigned long long>(agg));
     } else {
-      st_relaxed(&status[tile], kScanAgg | static_cast<unsigned long long>(agg));
-      int64_t j = tile - 1;
-      long long spins = 0;
-      while (j >= 0) {
-        const unsigned long long s = ld_relaxed(&status[j]);
-        const unsigned long long flag = s & ~kScanMask;
-        if (flag == 0) {
-          if (++spins > kSpinLimit) {
-            atomicOr(err, kErrLookbackTimeout);
-            break;
-          }
-          continue;
-        }
-        prefix += static_cast<long long>(s & kScanMask);
-        if (flag == kScanInc) break;
-        --j;
-      }
-      st_relaxed(&status[tile], kScanInc | static_cast<unsigned long long>(prefix + agg));
+      if (lane == 0) st_relaxed(&status[tile], kLookbackAgg | static_cast<unsigned long long>(agg));
+      prefix = warp_lookback(status, tile, err);
+      if (lane == 0)
+        st_relaxed(&status[tile], kLookbackInc | static_cast<unsigned long long>(prefix + agg));
     }
-    s_prefix = prefix;
+    if (lane == 0) s_prefix = prefix;
   }
   __syncthreads();
   long long run = s_prefix + wpre + inc - tsum;
@@ -326,9 +309,6 @@ constexpr int kItems32 = 8;  // 4096 keys per tile for 32-bit keys
 constexpr int kItems64 = 6;  // 3072 keys per tile for 64-bit keys
 constexpr int kHistThreads = 256;
 constexpr int kHistItems = 32;
-constexpr unsigned long long kFlagAgg = 1ull << 62;
-constexpr unsigned long long kFlagInc = 2ull << 62;
-constexpr unsigned long long kValMask = (1ull << 62) - 1;
 
 template <typename K>
 __global__ void __launch_bounds__(kHistThreads)
@@ -442,14 +422,14 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
     }
     unsigned long long* st = status + tile * 256 + dg;
     if (tile == 0) {
-      st_relaxed(st, kFlagInc | sum);
+      st_relaxed(st, kLookbackInc | sum);
     } else {
-      st_relaxed(st, kFlagAgg | sum);
+      st_relaxed(st, kLookbackAgg | sum);
       int64_t j = tile - 1;
       long long spins = 0;
       while (j >= 0) {
         const unsigned long long s = ld_relaxed(status + j * 256 + dg);
-        const unsigned long long flag = s & ~kValMask;
+        const unsigned long long flag = s & ~kLookbackMask;
         if (flag == 0) {
           if (++spins > kSpinLimit) {
             atomicOr(err, kErrLookbackTimeout);
@@ -457,11 +437,11 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
           }
           continue;
         }
-        prefix += static_cast<long long>(s & kValMask);
-        if (flag == kFlagInc) break;
+        prefix += static_cast<long long>(s & kLookbackMask);
+        if (flag == kLookbackInc) break;
         --j;
       }
-      st_relaxed(st, kFlagInc | (static_cast<unsigned long long>(prefix) + sum));
+      st_relaxed(st, kLookbackInc | (static_cast<unsigned long long>(prefix) + sum));
     }
   }
   const uint32_t excl = block_exclusive_scan<NT>(sum, s_warp);
