@@ -185,6 +185,17 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// Packed fp32x2 arithmetic (sm_100 FFMA2 / FMUL2 / FADD2): two lanes of IEEE round-to-nearest
+// math per instruction, each lane bit-identical to the scalar fmaf / * / +.
+__device__ __forceinline__ float2 splat2(float s) { return make_float2(s, s); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+// 1 - a, rounded once (fma(a, -1, 1) is the exact difference rounded like 1.0f - a)
+__device__ __forceinline__ float2 one_minus2(float2 a) {
+  return __ffma2_rn(a, make_float2(-1.0f, -1.0f), make_float2(1.0f, 1.0f));
+}
+
 // log2(e) / 2 and log2(e), the scales of the staged conic q = -(log2 e / 2) * (a, 2b, c)
 constexpr float kHalfLog2e = 0.721347520444482f;
 constexpr float kLog2e = 1.442695040888963f;

@@ -3,12 +3,13 @@
 // (:1212-1302).
 //
 // Recompute-style: one 64-thread CTA per (output image, tile); each warp owns a 16x8 block and
-// each thread four vertically adjacent pixels. A warp skips every gaussian whose alpha >= 1/255
-// ellipse misses its block (those evaluations are all rejected). The walk runs back to front from the block's largest
+// each thread four vertically adjacent pixels, advanced as two pairs with packed fp32x2
+// instructions. A warp skips every gaussian whose alpha >= 1/255 ellipse misses its block
+// (those evaluations are all rejected). The walk runs back to front from the block's largest
 // final_idx over batches of 256 records staged in shared memory (plus the flat ids that
 // address the gradients). Each pixel rebuilds T by dividing out (1 - alpha), and only entries
 // at or below its own final_idx count. All lanes of a warp visit the same entry together, so
-// each thread first adds its two pixels' cotangents, then the warp sums the 9 (10 with depth)
+// each thread first adds its four pixels' cotangents, then the warp sums the 9 (10 with depth)
 // per-gaussian values with one reduce-scatter (~K shuffles instead of 5K) and issues ONE atomic
 // instruction across K lanes. Warps where no pixel contributes skip the reduction.
 //
@@ -22,61 +23,77 @@ namespace {
 
 constexpr float kLn2 = 0.693147180559945f;
 
-struct BwdPixel {
-  int32_t bin_final;
-  float T, vo0, vo1, vo2, vod;
-  float tb;            // t_final * (background . v_out): the background's share of v_alpha
-  float bufdot = 0.0f; // (colour, depth) accumulated behind this gaussian, dotted with v_out
+// Two vertically adjacent pixels of one thread, advanced in lock-step with packed fp32x2 math.
+struct BwdPair {
+  int32_t bf0, bf1;  // bin_final of each pixel
+  float2 T, vo0, vo1, vo2, vod;
+  float2 tb;      // t_final * (background . v_out): the background's share of v_alpha
+  float2 bufdot;  // (colour, depth) accumulated behind this gaussian, dotted with v_out
 };
 
-// Accumulators of one thread for the current gaussian, over its two pixels:
-// [0..2] colour, [3] sum v_sigma, [4] sum v_sigma dy, [5] sum v_sigma dy^2, [6] opacity,
-// [7] depth. The xy and conic cotangents are formed from these once per thread.
-//
-// _blend_color_vjp (splax/_rasterize/_kernels.py:1212-1254) restated with the colour buffer
-// kept as its dot product with v_out: v_alpha = T (c . v_out) - ra (buf . v_out + t_final
+// Per-thread sums for the current gaussian, lane-wise over a pixel pair (the two lanes are
+// added once per gaussian): colour cotangents, w = ovm * v_alpha and its dy moments, depth.
+// v_sigma = -w, so sum v_sigma = -sum w, and the opacity cotangent sum vis * v_alpha is
+// sum w / opacity (ov = opacity * vis; both use the same clamp mask).
+struct BwdAcc {
+  float2 c0, c1, c2, w, wy, wyy, d;
+};
+
+// _blend_color_vjp (splax/_rasterize/_kernels.py:1212-1254) for a pixel pair, branch-free:
+// a pixel that does not take part (entry past its final_idx, sigma < 0, alpha < 1/255) gets
+// alpha 0, leaves T and the colour buffer unchanged and adds exact zeros. The colour buffer
+// is kept as its dot product with v_out: v_alpha = T (c . v_out) - ra (buf . v_out + t_final
 // bg . v_out), and buf . v_out grows by (c . v_out) fac.
-template <bool DEPTH>
-__device__ __forceinline__ bool vjp_one(BwdPixel& s, int32_t idx, float p, float dy, float opac,
-                                        float r, float g, float b, float depth, float* acc) {
-  if (idx > s.bin_final || p > 0.0f) return false;
-  const float vis = ex2_approx(p);
-  const float ov = opac * vis;
-  const float alpha = fminf(kAlphaMax, ov);
-  if (alpha < kAlphaThreshold) return false;
-  const float ra = __fdividef(1.0f, 1.0f - alpha);
-  s.T = s.T * ra;
-  const float fac = alpha * s.T;
-  acc[0] += s.vo0 * fac;
-  acc[1] += s.vo1 * fac;
-  acc[2] += s.vo2 * fac;
-  float cv = r * s.vo0 + g * s.vo1 + b * s.vo2;
+template <bool DEPTH, bool COUNT>
+__device__ __forceinline__ bool vjp_pair(BwdPair& s, int32_t idx, float2 p, float2 dy,
+                                         float2 opac, float2 r, float2 g, float2 b, float2 depth,
+                                         BwdAcc& acc, unsigned long long& contribs) {
+  const float2 vis = make_float2(ex2_approx(p.x), ex2_approx(p.y));
+  const float2 ov = mul2(opac, vis);
+  const float a0 = fminf(kAlphaMax, ov.x), a1 = fminf(kAlphaMax, ov.y);
+  const bool v0 = idx <= s.bf0 && !(p.x > 0.0f) && !(a0 < kAlphaThreshold);
+  const bool v1 = idx <= s.bf1 && !(p.y > 0.0f) && !(a1 < kAlphaThreshold);
+  if constexpr (COUNT) contribs += static_cast<unsigned>(v0) + static_cast<unsigned>(v1);
+  const float2 am = make_float2(v0 ? a0 : 0.0f, v1 ? a1 : 0.0f);
+  const float2 om = one_minus2(am);
+  const float2 ra = make_float2(__fdividef(1.0f, om.x), __fdividef(1.0f, om.y));
+  const float2 Tn = mul2(s.T, ra);
+  s.T = make_float2(v0 ? Tn.x : s.T.x, v1 ? Tn.y : s.T.y);
+  const float2 fac = mul2(am, s.T);
+  acc.c0 = fma2(s.vo0, fac, acc.c0);
+  acc.c1 = fma2(s.vo1, fac, acc.c1);
+  acc.c2 = fma2(s.vo2, fac, acc.c2);
+  float2 cv = mul2(r, s.vo0);
+  cv = fma2(g, s.vo1, cv);
+  cv = fma2(b, s.vo2, cv);
   if constexpr (DEPTH) {
-    cv += depth * s.vod;
-    acc[7] += s.vod * fac;
+    cv = fma2(depth, s.vod, cv);
+    acc.d = fma2(s.vod, fac, acc.d);
   }
-  const float v_alpha = s.T * cv - ra * (s.bufdot + s.tb);
-  s.bufdot += cv * fac;
+  const float2 rb = mul2(ra, add2(s.bufdot, s.tb));
+  const float2 va = fma2(s.T, cv, make_float2(-rb.x, -rb.y));
+  s.bufdot = fma2(cv, fac, s.bufdot);
   // where the 0.999 clamp is active alpha is constant: no sigma or opacity cotangent
-  const bool live = ov <= kAlphaMax;
-  const float vs = live ? -ov * v_alpha : 0.0f;
-  acc[6] += live ? vis * v_alpha : 0.0f;
-  acc[3] += vs;
-  const float vsy = vs * dy;
-  acc[4] += vsy;
-  acc[5] += vsy * dy;
-  return true;
+  const float2 ovm = make_float2(v0 && ov.x <= kAlphaMax ? ov.x : 0.0f,
+                                 v1 && ov.y <= kAlphaMax ? ov.y : 0.0f);
+  const float2 w = mul2(ovm, va);
+  acc.w = add2(acc.w, w);
+  const float2 wy = mul2(w, dy);
+  acc.wy = add2(acc.wy, wy);
+  acc.wyy = fma2(wy, dy, acc.wyy);
+  return v0 || v1;
 }
 
-// PIX vertically adjacent pixels per thread; a warp owns a 16 x (2 PIX) block of the tile and
-// the CTA (256 / PIX threads) the whole tile. Four pixels per thread amortise the per-gaussian
-// warp reduction over 128 pixels.
+// Four vertically adjacent pixels per thread (two packed pairs); a warp owns a 16x8 block of
+// the tile and the 64-thread CTA the whole tile. Four pixels per thread amortise the
+// per-gaussian warp reduction over 128 pixels.
 constexpr int kPixels = 4;
+constexpr int kPairs = kPixels / 2;
 
-template <bool DEPTH, bool COUNT, int PIX>
-__global__ void __launch_bounds__(kBlockSize / PIX)
+template <bool DEPTH, bool COUNT>
+__global__ void __launch_bounds__(kBlockSize / kPixels)
 raster_bwd_kernel(RasterBwdArgs a) {
-  constexpr int kBwdThreads = kBlockSize / PIX;
+  constexpr int kBwdThreads = kBlockSize / kPixels;
   constexpr int K = DEPTH ? 10 : 9;
   unsigned long long evals = 0, contribs = 0;
   unsigned steps = 0, steps_uncull = 0, steps_active = 0;  // warp steps (COUNT builds only)
@@ -99,38 +116,48 @@ raster_bwd_kernel(RasterBwdArgs a) {
   const int tr = threadIdx.x, lane = tr & 31, warp = tr >> 5;
   const int32_t tile_x = tile_local % a.tbx, tile_y = tile_local / a.tbx;
   const int32_t j = tile_x * kBlockWidth + (lane & 15);
-  const int32_t i0 = tile_y * kBlockWidth + 2 * PIX * warp + PIX * (lane >> 4);
+  const int32_t i0 = tile_y * kBlockWidth + 2 * kPixels * warp + kPixels * (lane >> 4);
   const float px = static_cast<float>(j) + 0.5f;
   const float py0 = static_cast<float>(i0) + 0.5f;
-  // centre of the warp's block of pixel centres (half-extents 7.5 and PIX - 0.5)
+  // centre of the warp's block of pixel centres (half-extents 7.5 and kPixels - 0.5)
   const float wcx = static_cast<float>(tile_x * kBlockWidth) + 8.0f;
-  const float wcy = static_cast<float>(tile_y * kBlockWidth + 2 * PIX * warp + PIX);
-  constexpr float kHalfY = PIX - 0.5f;
+  const float wcy = static_cast<float>(tile_y * kBlockWidth + 2 * kPixels * warp + kPixels);
+  constexpr float kHalfY = kPixels - 0.5f;
 
-  BwdPixel px_s[PIX];
+  BwdPair pr[kPairs];
   const float* bg = a.background + 3 * (a.sel_bg ? image_id : 0);
+  const float bg0 = bg[0], bg1 = bg[1], bg2 = bg[2];
+  int32_t tmax = range_start - 1;
 #pragma unroll
-  for (int k = 0; k < PIX; ++k) {
-    BwdPixel& s = px_s[k];
+  for (int k = 0; k < kPixels; ++k) {
     const int32_t i = i0 + k;
-    s.bin_final = range_start - 1;
-    s.T = 1.0f;
-    s.vo0 = s.vo1 = s.vo2 = s.vod = s.tb = 0.0f;
+    int32_t bf = range_start - 1;
+    float T = 1.0f, vo0 = 0.0f, vo1 = 0.0f, vo2 = 0.0f, vod = 0.0f, tb = 0.0f;
     if (i < a.img_h && j < a.img_w) {
       const int64_t fpix = (geom_image * a.img_h + i) * static_cast<int64_t>(a.img_w) + j;
-      s.bin_final = min(a.final_idx[fpix], range_end - 1);
-      const float t_final = a.final_Ts[fpix];
-      s.T = t_final;
+      bf = min(a.final_idx[fpix], range_end - 1);
+      T = a.final_Ts[fpix];
       const int64_t vrow = (image_id * a.img_h + i) % a.vout_rows;
       const float* vo = a.v_out_img + 3 * (vrow * a.img_w + j);
-      s.vo0 = vo[0];
-      s.vo1 = vo[1];
-      s.vo2 = vo[2];
+      vo0 = vo[0];
+      vo1 = vo[1];
+      vo2 = vo[2];
       if constexpr (DEPTH) {
         const int64_t drow = (image_id * a.img_h + i) % a.vdepth_rows;
-        s.vod = a.v_out_depth[drow * a.img_w + j];
+        vod = a.v_out_depth[drow * a.img_w + j];
       }
-      s.tb = t_final * (bg[0] * s.vo0 + bg[1] * s.vo1 + bg[2] * s.vo2);
+      tb = T * (bg0 * vo0 + bg1 * vo1 + bg2 * vo2);
+    }
+    tmax = max(tmax, bf);
+    BwdPair& q = pr[k >> 1];
+    if (k & 1) {
+      q.bf1 = bf;
+      q.T.y = T; q.vo0.y = vo0; q.vo1.y = vo1; q.vo2.y = vo2; q.vod.y = vod; q.tb.y = tb;
+      q.bufdot.y = 0.0f;
+    } else {
+      q.bf0 = bf;
+      q.T.x = T; q.vo0.x = vo0; q.vo1.x = vo1; q.vo2.x = vo2; q.vod.x = vod; q.tb.x = tb;
+      q.bufdot.x = 0.0f;
     }
   }
 
@@ -152,9 +179,6 @@ raster_bwd_kernel(RasterBwdArgs a) {
   }
 
   // walk starts at the block maximum of final_idx
-  int32_t tmax = px_s[0].bin_final;
-#pragma unroll
-  for (int k = 1; k < PIX; ++k) tmax = max(tmax, px_s[k].bin_final);
   const int32_t wmax = __reduce_max_sync(0xffffffffu, tmax);
   if (lane == 0) s_wmax[warp] = wmax;
   __syncthreads();
@@ -163,9 +187,9 @@ raster_bwd_kernel(RasterBwdArgs a) {
   for (int w = 1; w < kBwdThreads / 32; ++w) start_idx = max(start_idx, s_wmax[w]);
   const int32_t num_batches = (start_idx - range_start + kBlockSize) / kBlockSize;
 
-  for (int32_t b = 0; b < num_batches; ++b) {
+  for (int32_t bt = 0; bt < num_batches; ++bt) {
     __syncthreads();  // previous batch's shared reads are complete
-    const int32_t batch_end = start_idx - b * kBlockSize;
+    const int32_t batch_end = start_idx - bt * kBlockSize;
 #pragma unroll
     for (int h = 0; h < kBlockSize / kBwdThreads; ++h) {
       const int slot = tr + h * kBwdThreads;
@@ -196,44 +220,45 @@ raster_bwd_kernel(RasterBwdArgs a) {
       const float4 r2 = s_r2[t];
       if constexpr (COUNT) {
 #pragma unroll
-        for (int k = 0; k < PIX; ++k) evals += idx <= px_s[k].bin_final;
+        for (int q = 0; q < kPairs; ++q)
+          evals += static_cast<unsigned>(idx <= pr[q].bf0) + static_cast<unsigned>(idx <= pr[q].bf1);
         ++steps;
       }
       if (fabsf(r0.x - wcx) > r2.z + 7.5f || fabsf(r0.y - wcy) > r2.w + kHalfY) continue;
       if constexpr (COUNT) ++steps_uncull;
-      const float4 r1 = s_r1[t];
+      const float4 r1 = s_r1[t];  // qc, opacity, r, g
       const float dx = r0.x - px;
       const float dy0 = r0.y - py0;
-      const float qxx = r0.z * dx * dx, qbx = r0.w * dx;
-      float acc[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) acc[k] = 0.0f;
+      const float2 qxx = splat2(r0.z * dx * dx), qbx = splat2(r0.w * dx), qc = splat2(r1.x);
+      const float2 opac = splat2(r1.y), cr = splat2(r1.z), cg = splat2(r1.w),
+                   cb = splat2(r2.x), cd = splat2(r2.y);
+      BwdAcc acc;
+      acc.c0 = acc.c1 = acc.c2 = acc.w = acc.wy = acc.wyy = acc.d = make_float2(0.0f, 0.0f);
       bool any = false;
 #pragma unroll
-      for (int k = 0; k < PIX; ++k) {
-        const float dy = dy0 - static_cast<float>(k);
-        const float p = fmaf(fmaf(r1.x, dy, qbx), dy, qxx);
-        const bool c = vjp_one<DEPTH>(px_s[k], idx, p, dy, r1.y, r1.z, r1.w, r2.x, r2.y, acc);
-        if constexpr (COUNT) contribs += c;
-        any |= c;
+      for (int q = 0; q < kPairs; ++q) {
+        const float2 dy = add2(splat2(dy0), make_float2(-2.0f * q, -2.0f * q - 1.0f));
+        const float2 p = fma2(fma2(qc, dy, qbx), dy, qxx);
+        any |= vjp_pair<DEPTH, COUNT>(pr[q], idx, p, dy, opac, cr, cg, cb, cd, acc, contribs);
       }
       if (__ballot_sync(0xffffffffu, any) == 0u) continue;
       if constexpr (COUNT) ++steps_active;
-      // per-thread cotangents: sum_px v_sigma (dx, dy) and the second moments give the conic
-      // and xy terms; (a, b, c) = -ln2 (2 qa, qb, 2 qc) recovers the unscaled conic
-      const float sx = acc[3] * dx, sy = acc[4];
-      const float a2 = -2.0f * kLn2 * r0.z, bq = -kLn2 * r0.w, c2 = -2.0f * kLn2 * r1.x;
+      // per-thread cotangents from the sums (v_sigma = -w): the conic and xy terms use the
+      // second moments; (a, b, c) = -ln2 (2 qa, qb, 2 qc) recovers the unscaled conic
+      const float W = acc.w.x + acc.w.y, WY = acc.wy.x + acc.wy.y, WYY = acc.wyy.x + acc.wyy.y;
+      const float sxn = W * dx;  // -sum v_sigma dx
+      const float a2n = 2.0f * kLn2 * r0.z, bqn = kLn2 * r0.w, c2n = 2.0f * kLn2 * r1.x;
       float v[K];
-      v[0] = acc[0];
-      v[1] = acc[1];
-      v[2] = acc[2];
-      v[3] = 0.5f * sx * dx;
-      v[4] = sy * dx;
-      v[5] = 0.5f * acc[5];
-      v[6] = fmaf(a2, sx, bq * sy);
-      v[7] = fmaf(bq, sx, c2 * sy);
-      v[8] = acc[6];
-      if constexpr (DEPTH) v[9] = acc[7];
+      v[0] = acc.c0.x + acc.c0.y;
+      v[1] = acc.c1.x + acc.c1.y;
+      v[2] = acc.c2.x + acc.c2.y;
+      v[3] = -0.5f * sxn * dx;
+      v[4] = -WY * dx;
+      v[5] = -0.5f * WYY;
+      v[6] = fmaf(a2n, sxn, bqn * WY);
+      v[7] = fmaf(bqn, sxn, c2n * WY);
+      v[8] = __fdividef(W, r1.y);  // opacity > 0 whenever a lane of the warp contributes
+      if constexpr (DEPTH) v[9] = acc.d.x + acc.d.y;
       warp_reduce_scatter<K>(v, lane);
       if (my_base != nullptr && v[0] != 0.0f) {
         const int64_t og = og_base + s_id[t];
@@ -254,15 +279,14 @@ raster_bwd_kernel(RasterBwdArgs a) {
   }
 }
 
-template <int PIX>
 void launch_bwd(const RasterBwdArgs& a, unsigned g, cudaStream_t stream) {
-  constexpr int nt = kBlockSize / PIX;
+  constexpr int nt = kBlockSize / kPixels;
   if (a.v_out_depth) {
-    if (a.work) raster_bwd_kernel<true, true, PIX><<<g, nt, 0, stream>>>(a);
-    else raster_bwd_kernel<true, false, PIX><<<g, nt, 0, stream>>>(a);
+    if (a.work) raster_bwd_kernel<true, true><<<g, nt, 0, stream>>>(a);
+    else raster_bwd_kernel<true, false><<<g, nt, 0, stream>>>(a);
   } else {
-    if (a.work) raster_bwd_kernel<false, true, PIX><<<g, nt, 0, stream>>>(a);
-    else raster_bwd_kernel<false, false, PIX><<<g, nt, 0, stream>>>(a);
+    if (a.work) raster_bwd_kernel<false, true><<<g, nt, 0, stream>>>(a);
+    else raster_bwd_kernel<false, false><<<g, nt, 0, stream>>>(a);
   }
 }
 
@@ -272,7 +296,7 @@ void launch_raster_bwd(const RasterBwdArgs& a, cudaStream_t stream) {
   const int64_t blocks = a.B_out * a.num_tiles;
   if (blocks == 0) return;
   const unsigned g = static_cast<unsigned>(blocks);
-  launch_bwd<kPixels>(a, g, stream);
+  launch_bwd(a, g, stream);
 }
 
 }  // namespace splax

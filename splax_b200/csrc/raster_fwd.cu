@@ -3,7 +3,8 @@
 //
 // One 64-thread CTA per (image, 16x16 tile); each warp owns a 16x8 block of the tile and each
 // thread four vertically adjacent pixels, so every shared-memory record read and the x-terms of
-// the Gaussian exponent serve four evaluations. The tile's sorted list is walked in batches of
+// the Gaussian exponent serve four evaluations; the exponents are computed as two pairs with
+// packed fp32x2 instructions, the blend step per pixel (branches skip finished pixels). The tile's sorted list is walked in batches of
 // 256: the CTA
 // gathers the packed 48-byte records (three 16-byte loads each, written by the emission pass)
 // into shared memory, then blends the batch front to back from shared memory with broadcast
@@ -26,11 +27,14 @@ struct PixelState {
   bool done;
 };
 
+// The reference blend step (splax/_rasterize/_kernels.py:185-197) for one pixel.
 template <bool DEPTH, bool COUNT>
 __device__ __forceinline__ void blend_one(PixelState& s, float p, float opac, float r, float g,
                                           float b, float depth, int32_t idx,
+                                          unsigned long long& evals,
                                           unsigned long long& contribs) {
   if (s.done) return;
+  if constexpr (COUNT) ++evals;
   const float alpha = fminf(kAlphaMax, opac * ex2_approx(p));
   if (p > 0.0f || alpha < kAlphaThreshold) return;
   const float next_T = s.T * (1.0f - alpha);
@@ -48,14 +52,15 @@ __device__ __forceinline__ void blend_one(PixelState& s, float p, float opac, fl
   if constexpr (COUNT) ++contribs;
 }
 
-// PIX vertically adjacent pixels per thread; a warp owns a 16 x (2 PIX) block of the tile and
-// the CTA (256 / PIX threads) the whole tile.
-constexpr int kPixels = 4;  // pixels per thread: 64 threads per tile
+// Four vertically adjacent pixels per thread (exponents computed as two packed pairs); a warp
+// owns a 16x8 block of the tile and the 64-thread CTA the whole tile.
+constexpr int kPixels = 4;
+constexpr int kPairs = kPixels / 2;
 
-template <bool DEPTH, bool COUNT, int PIX>
-__global__ void __launch_bounds__(kBlockSize / PIX)
+template <bool DEPTH, bool COUNT>
+__global__ void __launch_bounds__(kBlockSize / kPixels)
 raster_fwd_kernel(RasterFwdArgs a) {
-  constexpr int kFwdThreads = kBlockSize / PIX;
+  constexpr int kFwdThreads = kBlockSize / kPixels;
   unsigned long long evals = 0, contribs = 0;
   __shared__ float4 s_r0[kBlockSize];
   __shared__ float4 s_r1[kBlockSize];
@@ -66,23 +71,23 @@ raster_fwd_kernel(RasterFwdArgs a) {
   const int32_t tile_x = tile_local % a.tbx, tile_y = tile_local / a.tbx;
   const int tr = threadIdx.x, lane = tr & 31, warp = tr >> 5;
   const int32_t j = tile_x * kBlockWidth + (lane & 15);
-  const int32_t i0 = tile_y * kBlockWidth + 2 * PIX * warp + PIX * (lane >> 4);
+  const int32_t i0 = tile_y * kBlockWidth + 2 * kPixels * warp + kPixels * (lane >> 4);
   const float px = static_cast<float>(j) + 0.5f;
   const float py0 = static_cast<float>(i0) + 0.5f;
-  PixelState st[PIX];
+  PixelState st[kPixels];
   bool all_done = true;
 #pragma unroll
-  for (int k = 0; k < PIX; ++k) {
+  for (int k = 0; k < kPixels; ++k) {
     st[k].done = !(i0 + k < a.img_h && j < a.img_w);
     all_done &= st[k].done;
   }
   const int2 range = reinterpret_cast<const int2*>(a.tile_bins)[tile_g];
   const int32_t range_start = range.x, range_end = range.y;
   const int32_t num_batches = (range_end - range_start + kBlockSize - 1) / kBlockSize;
-  for (int32_t b = 0; b < num_batches; ++b) {
+  for (int32_t bt = 0; bt < num_batches; ++bt) {
     // block vote doubles as the barrier protecting the previous batch's shared reads
     if (__syncthreads_count(all_done) >= kFwdThreads) break;
-    const int32_t batch_start = range_start + b * kBlockSize;
+    const int32_t batch_start = range_start + bt * kBlockSize;
 #pragma unroll
     for (int h = 0; h < kBlockSize / kFwdThreads; ++h) {
       const int slot = tr + h * kFwdThreads;
@@ -111,16 +116,19 @@ raster_fwd_kernel(RasterFwdArgs a) {
         const float2 r2 = s_r2[t];  // b, depth
         const float dx = r0.x - px;
         const float dy0 = r0.y - py0;
-        const float qxx = r0.z * dx * dx, qbx = r0.w * dx;
+        const float2 qxx = splat2(r0.z * dx * dx), qbx = splat2(r0.w * dx), qc = splat2(r1.x);
         const int32_t idx = batch_start + t;
         all_done = true;
 #pragma unroll
-        for (int k = 0; k < PIX; ++k) {
-          if constexpr (COUNT) evals += !st[k].done;
-          const float dy = dy0 - static_cast<float>(k);
-          const float p = fmaf(fmaf(r1.x, dy, qbx), dy, qxx);
-          blend_one<DEPTH, COUNT>(st[k], p, r1.y, r1.z, r1.w, r2.x, r2.y, idx, contribs);
-          all_done &= st[k].done;
+        for (int q = 0; q < kPairs; ++q) {
+          // the exponents of a pixel pair in packed form, then the branchy per-pixel step
+          const float2 dy = add2(splat2(dy0), make_float2(-2.0f * q, -2.0f * q - 1.0f));
+          const float2 p = fma2(fma2(qc, dy, qbx), dy, qxx);
+          blend_one<DEPTH, COUNT>(st[2 * q], p.x, r1.y, r1.z, r1.w, r2.x, r2.y, idx, evals,
+                                  contribs);
+          blend_one<DEPTH, COUNT>(st[2 * q + 1], p.y, r1.y, r1.z, r1.w, r2.x, r2.y, idx, evals,
+                                  contribs);
+          all_done &= st[2 * q].done && st[2 * q + 1].done;
         }
         if (all_done) break;
       }
@@ -137,7 +145,7 @@ raster_fwd_kernel(RasterFwdArgs a) {
   const float* bg = a.background + 3 * (a.sel_bg ? image_id : 0);
   const float bg0 = bg[0], bg1 = bg[1], bg2 = bg[2];
 #pragma unroll
-  for (int k = 0; k < PIX; ++k) {
+  for (int k = 0; k < kPixels; ++k) {
     const PixelState& s = st[k];
     const int32_t i = i0 + k;
     if (!(i < a.img_h && j < a.img_w)) continue;
@@ -151,15 +159,14 @@ raster_fwd_kernel(RasterFwdArgs a) {
   }
 }
 
-template <int PIX>
 void launch_fwd(const RasterFwdArgs& a, unsigned g, cudaStream_t stream) {
-  constexpr int nt = kBlockSize / PIX;
+  constexpr int nt = kBlockSize / kPixels;
   if (a.out_depth) {
-    if (a.work) raster_fwd_kernel<true, true, PIX><<<g, nt, 0, stream>>>(a);
-    else raster_fwd_kernel<true, false, PIX><<<g, nt, 0, stream>>>(a);
+    if (a.work) raster_fwd_kernel<true, true><<<g, nt, 0, stream>>>(a);
+    else raster_fwd_kernel<true, false><<<g, nt, 0, stream>>>(a);
   } else {
-    if (a.work) raster_fwd_kernel<false, true, PIX><<<g, nt, 0, stream>>>(a);
-    else raster_fwd_kernel<false, false, PIX><<<g, nt, 0, stream>>>(a);
+    if (a.work) raster_fwd_kernel<false, true><<<g, nt, 0, stream>>>(a);
+    else raster_fwd_kernel<false, false><<<g, nt, 0, stream>>>(a);
   }
 }
 
@@ -169,7 +176,7 @@ void launch_raster_fwd(const RasterFwdArgs& a, cudaStream_t stream) {
   const int64_t blocks = a.num_images * a.num_tiles;
   if (blocks == 0) return;
   const unsigned g = static_cast<unsigned>(blocks);
-  launch_fwd<kPixels>(a, g, stream);
+  launch_fwd(a, g, stream);
 }
 
 }  // namespace splax
