@@ -9,7 +9,7 @@
 //                  (_kernels.py:76-211), writing (image | tile) bin keys and flat ids, and
 //                  packing the pair's blend record (xy, conic, opacity, colour, depth).
 //  radix sort      stable LSD onesweep (used for both sorts): one upfront histogram pass, then one
-//                  kernel per 8-bit digit that ranks keys with warp ballots, resolves the
+//                  kernel per 8-bit digit that ranks keys with warp match groups, resolves the
 //                  tile's global digit offsets by a decoupled look-back (bounded spin) and
 //                  scatters through shared memory so the global writes coalesce per digit.
 //                  Only the significant key bits are sorted.
@@ -305,8 +305,8 @@ __global__ void reference_keys_kernel(const uint32_t* __restrict__ bin_keys,
 
 // ------------------------------------------------------------------ onesweep radix sort
 constexpr int kSortThreads = 512;
-constexpr int kItems32 = 8;  // 4096 keys per tile for 32-bit keys
-constexpr int kItems64 = 6;  // 3072 keys per tile for 64-bit keys
+constexpr int kItems32 = 12;  // 6144 keys per tile for 32-bit keys
+constexpr int kItems64 = 8;   // 4096 keys per tile for 64-bit keys
 constexpr int kHistThreads = 256;
 constexpr int kHistItems = 32;
 
@@ -394,19 +394,21 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
     k[it] = valid ? kin[base + pos] : K(0);
     val[it] = valid ? vin[base + pos] : 0;
   }
-  // stable warp-level ranking: keys of one digit keep their input order (iteration, lane)
+  // stable warp-level ranking: keys of one digit keep their input order (iteration, lane).
+  // The lowest lane of each digit group adds the group's size to the warp's counter with one
+  // shared atomic and broadcasts the old value; the atomics of successive iterations are
+  // independent instructions executed in order, so the iterations pipeline.
 #pragma unroll
   for (int it = 0; it < ITEMS; ++it) {
     const int pos = warp_base + it * 32 + lane;
     const bool valid = pos < nvalid;
     const uint32_t d = static_cast<uint32_t>(static_cast<uint64_t>(k[it]) >> shift) & 255u;
     const unsigned peers = __match_any_sync(0xffffffffu, valid ? d : 256u + lane);
-    const uint32_t lt = __popc(peers & lt_mask);
-    const uint32_t prev = valid ? s_wh[warp][d] : 0u;
-    __syncwarp();
-    if (valid && lt == 0) s_wh[warp][d] = prev + __popc(peers);
-    __syncwarp();
-    rank[it] = prev + lt;
+    const int leader = __ffs(peers) - 1;
+    uint32_t prev = 0;
+    if (valid && lane == leader) prev = atomicAdd(&s_wh[warp][d], __popc(peers));
+    prev = __shfl_sync(0xffffffffu, prev, leader);
+    rank[it] = prev + __popc(peers & lt_mask);
   }
   __syncthreads();
   // per digit (threads 0..255): warp exclusive offsets, the block's count, the look-back
