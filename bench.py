@@ -197,14 +197,14 @@ def main() -> None:
     kw = dict(background=bg, img_shape=(H, W), f=(f, f))
     denom = float(B * H * W * 3)
 
-    def step(vm, tgt):
-        for p in params:
+    def step(vm, tgt, ps=params):
+        for p in ps:
             p.grad = None
-        imgs, _ = sx.render(*params, viewmat=vm, **kw)
-        loss = ((imgs - tgt) ** 2).sum() / denom
+        imgs, _ = sx.render(*ps, viewmat=vm, **kw)
+        loss = sx.mse_loss(imgs, tgt, denom=denom)
         loss.backward()
         if world > 1:
-            flat = torch.cat([p.grad.reshape(-1) for p in params])
+            flat = torch.cat([p.grad.reshape(-1) for p in ps])
             dist.all_reduce(flat)
             dist.all_reduce(loss.detach())
         return loss
@@ -256,42 +256,69 @@ def main() -> None:
     work = _lib.profile_report()["units"]
     _lib.profile_enable(timing=False, count_work=False)
 
-    # end to end through the public API from pinned host buffers
+    # end to end through the public API from pinned host buffers. Every step copies its inputs
+    # (the five parameter arrays, its cameras and its target images) from pinned host memory
+    # and reads its loss back. A copy stream fills one of two device slots with step k+1's
+    # inputs while step k computes, as a prefetching data loader does; all K copies are inside
+    # the timed region.
     e2e = None
     if not args.no_e2e:
         pinned = [torch.from_numpy(host[k]).pin_memory() for k in host]
         v_host = torch.from_numpy(np.ascontiguousarray(scene["viewmats"][cams])).pin_memory()
         t_host = torch.from_numpy(np.ascontiguousarray(targets_np[cams])).pin_memory()
-        loss_host = torch.empty((), dtype=torch.float32).pin_memory()
-        vm_d = torch.empty_like(views)
-        tg_d = torch.empty_like(target)
+        loss_host = torch.empty((args.steps + 1,), dtype=torch.float32).pin_memory()
+        slots = [([torch.empty_like(p) for p in params], torch.empty_like(views),
+                  torch.empty_like(target)) for _ in range(2)]
+        slot_params = [[sp.requires_grad_() for sp in sl[0]] for sl in slots]
         h2d = sum(t.numel() * 4 for t in pinned) + v_host.numel() * 4 + t_host.numel() * 4
+        compute = torch.cuda.current_stream(dev)
+        copier = torch.cuda.Stream(dev)
+        copied = [torch.cuda.Event() for _ in range(2)]
+        released = [torch.cuda.Event() for _ in range(2)]
 
-        def e2e_step():
-            with torch.no_grad():
-                for p, hp in zip(params, pinned):
-                    p.copy_(hp, non_blocking=True)
-                vm_d.copy_(v_host, non_blocking=True)
-                tg_d.copy_(t_host, non_blocking=True)
-            loss = step(vm_d, tg_d)
-            loss_host.copy_(loss.detach(), non_blocking=True)
+        def load(k):
+            s = k % 2
+            with torch.cuda.stream(copier), torch.no_grad():
+                copier.wait_event(released[s])
+                for sp, hp in zip(slot_params[s], pinned):
+                    sp.copy_(hp, non_blocking=True)
+                slots[s][1].copy_(v_host, non_blocking=True)
+                slots[s][2].copy_(t_host, non_blocking=True)
+                copied[s].record(copier)
 
-        e2e_step()
+        def run(k):
+            s = k % 2
+            compute.wait_event(copied[s])
+            loss = step(slots[s][1], slots[s][2], slot_params[s])
+            loss_host[k].copy_(loss.detach(), non_blocking=True)
+            released[s].record(compute)
+
+        for s in range(2):
+            released[s].record(compute)
+        load(0)
+        run(0)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(args.steps):
-            e2e_step()
-        e1.record()
+        e0.record(compute)
+        copier.wait_event(e0)
+        load(1)
+        for k in range(1, args.steps + 1):
+            if k + 1 <= args.steps:
+                load(k + 1)
+            run(k)
+        e1.record(compute)
         torch.cuda.synchronize()
         ems = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
         if world > 1:
             dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+        if not bool(torch.isfinite(loss_host[1:]).all()):
+            raise SystemExit("non-finite loss in the end-to-end steps")
         e2e = {"value": B * args.steps / (float(ems.item()) / 1e3), "unit": "frames/s",
-               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4}
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4,
+               "pipelining": "copy stream, two input slots"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -175,6 +175,20 @@ int splax_sort_and_bin(const float *xys, const float *depths, const int32_t *rad
                        int64_t *sorted_keys, int32_t *tile_bins, int64_t *num_intersects,
                        int32_t *used_key_bits, void *stream);
 
+/* Fused mean-squared-error loss of a rendered image stack. No counterpart in the reference,
+ * whose callers take the loss in JAX (the MSE objective of the benchmark configurations; the
+ * training step of scripts/train_colmap.py:118-295): loss[0] = sum((img - target)^2) / denom
+ * over `count` floats, one pass over both arrays. img, target and loss are device pointers.
+ * Deterministic (fixed grid, fixed-order final sum in fp64). */
+int splax_mse_loss(const float *img, const float *target, int64_t count, float denom,
+                   float *loss, void *stream);
+
+/* Gradient of splax_mse_loss: grad = v_loss[0] * 2 (img - target) / denom, where v_loss is the
+ * incoming cotangent as a device float (no host synchronisation). grad may alias neither
+ * input. */
+int splax_mse_loss_bwd(const float *img, const float *target, int64_t count, float denom,
+                       const float *v_loss, float *grad, void *stream);
+
 /* clear_cache, splax/_cache.py:158-164: release the scratch of every device. */
 void splax_clear_cache(void);
 

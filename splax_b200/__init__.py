@@ -5,19 +5,22 @@ and the forward and recompute-style backward blends run in libsplax_b200 (hand-w
 behind a C ABI, include/splax_b200.h). This package mirrors the reference's public API
 (splax/__init__.py:30-47) over torch tensors: ``render`` and ``render_log`` are differentiable
 with torch.autograd with respect to the gaussian parameters, the camera pose and per-object
-rigid transforms. There is no CPU fallback.
+rigid transforms. ``mse_loss`` is a fused loss-and-gradient kernel for the training step
+around the render. There is no CPU fallback.
 """
 
 __version__ = "0.1.0"
 
 from splax_b200 import utils
 from splax_b200._cache import clear_cache, scratch_info
+from splax_b200._loss import mse_loss
 from splax_b200._project import opacity_compensation, project, transform_ids
 from splax_b200._rasterize import rasterize, rasterize_depth
 from splax_b200._render import render, render_log
 
 __all__ = [
     "clear_cache",
+    "mse_loss",
     "opacity_compensation",
     "project",
     "rasterize",

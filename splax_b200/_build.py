@@ -31,6 +31,7 @@ SOURCES = {
     "raster_bwd.cu": [],
     "capi.cu": [],
     "project_noalloc.cu": [],
+    "loss.cu": [],
 }
 
 

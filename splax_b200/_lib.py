@@ -50,6 +50,8 @@ SIGNATURES: dict[str, list] = {
     "splax_profile_enable": [I32, I32],
     "splax_profile_reset": [],
     "splax_profile_report": [P, I32],
+    "splax_mse_loss": [P, P, I64, F32, P, P],
+    "splax_mse_loss_bwd": [P, P, I64, F32, P, P, P],
     "splax_last_error": [],
     "splax_version": [],
 }

@@ -206,6 +206,7 @@ struct DeviceState {
   // device work counters: fwd evals, fwd contribs, bwd evals, bwd contribs, bwd warp steps,
   // bwd warp steps past the ellipse cull, bwd warp steps with a contribution
   DevBuf work;
+  DevBuf loss;  // fused loss: per-CTA fp64 partials, then the completion counter
   KernelTimer timer;
   WorkUnits units;
   // the most recent sort_and_bin result, reusable by a backward over the same inputs
@@ -232,7 +233,7 @@ struct DeviceState {
     for (const DevBuf* b : {&keys[0], &keys[1], &vals[0], &vals[1], &records, &tile_bins,
                             &depth_mm, &status, &pkeys[0], &pkeys[1], &pvals[0], &pvals[1],
                             &poffs, &scan_status, &walk, &counts, &misc, &hist,
-                            &proj_status})
+                            &proj_status, &loss})
       s += b->bytes;
     return s;
   }
@@ -994,6 +995,48 @@ int splax_sort_and_bin(const float* xys, const float* depths, const int32_t* rad
   }
   *num_intersects = so.count;
   *used_key_bits = so.key_bits;
+  return finish(*st, stream);
+}
+
+int splax_mse_loss(const float* img, const float* target, int64_t count, float denom,
+                   float* loss, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (count < 0 || !(denom > 0.0f) || loss == nullptr ||
+      (count > 0 && (img == nullptr || target == nullptr)))
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "mse_loss: invalid count, denom or pointers");
+  DeviceState* st;
+  int rc = current_state(&st);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(st->mu);
+  rc = st->init();
+  if (rc) return rc;
+  const int blocks = mse_loss_blocks();
+  const size_t need = sizeof(double) * (blocks + 1);
+  if (st->loss.bytes < need) {
+    SPLAX_CUDA(buf_reserve(st->loss, need));
+    SPLAX_CUDA(cudaMemsetAsync(st->loss.p, 0, need, stream));
+  }
+  double* partials = static_cast<double*>(st->loss.p);
+  launch_mse_loss(img, target, count, 1.0 / static_cast<double>(denom), partials,
+                  reinterpret_cast<unsigned*>(partials + blocks), loss, blocks, stream);
+  return finish(*st, stream);
+}
+
+int splax_mse_loss_bwd(const float* img, const float* target, int64_t count, float denom,
+                       const float* v_loss, float* grad, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (count < 0 || !(denom > 0.0f) || v_loss == nullptr ||
+      (count > 0 && (img == nullptr || target == nullptr || grad == nullptr)))
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "mse_loss_bwd: invalid count, denom or pointers");
+  DeviceState* st;
+  int rc = current_state(&st);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(st->mu);
+  rc = st->init();
+  if (rc) return rc;
+  if (count > 0)
+    launch_mse_loss_bwd(img, target, count, 2.0f / denom, v_loss, grad, mse_loss_blocks(),
+                        stream);
   return finish(*st, stream);
 }
 

@@ -180,4 +180,13 @@ void launch_raster_bwd(const RasterBwdArgs& a, cudaStream_t stream);
 // capi.cu: set the calling thread's splax_last_error() message and return `code`
 int record_error(int code, const char* msg);
 
+// Fused MSE loss (loss.cu). `partials` holds `blocks` doubles; `done` is a zeroed counter the
+// kernel leaves zeroed.
+int mse_loss_blocks();
+void launch_mse_loss(const float* img, const float* tgt, int64_t count, double inv_denom,
+                     double* partials, unsigned* done, float* loss, int blocks,
+                     cudaStream_t stream);
+void launch_mse_loss_bwd(const float* img, const float* tgt, int64_t count, float scale,
+                         const float* v_loss, float* grad, int blocks, cudaStream_t stream);
+
 }  // namespace splax
