@@ -78,7 +78,7 @@ constexpr double kScratchHeadroom = 1.25;  // splax/_cache.py:149
 // ------------------------------------------------------------------ profiling (opt-in)
 std::atomic<bool> g_timing{false};
 std::atomic<bool> g_count_work{false};
-constexpr int kWorkWords = 7;  // device work counters (see DeviceState::work)
+constexpr int kWorkWords = 6;  // device work counters (see DeviceState::work)
 
 enum Kind { kProjectFwd, kProjectBwd, kDepthMinmax, kPairKeys, kPairSort, kPairScan, kEmit,
             kRadixSort, kTileBins, kRasterFwd, kRasterBwd, kNumKinds };
@@ -204,7 +204,7 @@ struct DeviceState {
   int32_t* pinned = nullptr;  // [0] count, [1] error word
   cudaEvent_t ev = nullptr;
   // device work counters: fwd evals, fwd contribs, bwd evals, bwd contribs, bwd warp steps,
-  // bwd warp steps past the ellipse cull, bwd warp steps with a contribution
+  // bwd warp steps with a contribution
   DevBuf work;
   DevBuf loss;  // fused loss: per-CTA fp64 partials, then the completion counter
   KernelTimer timer;
@@ -522,8 +522,8 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
   out.gids = ss.vals[fin];
   out.keys = static_cast<const uint32_t*>(ss.keys[fin]);
   st.timer.begin(kTileBins, 1, stream);
-  launch_tile_bins(out.keys, false, count, 0, tile_n_bits, static_cast<int32_t>(num_tiles),
-                   bins_len, static_cast<int32_t*>(st.tile_bins.p), st.err_word(), stream);
+  launch_tile_bins(out.keys, count, tile_n_bits, static_cast<int32_t>(num_tiles), bins_len,
+                   static_cast<int32_t*>(st.tile_bins.p), st.err_word(), stream);
   st.timer.end(stream);
   SPLAX_CUDA(cudaGetLastError());
   st.units.intersections += count;
@@ -1141,9 +1141,7 @@ int splax_profile_report(char* buf, int32_t len) {
            (long long)u.pairs_sorted, (long long)u.pair_key_bytes, (long long)u.pair_pass_keys);
   js += tmp;
   snprintf(tmp, sizeof tmp,
-           "\"bwd_warp_steps\": %llu, \"bwd_warp_steps_uncull\": %llu, "
-           "\"bwd_warp_steps_active\": %llu}}",
-           w[4], w[5], w[6]);
+           "\"bwd_warp_steps\": %llu, \"bwd_warp_steps_active\": %llu}}", w[4], w[5]);
   js += tmp;
   if (static_cast<int32_t>(js.size()) + 1 > len) return -SPLAX_ERR_INVALID_ARGUMENT;
   memcpy(buf, js.c_str(), js.size() + 1);

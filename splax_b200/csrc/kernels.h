@@ -53,9 +53,9 @@ struct ProjectBwdArgs {
 };
 
 // Per-gaussian record staged by the blend kernels: 3 x float4 =
-// (x, y, qa, qb), (qc, opacity, r, g), (b, depth, ex, ey), with the conic pre-scaled for a
-// base-2 exponent, (qa, qb, qc) = -log2(e)/2 * (a, 2b, c), and (ex, ey) the half-extents of
-// the ellipse outside which alpha < 1/255.
+// (x, y, qa, qb), (qc, opacity, r, g), (b, depth, 0, 0), with the conic pre-scaled for a
+// base-2 exponent, (qa, qb, qc) = -log2(e)/2 * (a, 2b, c); the last two floats pad the record
+// to 16-byte loads.
 constexpr int kRecordFloat4 = 3;
 
 struct EmitArgs {
@@ -131,7 +131,7 @@ struct SortScratch {
 int sort_tile_items(bool key64);
 int radix_sort_pairs(const SortScratch& s, bool key64, int64_t count, int bits,
                      cudaStream_t stream);
-void launch_tile_bins(const void* keys, bool key64, int64_t count, int shift, int32_t tile_n_bits,
+void launch_tile_bins(const uint32_t* keys, int64_t count, int32_t tile_n_bits,
                       int32_t num_tiles, int64_t num_bins, int32_t* tile_bins, unsigned* err,
                       cudaStream_t stream);
 

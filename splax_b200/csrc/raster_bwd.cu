@@ -2,16 +2,15 @@
 // (splax/_rasterize/_kernels.py:530-794, 935-1209) with _blend_color_vjp / _blend_depth_vjp
 // (:1212-1302).
 //
-// Recompute-style: one 64-thread CTA per (output image, tile); each warp owns a 16x8 block and
-// each thread four vertically adjacent pixels, advanced as two pairs with packed fp32x2
-// instructions. A warp skips every gaussian whose alpha >= 1/255 ellipse misses its block
-// (those evaluations are all rejected). The walk runs back to front from the block's largest
-// final_idx over batches of 256 records staged in shared memory (plus the flat ids that
-// address the gradients). Each pixel rebuilds T by dividing out (1 - alpha), and only entries
-// at or below its own final_idx count. All lanes of a warp visit the same entry together, so
-// each thread first adds its four pixels' cotangents, then the warp sums the 9 (10 with depth)
-// per-gaussian values with one reduce-scatter (~K shuffles instead of 5K) and issues ONE atomic
-// instruction across K lanes. Warps where no pixel contributes skip the reduction.
+// Recompute-style: one warp per (output image, 16x16 tile); each thread owns eight vertically
+// adjacent pixels of one column, advanced as four pairs with packed fp32x2 instructions. The
+// walk runs back to front from the tile's largest final_idx over batches of 256 records
+// staged in shared memory (plus the flat ids that address the gradients). Each pixel rebuilds
+// T by dividing out (1 - alpha), and only entries at or below its own final_idx count. All
+// lanes visit the same entry together, so each thread first adds its eight pixels'
+// cotangents, then the warp sums the 9 (10 with depth) per-gaussian values with one
+// reduce-scatter (~K shuffles instead of 5K) and issues ONE atomic instruction across K
+// lanes. Entries to which no pixel of the tile contributes skip the reduction.
 //
 // The staged conic is pre-scaled (q = -log2(e)/2 * (a, 2b, c)), so the exponent is one ex2;
 // the xy cotangent rescales by -ln 2 to recover the conic.
@@ -84,10 +83,9 @@ __device__ __forceinline__ bool vjp_pair(BwdPair& s, int32_t idx, float2 p, floa
   return v0 || v1;
 }
 
-// Four vertically adjacent pixels per thread (two packed pairs); a warp owns a 16x8 block of
-// the tile and the 64-thread CTA the whole tile. Four pixels per thread amortise the
-// per-gaussian warp reduction over 128 pixels.
-constexpr int kPixels = 4;
+// Eight vertically adjacent pixels per thread (four packed pairs): one warp covers the tile and
+// amortises the per-gaussian reduction and record reads over 256 pixels.
+constexpr int kPixels = 8;
 constexpr int kPairs = kPixels / 2;
 
 template <bool DEPTH, bool COUNT>
@@ -96,10 +94,10 @@ raster_bwd_kernel(RasterBwdArgs a) {
   constexpr int kBwdThreads = kBlockSize / kPixels;
   constexpr int K = DEPTH ? 10 : 9;
   unsigned long long evals = 0, contribs = 0;
-  unsigned steps = 0, steps_uncull = 0, steps_active = 0;  // warp steps (COUNT builds only)
+  unsigned steps = 0, steps_active = 0;  // warp steps (COUNT builds only)
   __shared__ float4 s_r0[kBlockSize];
   __shared__ float4 s_r1[kBlockSize];
-  __shared__ float4 s_r2[kBlockSize];
+  __shared__ float2 s_r2[kBlockSize];
   __shared__ int32_t s_id[kBlockSize];
   __shared__ int32_t s_wmax[kBwdThreads / 32];
 
@@ -119,10 +117,6 @@ raster_bwd_kernel(RasterBwdArgs a) {
   const int32_t i0 = tile_y * kBlockWidth + 2 * kPixels * warp + kPixels * (lane >> 4);
   const float px = static_cast<float>(j) + 0.5f;
   const float py0 = static_cast<float>(i0) + 0.5f;
-  // centre of the warp's block of pixel centres (half-extents 7.5 and kPixels - 0.5)
-  const float wcx = static_cast<float>(tile_x * kBlockWidth) + 8.0f;
-  const float wcy = static_cast<float>(tile_y * kBlockWidth + 2 * kPixels * warp + kPixels);
-  constexpr float kHalfY = kPixels - 0.5f;
 
   BwdPair pr[kPairs];
   const float* bg = a.background + 3 * (a.sel_bg ? image_id : 0);
@@ -200,32 +194,31 @@ raster_bwd_kernel(RasterBwdArgs a) {
           const float4* rec = a.records + kRecordFloat4 * static_cast<int64_t>(g);
           s_r0[slot] = rec[0];
           s_r1[slot] = rec[1];
-          s_r2[slot] = rec[2];
+          const float4 r2 = rec[2];
+          s_r2[slot] = make_float2(r2.x, r2.y);
           s_id[slot] = g;
         } else {  // only after a reported emission error: a transparent record, id 0
           s_r0[slot] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
           s_r1[slot] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-          s_r2[slot] = make_float4(0.0f, 0.0f, -1.0e30f, -1.0e30f);
+          s_r2[slot] = make_float2(0.0f, 0.0f);
           s_id[slot] = 0;
         }
       }
     }
     __syncthreads();
     const int32_t batch_size = min(kBlockSize, batch_end - range_start + 1);
-    // entries above every pixel of this warp are skipped as a whole
+    // entries above every pixel of the tile are skipped as a whole
     const int32_t t_begin = max(0, batch_end - wmax);
     for (int32_t t = t_begin; t < batch_size; ++t) {
       const int32_t idx = batch_end - t;
       const float4 r0 = s_r0[t];
-      const float4 r2 = s_r2[t];
+      const float2 r2 = s_r2[t];  // b, depth
       if constexpr (COUNT) {
 #pragma unroll
         for (int q = 0; q < kPairs; ++q)
           evals += static_cast<unsigned>(idx <= pr[q].bf0) + static_cast<unsigned>(idx <= pr[q].bf1);
         ++steps;
       }
-      if (fabsf(r0.x - wcx) > r2.z + 7.5f || fabsf(r0.y - wcy) > r2.w + kHalfY) continue;
-      if constexpr (COUNT) ++steps_uncull;
       const float4 r1 = s_r1[t];  // qc, opacity, r, g
       const float dx = r0.x - px;
       const float dy0 = r0.y - py0;
@@ -273,8 +266,7 @@ raster_bwd_kernel(RasterBwdArgs a) {
       atomicAdd(&a.work[0], evals);
       atomicAdd(&a.work[1], contribs);
       atomicAdd(&a.work[2], static_cast<unsigned long long>(steps));
-      atomicAdd(&a.work[3], static_cast<unsigned long long>(steps_uncull));
-      atomicAdd(&a.work[4], static_cast<unsigned long long>(steps_active));
+      atomicAdd(&a.work[3], static_cast<unsigned long long>(steps_active));
     }
   }
 }

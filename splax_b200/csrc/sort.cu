@@ -158,17 +158,11 @@ pair_prep_kernel(PairKeyArgs a, K* keys, int32_t* vals) {
   if (a.records) {
     const int64_t ci = idx % a.color_rows;
     const float op = a.opacities[idx % a.opac_rows];
-    // half-extents of the region where either opacity can reach alpha >= 1/255 (the larger
-    // isocontour), widened against rounding: the blends skip a warp's block outside it
-    const float tc = iso_level(fmax_w(mop, op));
-    const float nt = -tc / (cb * cb - ca * cc);
-    const float ex = sqrtf(nt * cc) * 1.001f + 0.01f;
-    const float ey = sqrtf(nt * ca) * 1.001f + 0.01f;
     float4* rec = a.records + kRecordFloat4 * idx;
     // conic pre-scaled for the blends' base-2 exponent: q = -log2(e)/2 * (a, 2b, c)
     rec[0] = make_float4(x, y, -kHalfLog2e * ca, -kLog2e * cb);
     rec[1] = make_float4(-kHalfLog2e * cc, op, a.colors[3 * ci], a.colors[3 * ci + 1]);
-    rec[2] = make_float4(a.colors[3 * ci + 2], depth, ex, ey);
+    rec[2] = make_float4(a.colors[3 * ci + 2], depth, 0.0f, 0.0f);
   }
 }
 
@@ -310,24 +304,46 @@ constexpr int kItems64 = 8;   // 4096 keys per tile for 64-bit keys
 constexpr int kHistThreads = 256;
 constexpr int kHistItems = 32;
 
+// Upfront digit histograms of every pass (up to 8) in one read of the keys: four sets of
+// shared counters, each shared by two warps (less same-address contention than one
+// block-wide set), 16-byte loads, then one global atomic per (pass, digit) and block.
 template <typename K>
 __global__ void __launch_bounds__(kHistThreads)
 radix_hist_kernel(const K* __restrict__ keys, int64_t count, int passes, uint32_t* hist) {
-  __shared__ uint32_t s[8][256];
-  for (int i = threadIdx.x; i < 8 * 256; i += kHistThreads) (&s[0][0])[i] = 0;
+  constexpr int kSets = 4;
+  constexpr int kVec = 16 / sizeof(K);  // keys per 16-byte load
+  __shared__ uint32_t s[kSets][8][256];
+  const int warp = (threadIdx.x >> 5) & (kSets - 1);
+  for (int i = threadIdx.x; i < kSets * 8 * 256; i += kHistThreads) (&s[0][0][0])[i] = 0;
   __syncthreads();
   const int64_t base = static_cast<int64_t>(blockIdx.x) * kHistThreads * kHistItems;
-#pragma unroll 4
-  for (int k = 0; k < kHistItems; ++k) {
-    const int64_t i = base + k * kHistThreads + threadIdx.x;
-    if (i >= count) break;
-    const uint64_t key = static_cast<uint64_t>(keys[i]);
-    for (int p = 0; p < passes; ++p) atomicAdd(&s[p][(key >> (8 * p)) & 255u], 1u);
+  const int64_t end = min(count, base + static_cast<int64_t>(kHistThreads) * kHistItems);
+  auto add = [&](uint64_t key) {
+    for (int p = 0; p < passes; ++p) atomicAdd(&s[warp][p][(key >> (8 * p)) & 255u], 1u);
+  };
+  if (end - base == static_cast<int64_t>(kHistThreads) * kHistItems) {
+    const uint4* v = reinterpret_cast<const uint4*>(keys + base);
+#pragma unroll 2
+    for (int j = 0; j < kHistItems / kVec; ++j) {
+      const uint4 q = v[j * kHistThreads + threadIdx.x];
+      if constexpr (sizeof(K) == 4) {
+        add(q.x); add(q.y); add(q.z); add(q.w);
+      } else {
+        add((static_cast<uint64_t>(q.y) << 32) | q.x);
+        add((static_cast<uint64_t>(q.w) << 32) | q.z);
+      }
+    }
+  } else {
+    for (int64_t i = base + threadIdx.x; i < end; i += kHistThreads)
+      add(static_cast<uint64_t>(keys[i]));
   }
   __syncthreads();
-  for (int p = 0; p < passes; ++p) {
-    const uint32_t c = s[p][threadIdx.x];
-    if (c) atomicAdd(&hist[p * 256 + threadIdx.x], c);
+  for (int i = threadIdx.x; i < passes * 256; i += kHistThreads) {
+    const int p = i >> 8, d = i & 255;
+    uint32_t c = 0;
+#pragma unroll
+    for (int w = 0; w < kSets; ++w) c += s[w][p][d];
+    if (c) atomicAdd(&hist[p * 256 + d], c);
   }
 }
 
@@ -481,30 +497,52 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
 }
 
 // ------------------------------------------------------------------ bin edges
-template <typename K>
-__global__ void tile_bins_kernel(const K* __restrict__ keys, int64_t count, int shift,
-                                 int32_t tile_n_bits, int32_t num_tiles, int64_t num_bins,
-                                 int2* bins, unsigned* err) {
-  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= count) return;
-  const uint64_t mask = (1ull << tile_n_bits) - 1ull;
-  const uint64_t key = static_cast<uint64_t>(keys[idx]) >> shift;
-  const int64_t cur = static_cast<int64_t>((key >> tile_n_bits) * num_tiles + (key & mask));
-  if (cur >= num_bins) {
-    atomicOr(err, kErrBinRange);
-    return;
+// Eight sorted keys per thread (two 16-byte loads); the key before the first comes from the
+// previous lane by shuffle (global load for lane 0). The edge logic per index is the
+// reference's, including its index-0 early return before the last-index test.
+constexpr int kBinThreads = 256;
+constexpr int kBinItems = 8;
+
+__global__ void __launch_bounds__(kBinThreads)
+tile_bins_kernel(const uint32_t* __restrict__ keys, int64_t count, int32_t tile_n_bits,
+                 int32_t num_tiles, int64_t num_bins, int2* bins, unsigned* err) {
+  const int64_t base =
+      (static_cast<int64_t>(blockIdx.x) * kBinThreads + threadIdx.x) * kBinItems;
+  const int lane = threadIdx.x & 31;
+  uint32_t k[kBinItems];
+  if (base + kBinItems <= count) {
+    const uint4 a = *reinterpret_cast<const uint4*>(keys + base);
+    const uint4 b = *reinterpret_cast<const uint4*>(keys + base + 4);
+    k[0] = a.x; k[1] = a.y; k[2] = a.z; k[3] = a.w;
+    k[4] = b.x; k[5] = b.y; k[6] = b.z; k[7] = b.w;
+  } else {
+#pragma unroll
+    for (int m = 0; m < kBinItems; ++m) k[m] = base + m < count ? keys[base + m] : 0u;
   }
-  // as in the reference, index 0 returns before the last-index test
-  if (idx == 0) {
-    bins[cur].x = 0;
-    return;
-  }
-  if (idx == count - 1) bins[cur].y = static_cast<int32_t>(count);
-  const uint64_t keyp = static_cast<uint64_t>(keys[idx - 1]) >> shift;
-  const int64_t prev = static_cast<int64_t>((keyp >> tile_n_bits) * num_tiles + (keyp & mask));
-  if (prev != cur && prev < num_bins) {
-    bins[prev].y = static_cast<int32_t>(idx);
-    bins[cur].x = static_cast<int32_t>(idx);
+  uint32_t prev_key = __shfl_up_sync(0xffffffffu, k[kBinItems - 1], 1);
+  if (lane == 0 && base > 0 && base - 1 < count) prev_key = keys[base - 1];
+  const uint32_t mask = (1u << tile_n_bits) - 1u;
+#pragma unroll
+  for (int m = 0; m < kBinItems; ++m) {
+    const int64_t idx = base + m;
+    const uint32_t key = k[m];
+    const uint32_t pk = m == 0 ? prev_key : k[m - 1];
+    if (idx >= count) break;
+    const int64_t cur = static_cast<int64_t>(key >> tile_n_bits) * num_tiles + (key & mask);
+    if (cur >= num_bins) {
+      atomicOr(err, kErrBinRange);
+      continue;
+    }
+    if (idx == 0) {
+      bins[cur].x = 0;
+      continue;
+    }
+    if (idx == count - 1) bins[cur].y = static_cast<int32_t>(count);
+    const int64_t prev = static_cast<int64_t>(pk >> tile_n_bits) * num_tiles + (pk & mask);
+    if (prev != cur && prev < num_bins) {
+      bins[prev].y = static_cast<int32_t>(idx);
+      bins[cur].x = static_cast<int32_t>(idx);
+    }
   }
 }
 
@@ -606,20 +644,13 @@ int radix_sort_pairs(const SortScratch& s, bool key64, int64_t count, int bits,
                : sort_impl<uint32_t, kItems32, kSortThreads>(s, count, bits, stream);
 }
 
-void launch_tile_bins(const void* keys, bool key64, int64_t count, int shift, int32_t tile_n_bits,
+void launch_tile_bins(const uint32_t* keys, int64_t count, int32_t tile_n_bits,
                       int32_t num_tiles, int64_t num_bins, int32_t* tile_bins, unsigned* err,
                       cudaStream_t stream) {
-  const int64_t blocks = (count + 255) / 256;
+  const int64_t per_block = static_cast<int64_t>(kBinThreads) * kBinItems;
+  const int64_t blocks = (count + per_block - 1) / per_block;
   if (blocks == 0) return;
-  int2* bins = reinterpret_cast<int2*>(tile_bins);
-  if (key64)
-    tile_bins_kernel<uint64_t><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-        reinterpret_cast<const uint64_t*>(keys), count, shift, tile_n_bits, num_tiles, num_bins,
-        bins, err);
-  else
-    tile_bins_kernel<uint32_t><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-        reinterpret_cast<const uint32_t*>(keys), count, shift, tile_n_bits, num_tiles, num_bins,
-        bins, err);
+  tile_bins_kernel<<<static_cast<unsigned>(blocks), kBinThreads, 0, stream>>>(
+      keys, count, tile_n_bits, num_tiles, num_bins, reinterpret_cast<int2*>(tile_bins), err);
 }
-
 }  // namespace splax
