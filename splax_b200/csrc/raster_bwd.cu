@@ -26,8 +26,9 @@ constexpr float kLn2 = 0.693147180559945f;
 struct BwdPair {
   int32_t bf0, bf1;  // bin_final of each pixel
   float2 T, vo0, vo1, vo2, vod;
-  float2 tb;      // t_final * (background . v_out): the background's share of v_alpha
-  float2 bufdot;  // (colour, depth) accumulated behind this gaussian, dotted with v_out
+  // (colour, depth) accumulated behind this gaussian dotted with v_out, plus the
+  // background's share t_final * (background . v_out): the term v_alpha subtracts
+  float2 behind;
 };
 
 // Per-thread sums for the current gaussian, lane-wise over a pixel pair (the two lanes are
@@ -41,8 +42,8 @@ struct BwdAcc {
 // _blend_color_vjp (splax/_rasterize/_kernels.py:1212-1254) for a pixel pair, branch-free:
 // a pixel that does not take part (entry past its final_idx, sigma < 0, alpha < 1/255) gets
 // alpha 0, leaves T and the colour buffer unchanged and adds exact zeros. The colour buffer
-// is kept as its dot product with v_out: v_alpha = T (c . v_out) - ra (buf . v_out + t_final
-// bg . v_out), and buf . v_out grows by (c . v_out) fac.
+// is kept as its dot product with v_out, plus the background's share: v_alpha = T (c . v_out)
+// - ra (buf . v_out + t_final bg . v_out), and buf . v_out grows by (c . v_out) fac.
 template <bool DEPTH, bool COUNT>
 __device__ __forceinline__ bool vjp_pair(BwdPair& s, int32_t idx, float2 p, float2 dy,
                                          float2 opac, float2 r, float2 g, float2 b, float2 depth,
@@ -56,8 +57,9 @@ __device__ __forceinline__ bool vjp_pair(BwdPair& s, int32_t idx, float2 p, floa
   const float2 am = make_float2(v0 ? a0 : 0.0f, v1 ? a1 : 0.0f);
   const float2 om = one_minus2(am);
   const float2 ra = make_float2(__fdividef(1.0f, om.x), __fdividef(1.0f, om.y));
-  const float2 Tn = mul2(s.T, ra);
-  s.T = make_float2(v0 ? Tn.x : s.T.x, v1 ? Tn.y : s.T.y);
+  // a pixel that does not take part has am = 0, om = 1 and ra = rcp.approx(1) = 1 exactly
+  // (an exact power of two; checked on B200), so T is left unchanged without a select
+  s.T = mul2(s.T, ra);
   const float2 fac = mul2(am, s.T);
   acc.c0 = fma2(s.vo0, fac, acc.c0);
   acc.c1 = fma2(s.vo1, fac, acc.c1);
@@ -69,9 +71,9 @@ __device__ __forceinline__ bool vjp_pair(BwdPair& s, int32_t idx, float2 p, floa
     cv = fma2(depth, s.vod, cv);
     acc.d = fma2(s.vod, fac, acc.d);
   }
-  const float2 rb = mul2(ra, add2(s.bufdot, s.tb));
+  const float2 rb = mul2(ra, s.behind);
   const float2 va = fma2(s.T, cv, make_float2(-rb.x, -rb.y));
-  s.bufdot = fma2(cv, fac, s.bufdot);
+  s.behind = fma2(cv, fac, s.behind);
   // where the 0.999 clamp is active alpha is constant: no sigma or opacity cotangent
   const float2 ovm = make_float2(v0 && ov.x <= kAlphaMax ? ov.x : 0.0f,
                                  v1 && ov.y <= kAlphaMax ? ov.y : 0.0f);
@@ -146,12 +148,10 @@ raster_bwd_kernel(RasterBwdArgs a) {
     BwdPair& q = pr[k >> 1];
     if (k & 1) {
       q.bf1 = bf;
-      q.T.y = T; q.vo0.y = vo0; q.vo1.y = vo1; q.vo2.y = vo2; q.vod.y = vod; q.tb.y = tb;
-      q.bufdot.y = 0.0f;
+      q.T.y = T; q.vo0.y = vo0; q.vo1.y = vo1; q.vo2.y = vo2; q.vod.y = vod; q.behind.y = tb;
     } else {
       q.bf0 = bf;
-      q.T.x = T; q.vo0.x = vo0; q.vo1.x = vo1; q.vo2.x = vo2; q.vod.x = vod; q.tb.x = tb;
-      q.bufdot.x = 0.0f;
+      q.T.x = T; q.vo0.x = vo0; q.vo1.x = vo1; q.vo2.x = vo2; q.vod.x = vod; q.behind.x = tb;
     }
   }
 
