@@ -230,7 +230,11 @@ sorted_offsets_kernel(const int32_t* __restrict__ perm, const int32_t* __restric
 // Emission in sorted pair order: the ellipse walk once more per visible pair (the count
 // projection made), from the pair's walk record, writing the (image | tile) bin key and the
 // flat id at the pair's offset -- adjacent threads write adjacent runs.
-__global__ void __launch_bounds__(256) emit_sorted_kernel(EmitArgs a) {
+// one warp per CTA: a pair's walk can be ~200x the median, and a warp that finishes frees its
+// slot at once instead of waiting for the slowest warp of a larger block
+constexpr int kEmitThreads = 32;
+
+__global__ void __launch_bounds__(kEmitThreads) emit_sorted_kernel(EmitArgs a) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= a.total) return;
   const int64_t idx = a.perm[i];
@@ -622,9 +626,9 @@ void launch_sorted_offsets(const int32_t* perm, const int32_t* counts, int64_t t
 }
 
 void launch_emit(const EmitArgs& a, cudaStream_t stream) {
-  const int64_t blocks = (a.total + 255) / 256;
+  const int64_t blocks = (a.total + kEmitThreads - 1) / kEmitThreads;
   if (blocks == 0) return;
-  emit_sorted_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
+  emit_sorted_kernel<<<static_cast<unsigned>(blocks), kEmitThreads, 0, stream>>>(a);
 }
 
 void launch_reference_keys(const uint32_t* bin_keys, const int32_t* gids, int64_t count,
