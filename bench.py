@@ -37,6 +37,10 @@ WORKLOAD = "config 2: 1M gaussians, 8 ring cams, 1080x1920, MSE fwd+bwd, grads o
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 # algorithmic work per unit: FLOPs per blend evaluation / contribution (FMA = 2), restated from
 # the reference blend loop (splax/_rasterize/_kernels.py:185-197) and vjp (:1235-1253)
+# DRAM bytes (read + write) per launch of the full config-2 workload from single-pass ncu
+# captures (dram__bytes_read.sum + dram__bytes_write.sum), summarised in profiles/*.md
+TRAFFIC_BYTES_PER_LAUNCH = {"raster_bwd": 620.40e6, "raster_fwd": 491.68e6,
+                            "emit_keys": 985.57e6}
 FWD_FLOPS_PER_EVAL = 22
 BWD_FLOPS_PER_EVAL = 12
 BWD_FLOPS_PER_CONTRIB = 45
@@ -381,9 +385,12 @@ def main() -> None:
                               "unit": "TFLOP/s", "frac": tf / fp32_peak, "ms": t}
         total_ms = {k: v["ms"] for k, v in kern.items()}
         dom = max(total_ms, key=total_ms.get)
+        for name, t in TRAFFIC_BYTES_PER_LAUNCH.items():
+            if name in rows and CONFIG == 2 and args.n is None and world == 1:
+                rows[name]["traffic"] = t
         roof = dict(rows.get(dom, {}))
         roof.pop("ms", None)
-        roof.update({"kernel": dom, "traffic": None,
+        roof.update({"kernel": dom, "traffic": roof.get("traffic"),
                      "peak_source": peak_src if roof.get("bound") == "hbm"
                      else f"derived: {props.multi_processor_count} SMs x 128 FP32 lanes x 2 x "
                           f"{sm_mhz:.0f} MHz sampled SM clock"})
