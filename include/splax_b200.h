@@ -95,6 +95,47 @@ int splax_project_bwd(const float *means3d, int64_t means3d_rows, const float *s
                       int64_t out_rows, float *v_mean3d, float *v_scale, float *v_quat,
                       float *v_viewmat, float *v_transforms, void *stream);
 
+/* Projection with options (no FFI counterpart in the reference, whose JAX side rolls the
+ * quaternions to xyzw and computes opacity_compensation, splax/_project/_project.py:95-117,
+ * from the projection's outputs): splax_project's arguments, then quats_wxyz (1: quaternions
+ * stored scalar-first, read without a reorder pass), and the antialiasing compensation folded
+ * into the same launch -- with rho non-NULL, rho (total,) receives
+ * sqrt(clip(1 - eps (a + c) + eps2 (a c - b^2), 0, 1)) of each pair's conic, 1 when culled;
+ * eps is the 0.3 px^2 dilation and eps2 = eps*eps as the caller rounds it to fp32. */
+int splax_project_ex(const float *means3d, int64_t means3d_rows, const float *scales,
+                     int64_t scales_rows, const float *quats, int64_t quats_rows,
+                     const float *viewmat, int64_t viewmat_rows, const float *opacities,
+                     int64_t opacities_rows, const float *gaussian_transforms,
+                     int64_t transforms_rows, const int32_t *transform_ids,
+                     int32_t num_gaussians, int32_t num_transforms, int32_t has_transforms,
+                     int32_t img_h, int32_t img_w, float fx, float fy, float cx, float cy,
+                     float glob_scale, float clip_thresh, int64_t total, float *xys,
+                     float *depths, int32_t *radii, float *conics, int32_t *num_tiles_hit,
+                     int32_t *cum_tiles_hit, int32_t quats_wxyz, float aa_eps, float aa_eps2,
+                     float *rho, void *stream);
+
+/* Backward of splax_project_ex: splax_project_bwd's arguments, with
+ * - v_xy / v_depth may be NULL (zero cotangents; their rows are ignored);
+ * - v_rho (n or B*n rows, or NULL): the cotangent of rho, chained through d rho / d conic into
+ *   the conic cotangent (zero where the clip is active or the pair is culled), with the same
+ *   eps and eps2;
+ * - quats_wxyz: quats and v_quat stored scalar-first;
+ * - fold_batch (1): v_mean3d, v_scale and v_quat get n rows, each the sum over the B images
+ *   (what a caller sums for operands shared by the batch); needs n-row means, scales, quats. */
+int splax_project_bwd_ex(const float *means3d, int64_t means3d_rows, const float *scales,
+                         int64_t scales_rows, const float *quats, int64_t quats_rows,
+                         const float *viewmat, int64_t viewmat_rows, const int32_t *radii,
+                         int64_t radii_rows, const float *conics, int64_t conics_rows,
+                         const float *v_xy, int64_t v_xy_rows, const float *v_depth,
+                         int64_t v_depth_rows, const float *v_conic, int64_t v_conic_rows,
+                         const float *v_rho, int64_t v_rho_rows, float aa_eps, float aa_eps2,
+                         const float *gaussian_transforms, int64_t transforms_rows,
+                         const int32_t *transform_ids, int32_t num_gaussians,
+                         int32_t num_transforms, int32_t has_transforms, float fx, float fy,
+                         float glob_scale, int64_t out_rows, int32_t quats_wxyz,
+                         int32_t fold_batch, float *v_mean3d, float *v_scale, float *v_quat,
+                         float *v_viewmat, float *v_transforms, void *stream);
+
 /* FFI target "rasterize": _rasterize_warp, splax/_rasterize/_kernels.py:37-87 (:90-99).
  * geom_rows = rows of xys / depths / radii / conics / cum_tiles_hit (= B*n); out_rows = B*H.
  * key_bits: 0 = the reference's automatic width (splax/_rasterize/_sort/_sort.py:23-26),

@@ -32,6 +32,12 @@ SIGNATURES: dict[str, list] = {
                               I32, I32, F32, F32, F32, F32, F32, F32, I64, P, P, P, P, P, P, P],
     "splax_project_bwd": [P, I64, P, I64, P, I64, P, I64, P, I64, P, I64, P, I64, P, I64, P, I64,
                           P, I64, P, I32, I32, I32, F32, F32, F32, I64, P, P, P, P, P, P],
+    "splax_project_ex": [P, I64, P, I64, P, I64, P, I64, P, I64, P, I64, P, I32, I32, I32, I32,
+                         I32, F32, F32, F32, F32, F32, F32, I64, P, P, P, P, P, P, I32, F32, F32,
+                         P, P],
+    "splax_project_bwd_ex": [P, I64, P, I64, P, I64, P, I64, P, I64, P, I64, P, I64, P, I64, P,
+                             I64, P, I64, F32, F32, P, I64, P, I32, I32, I32, F32, F32, F32, I64,
+                             I32, I32, P, P, P, P, P, P],
     "splax_rasterize": [P, I64, P, I64, P, I64, P, I64, P, P, P, P, P, I64, I32, I32, I32, I64,
                         I32, P, P, P, P],
     "splax_rasterize_depth": [P, I64, P, I64, P, I64, P, I64, P, P, P, P, P, I64, I32, I32, I32,

@@ -50,11 +50,11 @@ def batch_size(n: int, means3d, scales, quats, viewmat, opacities, transforms=No
 
 class _ProjectFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, means3d, scales, quats_xyzw, viewmat, opac, transforms, tf_ids, n, img_h,
-                img_w, fx, fy, cx, cy, glob_scale, clip_thresh, has_transforms, B):
-        dev = _lib.require_cuda(means3d, scales, quats_xyzw, viewmat, opac)
+    def forward(ctx, means3d, scales, quats_wxyz, viewmat, opac, transforms, tf_ids, n, img_h,
+                img_w, fx, fy, cx, cy, glob_scale, clip_thresh, has_transforms, B, aa_eps):
+        dev = _lib.require_cuda(means3d, scales, quats_wxyz, viewmat, opac)
         lib = _lib.load()
-        m, s, q, vm, o = map(_f32, (means3d, scales, quats_xyzw, viewmat, opac))
+        m, s, q, vm, o = map(_f32, (means3d, scales, quats_wxyz, viewmat, opac))
         tf = _f32(transforms)
         ids = tf_ids.detach().to(torch.int32).contiguous()
         K = transforms.shape[-3]
@@ -66,54 +66,71 @@ class _ProjectFn(torch.autograd.Function):
         conics = torch.empty((total, 3), device=dev, dtype=torch.float32)
         nth = torch.empty((total,), device=dev, dtype=torch.int32)
         cum = torch.empty((total,), device=dev, dtype=torch.int32)
+        aa = aa_eps is not None
+        rho = torch.empty((total if aa else 0,), device=dev, dtype=torch.float32)
         p = _lib.ptr
-        with torch.cuda.device(dev):
-            rc = lib.splax_project(
-                p(m), m.numel() // 3, p(s), s.numel() // 3, p(q), q.numel() // 4, p(vm),
+        args = [p(m), m.numel() // 3, p(s), s.numel() // 3, p(q), q.numel() // 4, p(vm),
                 vm.numel() // 4, p(o), o.numel(), p(tf), tf.numel() // 16, p(ids), n, K,
                 int(has_transforms), img_h, img_w, fx, fy, cx, cy, glob_scale, clip_thresh,
-                total, p(xys), p(depths), p(radii), p(conics), p(nth), p(cum), _lib.stream_of(m))
+                total, p(xys), p(depths), p(radii), p(conics), p(nth), p(cum)]
+        eps, eps2 = _aa_consts(aa_eps) if aa else (0.0, 0.0)
+        with torch.cuda.device(dev):
+            # quaternions stay scalar-first: the kernel reads wxyz directly
+            rc = lib.splax_project_ex(*args, 1, eps, eps2, p(rho) if aa else None,
+                                      _lib.stream_of(m))
         _lib.check(rc)
         lead = (B, n) if B else (n,)
         outs = (xys.view(*lead, 2), depths.view(*lead, 1), radii.view(*lead, 1),
-                conics.view(*lead, 3), nth.view(*lead, 1), cum.view(*lead, 1))
+                conics.view(*lead, 3), nth.view(*lead, 1), cum.view(*lead, 1),
+                rho.view(*lead) if aa else rho)
         ctx.save_for_backward(m, s, q, vm, tf, ids, radii, conics)
-        ctx.statics = (n, fx, fy, glob_scale, has_transforms, B, K)
-        ctx.shapes = (means3d.shape, scales.shape, quats_xyzw.shape, viewmat.shape,
+        ctx.statics = (n, fx, fy, glob_scale, has_transforms, B, K, aa_eps)
+        ctx.shapes = (means3d.shape, scales.shape, quats_wxyz.shape, viewmat.shape,
                       transforms.shape)
         ctx.mark_non_differentiable(outs[2], outs[4], outs[5])
+        if not aa:
+            ctx.mark_non_differentiable(outs[6])
+        # unused outputs get no zero-filled cotangents; the kernel treats NULL as zero
+        ctx.set_materialize_grads(False)
         return outs
 
     @staticmethod
-    def backward(ctx, v_xys, v_depths, _v_radii, v_conics, _v_nth, _v_cum):
+    def backward(ctx, v_xys, v_depths, _v_radii, v_conics, _v_nth, _v_cum, v_rho):
         m, s, q, vm, tf, ids, radii, conics = ctx.saved_tensors
-        n, fx, fy, glob_scale, has_transforms, B, K = ctx.statics
+        n, fx, fy, glob_scale, has_transforms, B, K, aa_eps = ctx.statics
         dev = m.device
         Bt = max(B, 1)
         total = Bt * n
-        zeros = lambda w: torch.zeros((total, w), device=dev, dtype=torch.float32)  # noqa: E731
-        vxy = _f32(v_xys) if v_xys is not None else zeros(2)
-        vd = _f32(v_depths) if v_depths is not None else zeros(1)
-        vc = _f32(v_conics) if v_conics is not None else zeros(3)
-        v_mean = torch.empty((total, 3), device=dev, dtype=torch.float32)
-        v_scale = torch.empty((total, 3), device=dev, dtype=torch.float32)
-        v_quat = torch.empty((total, 4), device=dev, dtype=torch.float32)
+        vxy = _f32(v_xys) if v_xys is not None else None
+        vd = _f32(v_depths) if v_depths is not None else None
+        vc = (_f32(v_conics) if v_conics is not None
+              else torch.zeros((total, 3), device=dev, dtype=torch.float32))
+        vr = _f32(v_rho) if (aa_eps is not None and v_rho is not None) else None
+        # operands shared by the batch get their gradient summed over the images in-kernel
+        fold = bool(B) and m.numel() // 3 == n and s.numel() // 3 == n and q.numel() // 4 == n
+        grows = n if fold else total
+        v_mean = torch.empty((grows, 3), device=dev, dtype=torch.float32)
+        v_scale = torch.empty((grows, 3), device=dev, dtype=torch.float32)
+        v_quat = torch.empty((grows, 4), device=dev, dtype=torch.float32)
         v_view = torch.empty((Bt, 4, 4), device=dev, dtype=torch.float32)
         v_tf = torch.empty((Bt, K, 4, 4), device=dev, dtype=torch.float32)
         p = _lib.ptr
         lib = _lib.load()
+        eps, eps2 = _aa_consts(aa_eps) if vr is not None else (0.0, 0.0)
         with torch.cuda.device(dev):
-            rc = lib.splax_project_bwd(
+            rc = lib.splax_project_bwd_ex(
                 p(m), m.numel() // 3, p(s), s.numel() // 3, p(q), q.numel() // 4, p(vm),
-                vm.numel() // 4, p(radii), radii.numel(), p(conics), conics.numel() // 3, p(vxy),
-                vxy.numel() // 2, p(vd), vd.numel(), p(vc), vc.numel() // 3, p(tf),
-                tf.numel() // 16, p(ids), n, K, int(has_transforms), fx, fy, glob_scale, total,
+                vm.numel() // 4, p(radii), radii.numel(), p(conics), conics.numel() // 3,
+                p(vxy), total if vxy is None else vxy.numel() // 2,
+                p(vd), total if vd is None else vd.numel(), p(vc), vc.numel() // 3,
+                p(vr), total if vr is None else vr.numel(), eps, eps2, p(tf), tf.numel() // 16,
+                p(ids), n, K, int(has_transforms), fx, fy, glob_scale, total, 1, int(fold),
                 p(v_mean), p(v_scale), p(v_quat), p(v_view), p(v_tf), _lib.stream_of(m))
         _lib.check(rc)
         ms, ss, qs, vs, ts = ctx.shapes
 
-        def fold(g, shape, width):
-            # shared operand: sum the per-image slots; batched: per-image rows
+        def fold_rows(g, shape, width):
+            # shared operand not folded in-kernel: sum the per-image slots
             if B and g.numel() // width != (torch.Size(shape).numel() // width):
                 g = g.view(Bt, -1).sum(0)
             return g.reshape(shape)
@@ -123,8 +140,16 @@ class _ProjectFn(torch.autograd.Function):
             g_tf = v_tf if len(ts) == 4 else v_tf.sum(0)
             g_tf = g_tf.reshape(ts)
         g_view = v_view if len(vs) == 3 else v_view.sum(0)
-        return (fold(v_mean, ms, 3), fold(v_scale, ss, 3), fold(v_quat, qs, 4),
-                g_view.reshape(vs), None, g_tf, None, *([None] * 11))
+        return (fold_rows(v_mean, ms, 3), fold_rows(v_scale, ss, 3), fold_rows(v_quat, qs, 4),
+                g_view.reshape(vs), None, g_tf, None, *([None] * 12))
+
+
+def _aa_consts(eps: float) -> tuple[float, float]:
+    """eps and eps^2 as fp32 operands, rounded like the torch expression in
+    ``opacity_compensation`` (a Python-float scalar times an fp32 tensor)."""
+    e = float(torch.tensor(eps, dtype=torch.float32))
+    e2 = float(torch.tensor(eps * eps, dtype=torch.float32))
+    return e, e2
 
 
 def project(
@@ -141,6 +166,7 @@ def project(
     clip_thresh: float = 0.01,
     gaussian_transforms: torch.Tensor | None = None,
     transform_ids: torch.Tensor | None = None,
+    antialias_eps: float | None = None,
 ):
     """Project gaussians to screen space with the opacity-aware tile intersection.
 
@@ -148,7 +174,10 @@ def project(
     ``c`` defaults to the image center, and the six outputs are the screen-space centers
     (N,2), depths (N,1), radii (N,1), conics (N,3), tile counts (N,1) and their global
     inclusive scan (N,1) -- each with a leading B when any operand is batched. The integer
-    outputs are int32.
+    outputs are int32. With ``antialias_eps`` (not in the reference's signature; ``render``
+    passes 0.3 when antialiased) the kernel also returns, as a seventh output, the per-pair
+    compensation ``opacity_compensation(conics, radii, eps)`` computed in the same launch, and
+    its gradient reaches the conics inside the backward kernel.
     """
     n = mean3ds.shape[-2]
     if c is None:
@@ -162,13 +191,13 @@ def project(
         raise ValueError("gaussian_transforms needs transform_ids")
     B = batch_size(n, mean3ds, scales, quats, viewmat, opacities,
                    gaussian_transforms if has_transforms else None)
-    # the kernels work scalar-last (xyzw); autograd rolls the quaternion gradient back
-    quats_xyzw = torch.roll(quats, -1, dims=-1)
     H, W = img_shape
-    return _ProjectFn.apply(
-        mean3ds, scales, quats_xyzw, viewmat, opacities.reshape(-1), gaussian_transforms,
+    outs = _ProjectFn.apply(
+        mean3ds, scales, quats, viewmat, opacities.reshape(-1), gaussian_transforms,
         transform_ids, int(n), int(H), int(W), float(f[0]), float(f[1]), float(c[0]),
-        float(c[1]), float(glob_scale), float(clip_thresh), bool(has_transforms), int(B))
+        float(c[1]), float(glob_scale), float(clip_thresh), bool(has_transforms), int(B),
+        None if antialias_eps is None else float(antialias_eps))
+    return outs if antialias_eps is not None else outs[:6]
 
 
 def opacity_compensation(conics: torch.Tensor, radii: torch.Tensor, eps: float = 0.3) -> torch.Tensor:

@@ -56,6 +56,8 @@ class _RasterizeFn(torch.autograd.Function):
         ctx.statics = (n, img_h, img_w, B, with_depth, key_bits)
         ctx.shapes = (colors.shape, opacities.shape, xys.shape, depths.shape, conics.shape)
         ctx.mark_non_differentiable(final_Ts, final_idx)
+        # the residual outputs get no zero-filled cotangents in the backward
+        ctx.set_materialize_grads(False)
         lead = (B, img_h, img_w) if B else (img_h, img_w)
         img = out_img.view(*lead, 3)
         if with_depth:

@@ -6,8 +6,10 @@ from collections.abc import Sequence
 
 import torch
 
-from splax_b200._project import opacity_compensation, project, transform_ids
+from splax_b200._project import project, transform_ids
 from splax_b200._rasterize import rasterize, rasterize_depth
+
+_AA_EPS = 0.3  # the projection's screen-space dilation (splax/_project/_project.py:95)
 
 
 def render(
@@ -47,15 +49,17 @@ def render(
                 f"match {len(gaussian_slices)} slices, expected (K, 4, 4)")
         tf_ids = transform_ids(means3d.shape[-2], gaussian_slices, device=means3d.device)
 
-    xys, depths, radii, conics, _, cum_tiles_hit = project(
+    outs = project(
         means3d, scales, quats, viewmat, opacities=opacities, img_shape=img_shape, f=f, c=c,
         glob_scale=glob_scale, clip_thresh=clip_thresh, gaussian_transforms=gaussian_transforms,
-        transform_ids=tf_ids)
+        transform_ids=tf_ids, antialias_eps=_AA_EPS if antialiased else None)
+    xys, depths, radii, conics, _, cum_tiles_hit = outs[:6]
 
     blend_opacities = opacities
     map_opacities = None
     if antialiased:
-        rho = opacity_compensation(conics, radii)
+        # opacity_compensation(conics, radii), computed by the projection kernel
+        rho = outs[6]
         n = means3d.shape[-2]
         lead = rho.shape[:-1]
         blend_opacities = opacities.reshape(*([1] * len(lead)), n) * rho if lead else \

@@ -727,15 +727,17 @@ const char* splax_last_error(void) { return g_last_error.c_str(); }
 
 const char* splax_version(void) { return "splax_b200 0.1.0 (sm_100a)"; }
 
-int splax_project(const float* means3d, int64_t means3d_rows, const float* scales,
-                  int64_t scales_rows, const float* quats_xyzw, int64_t quats_rows,
-                  const float* viewmat, int64_t viewmat_rows, const float* opacities,
-                  int64_t opacities_rows, const float* gaussian_transforms,
-                  int64_t transforms_rows, const int32_t* transform_ids, int32_t num_gaussians,
-                  int32_t num_transforms, int32_t has_transforms, int32_t img_h, int32_t img_w,
-                  float fx, float fy, float cx, float cy, float glob_scale, float clip_thresh,
-                  int64_t total, float* xys, float* depths, int32_t* radii, float* conics,
-                  int32_t* num_tiles_hit, int32_t* cum_tiles_hit, void* stream_) {
+static int project_impl(const float* means3d, int64_t means3d_rows, const float* scales,
+                        int64_t scales_rows, const float* quats_xyzw, int64_t quats_rows,
+                        const float* viewmat, int64_t viewmat_rows, const float* opacities,
+                        int64_t opacities_rows, const float* gaussian_transforms,
+                        int64_t transforms_rows, const int32_t* transform_ids,
+                        int32_t num_gaussians, int32_t num_transforms, int32_t has_transforms,
+                        int32_t img_h, int32_t img_w, float fx, float fy, float cx, float cy,
+                        float glob_scale, float clip_thresh, int64_t total, float* xys,
+                        float* depths, int32_t* radii, float* conics, int32_t* num_tiles_hit,
+                        int32_t* cum_tiles_hit, int32_t quats_wxyz, float aa_eps,
+                        float aa_eps2, float* rho, void* stream_) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   const int64_t n = num_gaussians;
   if (n <= 0 || total <= 0 || total % n != 0 || img_h <= 0 || img_w <= 0)
@@ -792,6 +794,10 @@ int splax_project(const float* means3d, int64_t means3d_rows, const float* scale
   a.conics = conics;
   a.num_tiles_hit = num_tiles_hit;
   a.cum_tiles_hit = cum_tiles_hit;
+  a.rho = rho;
+  a.aa_eps = aa_eps;
+  a.aa_eps2 = aa_eps2;
+  a.quats_wxyz = quats_wxyz != 0;
   unsigned long long* words = static_cast<unsigned long long*>(st->proj_status.p);
   st->timer.begin(kProjectFwd, 1, stream);
   launch_project_fwd(a, words + 1, reinterpret_cast<int*>(words), st->err_word(), stream);
@@ -800,17 +806,54 @@ int splax_project(const float* means3d, int64_t means3d_rows, const float* scale
   return finish(*st, stream);
 }
 
-int splax_project_bwd(const float* means3d, int64_t means3d_rows, const float* scales,
-                      int64_t scales_rows, const float* quats_xyzw, int64_t quats_rows,
-                      const float* viewmat, int64_t viewmat_rows, const int32_t* radii,
-                      int64_t radii_rows, const float* conics, int64_t conics_rows,
-                      const float* v_xy, int64_t v_xy_rows, const float* v_depth,
-                      int64_t v_depth_rows, const float* v_conic, int64_t v_conic_rows,
-                      const float* gaussian_transforms, int64_t transforms_rows,
-                      const int32_t* transform_ids, int32_t num_gaussians, int32_t num_transforms,
-                      int32_t has_transforms, float fx, float fy, float glob_scale,
-                      int64_t out_rows, float* v_mean3d, float* v_scale, float* v_quat,
-                      float* v_viewmat, float* v_transforms, void* stream_) {
+int splax_project(const float* means3d, int64_t means3d_rows, const float* scales,
+                  int64_t scales_rows, const float* quats_xyzw, int64_t quats_rows,
+                  const float* viewmat, int64_t viewmat_rows, const float* opacities,
+                  int64_t opacities_rows, const float* gaussian_transforms,
+                  int64_t transforms_rows, const int32_t* transform_ids, int32_t num_gaussians,
+                  int32_t num_transforms, int32_t has_transforms, int32_t img_h, int32_t img_w,
+                  float fx, float fy, float cx, float cy, float glob_scale, float clip_thresh,
+                  int64_t total, float* xys, float* depths, int32_t* radii, float* conics,
+                  int32_t* num_tiles_hit, int32_t* cum_tiles_hit, void* stream) {
+  return project_impl(means3d, means3d_rows, scales, scales_rows, quats_xyzw, quats_rows,
+                      viewmat, viewmat_rows, opacities, opacities_rows, gaussian_transforms,
+                      transforms_rows, transform_ids, num_gaussians, num_transforms,
+                      has_transforms, img_h, img_w, fx, fy, cx, cy, glob_scale, clip_thresh,
+                      total, xys, depths, radii, conics, num_tiles_hit, cum_tiles_hit, 0, 0.0f,
+                      0.0f, nullptr, stream);
+}
+
+int splax_project_ex(const float* means3d, int64_t means3d_rows, const float* scales,
+                     int64_t scales_rows, const float* quats, int64_t quats_rows,
+                     const float* viewmat, int64_t viewmat_rows, const float* opacities,
+                     int64_t opacities_rows, const float* gaussian_transforms,
+                     int64_t transforms_rows, const int32_t* transform_ids,
+                     int32_t num_gaussians, int32_t num_transforms, int32_t has_transforms,
+                     int32_t img_h, int32_t img_w, float fx, float fy, float cx, float cy,
+                     float glob_scale, float clip_thresh, int64_t total, float* xys,
+                     float* depths, int32_t* radii, float* conics, int32_t* num_tiles_hit,
+                     int32_t* cum_tiles_hit, int32_t quats_wxyz, float aa_eps, float aa_eps2,
+                     float* rho, void* stream) {
+  return project_impl(means3d, means3d_rows, scales, scales_rows, quats, quats_rows, viewmat,
+                      viewmat_rows, opacities, opacities_rows, gaussian_transforms,
+                      transforms_rows, transform_ids, num_gaussians, num_transforms,
+                      has_transforms, img_h, img_w, fx, fy, cx, cy, glob_scale, clip_thresh,
+                      total, xys, depths, radii, conics, num_tiles_hit, cum_tiles_hit,
+                      quats_wxyz, aa_eps, aa_eps2, rho, stream);
+}
+static int project_bwd_impl(const float* means3d, int64_t means3d_rows, const float* scales,
+                            int64_t scales_rows, const float* quats_xyzw, int64_t quats_rows,
+                            const float* viewmat, int64_t viewmat_rows, const int32_t* radii,
+                            int64_t radii_rows, const float* conics, int64_t conics_rows,
+                            const float* v_xy, int64_t v_xy_rows, const float* v_depth,
+                            int64_t v_depth_rows, const float* v_conic, int64_t v_conic_rows,
+                            const float* v_rho, int64_t v_rho_rows, float aa_eps, float aa_eps2,
+                            const float* gaussian_transforms, int64_t transforms_rows,
+                            const int32_t* transform_ids, int32_t num_gaussians,
+                            int32_t num_transforms, int32_t has_transforms, float fx, float fy,
+                            float glob_scale, int64_t out_rows, int32_t quats_wxyz,
+                            int32_t fold_batch, float* v_mean3d, float* v_scale, float* v_quat,
+                            float* v_viewmat, float* v_transforms, void* stream_) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   const int64_t n = num_gaussians;
   if (n <= 0 || out_rows <= 0 || out_rows % n != 0)
@@ -818,10 +861,14 @@ int splax_project_bwd(const float* means3d, int64_t means3d_rows, const float* s
   const int64_t B = out_rows / n;
   if (bad_rows(means3d_rows, n, out_rows) || bad_rows(scales_rows, n, out_rows) ||
       bad_rows(quats_rows, n, out_rows) || bad_rows(radii_rows, n, out_rows) ||
-      bad_rows(conics_rows, n, out_rows) || bad_rows(v_xy_rows, n, out_rows) ||
-      bad_rows(v_depth_rows, n, out_rows) || bad_rows(v_conic_rows, n, out_rows) ||
+      bad_rows(conics_rows, n, out_rows) || (v_xy && bad_rows(v_xy_rows, n, out_rows)) ||
+      (v_depth && bad_rows(v_depth_rows, n, out_rows)) || bad_rows(v_conic_rows, n, out_rows) ||
+      (v_rho != nullptr && bad_rows(v_rho_rows, n, out_rows)) ||
       !(viewmat_rows == 4 || viewmat_rows == 4 * B))
     return fail(SPLAX_ERR_INVALID_ARGUMENT, "project_bwd: operand rows must be n or B*n");
+  if (fold_batch && (means3d_rows != n || scales_rows != n || quats_rows != n))
+    return fail(SPLAX_ERR_INVALID_ARGUMENT,
+                "project_bwd: folded gradients need shared means, scales and quats");
   const int32_t K = num_transforms > 0 ? num_transforms : 1;
   if (has_transforms && !(transforms_rows == K || transforms_rows == K * B))
     return fail(SPLAX_ERR_INVALID_ARGUMENT, "project_bwd: transforms must have K or B*K matrices");
@@ -867,11 +914,59 @@ int splax_project_bwd(const float* means3d, int64_t means3d_rows, const float* s
   a.v_quat = v_quat;
   a.v_viewmat = v_viewmat;
   a.v_transforms = v_transforms;
+  a.v_rho = v_rho;
+  a.sel_vrho = v_rho_rows > n;
+  a.aa_eps = aa_eps;
+  a.aa_eps2 = aa_eps2;
+  a.quats_wxyz = quats_wxyz != 0;
+  a.fold_batch = fold_batch != 0;
   st->timer.begin(kProjectBwd, 1, stream);
   launch_project_bwd(a, stream);
   st->timer.end(stream);
   st->units.pairs_bwd += out_rows;
   return finish(*st, stream);
+}
+
+int splax_project_bwd(const float* means3d, int64_t means3d_rows, const float* scales,
+                      int64_t scales_rows, const float* quats_xyzw, int64_t quats_rows,
+                      const float* viewmat, int64_t viewmat_rows, const int32_t* radii,
+                      int64_t radii_rows, const float* conics, int64_t conics_rows,
+                      const float* v_xy, int64_t v_xy_rows, const float* v_depth,
+                      int64_t v_depth_rows, const float* v_conic, int64_t v_conic_rows,
+                      const float* gaussian_transforms, int64_t transforms_rows,
+                      const int32_t* transform_ids, int32_t num_gaussians, int32_t num_transforms,
+                      int32_t has_transforms, float fx, float fy, float glob_scale,
+                      int64_t out_rows, float* v_mean3d, float* v_scale, float* v_quat,
+                      float* v_viewmat, float* v_transforms, void* stream) {
+  return project_bwd_impl(means3d, means3d_rows, scales, scales_rows, quats_xyzw, quats_rows,
+                          viewmat, viewmat_rows, radii, radii_rows, conics, conics_rows, v_xy,
+                          v_xy_rows, v_depth, v_depth_rows, v_conic, v_conic_rows, nullptr, 0,
+                          0.0f, 0.0f, gaussian_transforms, transforms_rows, transform_ids,
+                          num_gaussians, num_transforms, has_transforms, fx, fy, glob_scale,
+                          out_rows, 0, 0, v_mean3d, v_scale, v_quat, v_viewmat, v_transforms,
+                          stream);
+}
+
+int splax_project_bwd_ex(const float* means3d, int64_t means3d_rows, const float* scales,
+                         int64_t scales_rows, const float* quats, int64_t quats_rows,
+                         const float* viewmat, int64_t viewmat_rows, const int32_t* radii,
+                         int64_t radii_rows, const float* conics, int64_t conics_rows,
+                         const float* v_xy, int64_t v_xy_rows, const float* v_depth,
+                         int64_t v_depth_rows, const float* v_conic, int64_t v_conic_rows,
+                         const float* v_rho, int64_t v_rho_rows, float aa_eps, float aa_eps2,
+                         const float* gaussian_transforms, int64_t transforms_rows,
+                         const int32_t* transform_ids, int32_t num_gaussians,
+                         int32_t num_transforms, int32_t has_transforms, float fx, float fy,
+                         float glob_scale, int64_t out_rows, int32_t quats_wxyz,
+                         int32_t fold_batch, float* v_mean3d, float* v_scale, float* v_quat,
+                         float* v_viewmat, float* v_transforms, void* stream) {
+  return project_bwd_impl(means3d, means3d_rows, scales, scales_rows, quats, quats_rows,
+                          viewmat, viewmat_rows, radii, radii_rows, conics, conics_rows, v_xy,
+                          v_xy_rows, v_depth, v_depth_rows, v_conic, v_conic_rows, v_rho,
+                          v_rho_rows, aa_eps, aa_eps2, gaussian_transforms, transforms_rows,
+                          transform_ids, num_gaussians, num_transforms, has_transforms, fx, fy,
+                          glob_scale, out_rows, quats_wxyz, fold_batch, v_mean3d, v_scale,
+                          v_quat, v_viewmat, v_transforms, stream);
 }
 
 int splax_rasterize(const float* colors, int64_t colors_rows, const float* opacities,

@@ -26,6 +26,11 @@ struct ProjectArgs {
   float* conics;
   int32_t* num_tiles_hit;
   int32_t* cum_tiles_hit;
+  // antialiased mode (optional): rho = sqrt(clip(1 - eps (a + c) + eps^2 (a c - b^2), 0, 1))
+  // of the dilated conic per pair, 1 when culled; nullptr skips it
+  float* rho = nullptr;
+  float aa_eps = 0.0f, aa_eps2 = 0.0f;
+  bool quats_wxyz = false;  // quaternions stored scalar-first
 };
 
 struct ProjectBwdArgs {
@@ -35,8 +40,8 @@ struct ProjectBwdArgs {
   const float* viewmat;
   const int32_t* radii;
   const float* conics;
-  const float* v_xy;
-  const float* v_depth;
+  const float* v_xy;     // nullptr: zero cotangent
+  const float* v_depth;  // nullptr: zero cotangent
   const float* v_conic;
   const float* transforms;
   const int32_t* transform_ids;
@@ -50,6 +55,13 @@ struct ProjectBwdArgs {
   float* v_quat;
   float* v_viewmat;     // (B, 4, 4), zeroed by the caller
   float* v_transforms;  // (B, K, 4, 4), zeroed by the caller
+  // antialiased mode (optional): cotangent of the forward's rho, chained into the conic's
+  const float* v_rho = nullptr;
+  bool sel_vrho = false;
+  float aa_eps = 0.0f, aa_eps2 = 0.0f;
+  bool quats_wxyz = false;  // quaternions (and v_quat) stored scalar-first
+  // v_mean3d / v_scale / v_quat hold n rows summed over the B images (shared operands)
+  bool fold_batch = false;
 };
 
 // Per-gaussian record staged by the blend kernels: 3 x float4 =

@@ -70,10 +70,12 @@ __device__ __forceinline__ void project_geom(const ProjectArgs& a, int64_t idx, 
   g.mean[0] = a.means[3 * m_idx];
   g.mean[1] = a.means[3 * m_idx + 1];
   g.mean[2] = a.means[3 * m_idx + 2];
-  q[0] = a.quats[4 * q_idx];
-  q[1] = a.quats[4 * q_idx + 1];
-  q[2] = a.quats[4 * q_idx + 2];
-  q[3] = a.quats[4 * q_idx + 3];
+  // q = (x, y, z, w); wxyz storage (the public API's order) is read without a reorder pass
+  const int qo = a.quats_wxyz ? 1 : 0;
+  q[0] = a.quats[4 * q_idx + qo];
+  q[1] = a.quats[4 * q_idx + qo + 1];
+  q[2] = a.quats[4 * q_idx + qo + 2];
+  q[3] = a.quats[4 * q_idx + (a.quats_wxyz ? 0 : 3)];
   sc[0] = a.scales[3 * s_idx];
   sc[1] = a.scales[3 * s_idx + 1];
   sc[2] = a.scales[3 * s_idx + 2];
@@ -111,7 +113,22 @@ __device__ __forceinline__ void project_geom(const ProjectArgs& a, int64_t idx, 
   }
 }
 
+// Mip-Splatting opacity compensation of a dilated conic (splax/_project/_project.py:95-117),
+// one IEEE operation per step in the order of the reference's expression; eps2 is eps^2 as
+// the caller rounds it. rho2 outside [0, 1] clamps (NaN propagates).
+__device__ __forceinline__ float aa_rho2(float a, float b, float c, float eps, float eps2) {
+  const float t3 = 1.0f - eps * (a + c);
+  const float t7 = eps2 * (a * c - b * b);
+  return t3 + t7;
+}
+__device__ __forceinline__ float aa_rho(float a, float b, float c, float eps, float eps2) {
+  float r2 = aa_rho2(a, b, c, eps, eps2);
+  r2 = r2 < 0.0f ? 0.0f : (r2 > 1.0f ? 1.0f : r2);
+  return sqrtf(r2);
+}
+
 // Projection of one pair; returns its tile count (0 when culled), writing every output row.
+template <bool AA>
 __device__ __forceinline__ int32_t project_one(const ProjectArgs& a, int64_t idx) {
   int64_t bid = idx / a.n, gid = idx % a.n;
   a.xys[2 * idx] = 0.0f;
@@ -122,6 +139,7 @@ __device__ __forceinline__ int32_t project_one(const ProjectArgs& a, int64_t idx
   a.conics[3 * idx + 1] = 0.0f;
   a.conics[3 * idx + 2] = 0.0f;
   a.num_tiles_hit[idx] = 0;
+  if constexpr (AA) a.rho[idx] = 1.0f;
   Geom g;
   float q[4], sc[3];
   project_geom(a, idx, bid, gid, g, q, sc);
@@ -178,6 +196,7 @@ __device__ __forceinline__ int32_t project_one(const ProjectArgs& a, int64_t idx
   a.conics[3 * idx] = ca;
   a.conics[3 * idx + 1] = cb;
   a.conics[3 * idx + 2] = cc;
+  if constexpr (AA) a.rho[idx] = aa_rho(ca, cb, cc, a.aa_eps, a.aa_eps2);
   return count;
 }
 
@@ -185,6 +204,7 @@ constexpr int kProjThreads = 256;
 constexpr int kProjItems = kProjScanTile / kProjThreads;  // pairs per thread
 constexpr int kProjTile = kProjScanTile;
 
+template <bool AA>
 __global__ void __launch_bounds__(kProjThreads)
 project_fwd_kernel(ProjectArgs a, unsigned long long* status, int* ticket, unsigned* err) {
   __shared__ int s_tile;
@@ -199,7 +219,7 @@ project_fwd_kernel(ProjectArgs a, unsigned long long* status, int* ticket, unsig
 #pragma unroll
   for (int k = 0; k < kProjItems; ++k) {
     const int64_t idx = base + k * kProjThreads + tid;
-    s_cnt[k * kProjThreads + tid] = idx < a.total ? project_one(a, idx) : 0;
+    s_cnt[k * kProjThreads + tid] = idx < a.total ? project_one<AA>(a, idx) : 0;
   }
   __syncthreads();
   // each thread scans 4 consecutive pairs; a block scan of the thread sums places them
@@ -251,12 +271,21 @@ project_fwd_kernel(ProjectArgs a, unsigned long long* status, int* ticket, unsig
 
 constexpr int kBwdThreads = 256;
 
+// FOLD: one thread per gaussian, looping over the B images and summing the gaussian's
+// cotangents over them in registers (means, scales and quats shared by the images: the sum
+// the caller would otherwise take over B*n rows). Otherwise one thread per (image, gaussian).
+template <bool AA, bool FOLD>
 __global__ void __launch_bounds__(kBwdThreads) project_bwd_kernel(ProjectBwdArgs a) {
   const int64_t blocks_per_image = (a.n + kBwdThreads - 1) / kBwdThreads;
-  const int64_t image_id = blockIdx.x / blocks_per_image;
-  const int64_t gid = (blockIdx.x % blocks_per_image) * kBwdThreads + threadIdx.x;
-  const int64_t idx = image_id * a.n + gid;
+  const int64_t img0 = FOLD ? 0 : blockIdx.x / blocks_per_image;
+  const int64_t img1 = FOLD ? a.B : img0 + 1;
+  const int64_t gid = (FOLD ? blockIdx.x : blockIdx.x % blocks_per_image) * kBwdThreads +
+                      threadIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float acc_mean[3] = {0.0f, 0.0f, 0.0f}, acc_scale[3] = {0.0f, 0.0f, 0.0f};
+  float acc_quat[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  for (int64_t image_id = img0; image_id < img1; ++image_id) {
+  const int64_t idx = image_id * a.n + gid;
   // 12 viewmat entries, then 12 transform entries
   float vv[12];
 #pragma unroll
@@ -279,6 +308,7 @@ __global__ void __launch_bounds__(kBwdThreads) project_bwd_kernel(ProjectBwdArgs
     pa.n = a.n; pa.num_transforms = a.num_transforms; pa.has_transforms = a.has_transforms;
     pa.sel_means = a.sel_means; pa.sel_scales = a.sel_scales; pa.sel_quats = a.sel_quats;
     pa.sel_view = a.sel_view; pa.sel_transforms = a.sel_transforms;
+    pa.quats_wxyz = a.quats_wxyz;
     pa.glob_scale = a.glob_scale;
     Geom g;
     float q[4], sc[3];
@@ -304,15 +334,29 @@ __global__ void __launch_bounds__(kBwdThreads) project_bwd_kernel(ProjectBwdArgs
     const float* conic = a.conics + 3 * c_idx;
     const float* vcon = a.v_conic + 3 * vc_idx;
     float X0 = conic[0], X1 = conic[1], X3 = conic[2];
-    float G0 = vcon[0], G1 = 0.5f * vcon[1], G3 = vcon[2];
+    float G0 = vcon[0], G1 = vcon[1], G3 = vcon[2];
+    if constexpr (AA) {
+      // rho = sqrt(clip(rho2, 0, 1)): d rho / d rho2 = 1 / (2 rho) inside [0, 1], else 0;
+      // d rho2 / d(a, b, c) = (-eps + eps^2 c, -2 eps^2 b, -eps + eps^2 a)
+      const float vr = a.v_rho[a.sel_vrho ? idx : gid];
+      const float r2 = aa_rho2(X0, X1, X3, a.aa_eps, a.aa_eps2);
+      if (r2 >= 0.0f && r2 <= 1.0f) {
+        const float d = vr / (2.0f * sqrtf(r2));
+        G0 += d * (a.aa_eps2 * X3 - a.aa_eps);
+        G1 += d * (-2.0f * a.aa_eps2 * X1);
+        G3 += d * (a.aa_eps2 * X0 - a.aa_eps);
+      }
+    }
+    G1 = 0.5f * G1;
     float XG0 = X0 * G0 + X1 * G1, XG1 = X0 * G1 + X1 * G3;
     float XG2 = X1 * G0 + X3 * G1, XG3 = X1 * G1 + X3 * G3;
     float S0 = XG0 * X0 + XG1 * X1, S1 = XG0 * X1 + XG1 * X3;
     float S2 = XG2 * X0 + XG3 * X1, S3 = XG2 * X1 + XG3 * X3;
     float vc0 = -S0, vc1 = -(S1 + S2), vc2 = -S3;
     // _proj_vjp (:487-533)
-    const float vx0 = a.v_xy[2 * vx_idx], vx1 = a.v_xy[2 * vx_idx + 1];
-    const float vdep = a.v_depth[vd_idx];
+    const float vx0 = a.v_xy ? a.v_xy[2 * vx_idx] : 0.0f;
+    const float vx1 = a.v_xy ? a.v_xy[2 * vx_idx + 1] : 0.0f;
+    const float vdep = a.v_depth ? a.v_depth[vd_idx] : 0.0f;
     float tx = p[0], ty = p[1], tz = p[2];
     float rz3 = rz2 * rz;
     float rw = 1.0f / (tz + 1e-6f);
@@ -364,13 +408,12 @@ __global__ void __launch_bounds__(kBwdThreads) project_bwd_kernel(ProjectBwdArgs
 #pragma unroll
       for (int k = 0; k < 9; ++k) v_M[k] = v_M_world[k];
     }
-    a.v_mean3d[3 * idx] = v_mean_out[0];
-    a.v_mean3d[3 * idx + 1] = v_mean_out[1];
-    a.v_mean3d[3 * idx + 2] = v_mean_out[2];
+#pragma unroll
+    for (int c = 0; c < 3; ++c) acc_mean[c] += v_mean_out[c];
     // _scale_vjp (:560-567)
 #pragma unroll
     for (int c = 0; c < 3; ++c)
-      a.v_scale[3 * idx + c] = ((R[c] * v_M[c] + R[3 + c] * v_M[3 + c]) + R[6 + c] * v_M[6 + c]) * gs;
+      acc_scale[c] += ((R[c] * v_M[c] + R[3 + c] * v_M[3 + c]) + R[6 + c] * v_M[6 + c]) * gs;
     // _quat_vjp (:570-599), written xyzw
     float vR[9];
 #pragma unroll
@@ -385,10 +428,10 @@ __global__ void __launch_bounds__(kBwdThreads) project_bwd_kernel(ProjectBwdArgs
                          w * (vR[2] - vR[6]));
     float vq_z = 2.0f * (x * (vR[6] + vR[2]) + y * (vR[7] + vR[5]) - 2.0f * z * (vR[0] + vR[4]) +
                          w * (vR[3] - vR[1]));
-    a.v_quat[4 * idx] = vq_x;
-    a.v_quat[4 * idx + 1] = vq_y;
-    a.v_quat[4 * idx + 2] = vq_z;
-    a.v_quat[4 * idx + 3] = vq_w;
+    acc_quat[0] += vq_x;
+    acc_quat[1] += vq_y;
+    acc_quat[2] += vq_z;
+    acc_quat[3] += vq_w;
     // _view_vjp (:602-606)
     float Jt[9], JtvT[9];
     mat_T(J, Jt);
@@ -399,17 +442,6 @@ __global__ void __launch_bounds__(kBwdThreads) project_bwd_kernel(ProjectBwdArgs
       for (int c = 0; c < 3; ++c) vv[4 * r + c] = v_p[r] * g.mean[c] + JtvT[3 * r + c];
       vv[4 * r + 3] = v_p[r];
     }
-  } else if (gid < a.n) {
-    a.v_mean3d[3 * idx] = 0.0f;
-    a.v_mean3d[3 * idx + 1] = 0.0f;
-    a.v_mean3d[3 * idx + 2] = 0.0f;
-    a.v_scale[3 * idx] = 0.0f;
-    a.v_scale[3 * idx + 1] = 0.0f;
-    a.v_scale[3 * idx + 2] = 0.0f;
-    a.v_quat[4 * idx] = 0.0f;
-    a.v_quat[4 * idx + 1] = 0.0f;
-    a.v_quat[4 * idx + 2] = 0.0f;
-    a.v_quat[4 * idx + 3] = 0.0f;
   }
   // per-image viewmat cotangent: warp reduce-scatter, then one atomic per entry per warp
   // (rows image_id*4 + r of the (4B, 4) output; row 3 stays zero)
@@ -436,6 +468,30 @@ __global__ void __launch_bounds__(kBwdThreads) project_bwd_kernel(ProjectBwdArgs
 #pragma unroll
       for (int k = 0; k < 12; ++k) atomicAdd(&out[k], vtf[k]);
     }
+    __syncthreads();  // s_tmin / s_tmax are reset by the next image
+  }
+  }  // images
+  if (gid < a.n) {
+    // one row per gaussian (FOLD) or per (image, gaussian); quats in the input's order
+    const int64_t row = FOLD ? gid : img0 * a.n + gid;
+    a.v_mean3d[3 * row] = acc_mean[0];
+    a.v_mean3d[3 * row + 1] = acc_mean[1];
+    a.v_mean3d[3 * row + 2] = acc_mean[2];
+    a.v_scale[3 * row] = acc_scale[0];
+    a.v_scale[3 * row + 1] = acc_scale[1];
+    a.v_scale[3 * row + 2] = acc_scale[2];
+    float* vq = a.v_quat + 4 * row;
+    if (a.quats_wxyz) {
+      vq[0] = acc_quat[3];
+      vq[1] = acc_quat[0];
+      vq[2] = acc_quat[1];
+      vq[3] = acc_quat[2];
+    } else {
+      vq[0] = acc_quat[0];
+      vq[1] = acc_quat[1];
+      vq[2] = acc_quat[2];
+      vq[3] = acc_quat[3];
+    }
   }
   (void)warp;
 }
@@ -446,8 +502,12 @@ void launch_project_fwd(const ProjectArgs& a, unsigned long long* status, int* t
                         unsigned* err, cudaStream_t stream) {
   const int64_t blocks = project_scan_tiles(a.total);
   if (blocks == 0) return;
-  project_fwd_kernel<<<static_cast<unsigned>(blocks), kProjThreads, 0, stream>>>(a, status, ticket,
-                                                                                 err);
+  if (a.rho)
+    project_fwd_kernel<true><<<static_cast<unsigned>(blocks), kProjThreads, 0, stream>>>(
+        a, status, ticket, err);
+  else
+    project_fwd_kernel<false><<<static_cast<unsigned>(blocks), kProjThreads, 0, stream>>>(
+        a, status, ticket, err);
 }
 
 int64_t project_scan_tiles(int64_t total) { return (total + kProjTile - 1) / kProjTile; }
@@ -456,7 +516,14 @@ void launch_project_bwd(const ProjectBwdArgs& a, cudaStream_t stream) {
   const int64_t blocks_per_image = (a.n + kBwdThreads - 1) / kBwdThreads;
   const int64_t blocks = blocks_per_image * a.B;
   if (blocks == 0) return;
-  project_bwd_kernel<<<static_cast<unsigned>(blocks), kBwdThreads, 0, stream>>>(a);
+  const unsigned g = static_cast<unsigned>(a.fold_batch ? blocks_per_image : blocks);
+  if (a.v_rho) {
+    if (a.fold_batch) project_bwd_kernel<true, true><<<g, kBwdThreads, 0, stream>>>(a);
+    else project_bwd_kernel<true, false><<<g, kBwdThreads, 0, stream>>>(a);
+  } else {
+    if (a.fold_batch) project_bwd_kernel<false, true><<<g, kBwdThreads, 0, stream>>>(a);
+    else project_bwd_kernel<false, false><<<g, kBwdThreads, 0, stream>>>(a);
+  }
 }
 
 }  // namespace splax
