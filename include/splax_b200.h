@@ -193,6 +193,24 @@ int splax_rasterize_bwd_depth(const float *colors, int64_t colors_rows, const fl
                               float *v_opacity, float *v_xy, float *v_conic, float *v_depths,
                               void *stream);
 
+/* Rasterize backward with options (no FFI counterpart: the reference's JAX side sums the
+ * per-image gradients of operands shared by the batch): the plain or depth variant (depth when
+ * v_out_depth and v_depths are both non-NULL), and fold_colors / fold_opacity (1: v_colors /
+ * v_opacity get n rows, each the sum over the images; needs n-row colors / opacities). */
+int splax_rasterize_bwd_ex(const float *colors, int64_t colors_rows, const float *opacities,
+                           int64_t opacities_rows, const float *map_opacities,
+                           int64_t map_opacities_rows, const float *background,
+                           int64_t background_rows, const float *xys, const float *depths,
+                           const int32_t *radii, const float *conics,
+                           const int32_t *cum_tiles_hit, int64_t geom_rows,
+                           const float *final_Ts, const int32_t *final_idx,
+                           const float *v_out_img, int64_t v_out_rows, const float *v_out_depth,
+                           int64_t v_out_depth_rows, int32_t num_gaussians, int32_t img_h,
+                           int32_t img_w, int64_t grad_rows, int32_t key_bits,
+                           int32_t fold_colors, int32_t fold_opacity, float *v_colors,
+                           float *v_opacity, float *v_xy, float *v_conic, float *v_depths,
+                           void *stream);
+
 /* Reuse of the forward's sort by its backward (the reference re-sorts in every backward,
  * splax/_rasterize/_kernels.py:422-424; the sort is deterministic, so reusing it gives identical
  * results). splax_last_sort_token() returns the token of the sort done by the calling thread's

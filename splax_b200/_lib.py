@@ -46,6 +46,8 @@ SIGNATURES: dict[str, list] = {
                             I32, I32, I64, I32, P, P, P, P, P],
     "splax_rasterize_bwd_depth": [P, I64, P, I64, P, I64, P, I64, P, P, P, P, P, I64, P, P, P,
                                   I64, P, I64, I32, I32, I32, I64, I32, P, P, P, P, P, P],
+    "splax_rasterize_bwd_ex": [P, I64, P, I64, P, I64, P, I64, P, P, P, P, P, I64, P, P, P, I64,
+                               P, I64, I32, I32, I32, I64, I32, I32, I32, P, P, P, P, P, P],
     "splax_sort_and_bin": [P, P, P, P, P, I64, P, I32, I32, I32, I32, I32, P, I64, P, P, P, P, P],
     "splax_clear_cache": [],
     "splax_scratch_info": [P, I32],

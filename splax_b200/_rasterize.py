@@ -74,29 +74,29 @@ class _RasterizeFn(torch.autograd.Function):
         lib = _lib.load()
         vo = (_f32(v_img) if v_img is not None
               else torch.zeros((Bt * img_h, img_w, 3), device=dev, dtype=torch.float32))
-        v_colors = torch.empty((rows, 3), device=dev, dtype=torch.float32)
-        v_opac = torch.empty((rows,), device=dev, dtype=torch.float32)
+        # colours / opacities shared by the images get their gradient summed in-kernel
+        fold_c = bool(B) and col.numel() // 3 == n
+        fold_o = bool(B) and op.numel() == n
+        v_colors = torch.empty((n if fold_c else rows, 3), device=dev, dtype=torch.float32)
+        v_opac = torch.empty((n if fold_o else rows,), device=dev, dtype=torch.float32)
         v_xy = torch.empty((rows, 2), device=dev, dtype=torch.float32)
         v_conic = torch.empty((rows, 3), device=dev, dtype=torch.float32)
+        vd, v_depths = None, None
+        if with_depth:
+            v_dimg = rest[0]
+            vd = (_f32(v_dimg) if v_dimg is not None
+                  else torch.zeros((Bt * img_h, img_w), device=dev, dtype=torch.float32))
+            v_depths = torch.empty((rows,), device=dev, dtype=torch.float32)
         p = _lib.ptr
-        common = [p(col), col.numel() // 3, p(op), op.numel(), p(mo), mo.numel(), p(bg),
-                  bg.numel() // 3, p(xy), p(dp), p(rd), p(cn), p(cum), rows, p(final_Ts),
-                  p(final_idx), p(vo), vo.numel() // (3 * img_w)]
-        v_depths = None
         with torch.cuda.device(dev):
             lib.splax_reuse_sort(ctx.sort_token)
-            if with_depth:
-                v_dimg = rest[0]
-                vd = (_f32(v_dimg) if v_dimg is not None
-                      else torch.zeros((Bt * img_h, img_w), device=dev, dtype=torch.float32))
-                v_depths = torch.empty((rows,), device=dev, dtype=torch.float32)
-                rc = lib.splax_rasterize_bwd_depth(
-                    *common, p(vd), vd.numel() // img_w, n, img_h, img_w, rows, key_bits,
-                    p(v_colors), p(v_opac), p(v_xy), p(v_conic), p(v_depths), _lib.stream_of(col))
-            else:
-                rc = lib.splax_rasterize_bwd(
-                    *common, n, img_h, img_w, rows, key_bits, p(v_colors), p(v_opac), p(v_xy),
-                    p(v_conic), _lib.stream_of(col))
+            rc = lib.splax_rasterize_bwd_ex(
+                p(col), col.numel() // 3, p(op), op.numel(), p(mo), mo.numel(), p(bg),
+                bg.numel() // 3, p(xy), p(dp), p(rd), p(cn), p(cum), rows, p(final_Ts),
+                p(final_idx), p(vo), vo.numel() // (3 * img_w), p(vd),
+                0 if vd is None else vd.numel() // img_w, n, img_h, img_w, rows, key_bits,
+                int(fold_c), int(fold_o), p(v_colors), p(v_opac), p(v_xy), p(v_conic),
+                p(v_depths), _lib.stream_of(col))
         _lib.check(rc)
         cs, os_, xs, ds, ks = ctx.shapes
 

@@ -641,7 +641,8 @@ int rasterize_bwd_common(const float* colors, int64_t colors_rows, const float* 
                          const float* v_out_depth, int64_t v_out_depth_rows, int32_t n,
                          int32_t img_h, int32_t img_w, int64_t grad_rows, int32_t key_bits,
                          float* v_colors, float* v_opacity, float* v_xy, float* v_conic,
-                         float* v_depths, cudaStream_t stream) {
+                         float* v_depths, bool fold_colors, bool fold_opacity,
+                         cudaStream_t stream) {
   if (n <= 0 || img_h <= 0 || img_w <= 0 || geom_rows <= 0 || geom_rows % n != 0 ||
       grad_rows <= 0 || grad_rows % n != 0)
     return fail(SPLAX_ERR_INVALID_ARGUMENT, "rasterize_bwd: invalid n, image size or rows");
@@ -657,12 +658,17 @@ int rasterize_bwd_common(const float* colors, int64_t colors_rows, const float* 
                 "rasterize_bwd: operand rows must be n or B*n (background 1 or B_out)");
   if (key_bits != 0 && key_bits != 32 && key_bits != 64)
     return fail(SPLAX_ERR_INVALID_ARGUMENT, "rasterize_bwd: key_bits must be 0, 32 or 64");
+  if ((fold_colors && colors_rows != n) || (fold_opacity && opacities_rows != n))
+    return fail(SPLAX_ERR_INVALID_ARGUMENT,
+                "rasterize_bwd: folded colour / opacity gradients need shared operands");
   DeviceState* st;
   int rc = current_state(&st);
   if (rc) return rc;
   std::lock_guard<std::mutex> lk(st->mu);
-  SPLAX_CUDA(cudaMemsetAsync(v_colors, 0, sizeof(float) * 3 * grad_rows, stream));
-  SPLAX_CUDA(cudaMemsetAsync(v_opacity, 0, sizeof(float) * grad_rows, stream));
+  SPLAX_CUDA(cudaMemsetAsync(v_colors, 0, sizeof(float) * 3 * (fold_colors ? n : grad_rows),
+                             stream));
+  SPLAX_CUDA(cudaMemsetAsync(v_opacity, 0, sizeof(float) * (fold_opacity ? n : grad_rows),
+                             stream));
   SPLAX_CUDA(cudaMemsetAsync(v_xy, 0, sizeof(float) * 2 * grad_rows, stream));
   SPLAX_CUDA(cudaMemsetAsync(v_conic, 0, sizeof(float) * 3 * grad_rows, stream));
   if (v_depths) SPLAX_CUDA(cudaMemsetAsync(v_depths, 0, sizeof(float) * grad_rows, stream));
@@ -705,6 +711,8 @@ int rasterize_bwd_common(const float* colors, int64_t colors_rows, const float* 
   ba.v_xy = v_xy;
   ba.v_conic = v_conic;
   ba.v_depths = v_depths;
+  ba.fold_colors = fold_colors;
+  ba.fold_opacity = fold_opacity;
   ba.work = st->work_bwd();
   st->timer.begin(kRasterBwd, 1, stream);
   launch_raster_bwd(ba, stream);
@@ -1014,7 +1022,7 @@ int splax_rasterize_bwd(const float* colors, int64_t colors_rows, const float* o
                               radii, conics, cum_tiles_hit, geom_rows, final_Ts, final_idx,
                               v_out_img, v_out_rows, nullptr, 0, num_gaussians, img_h, img_w,
                               grad_rows, key_bits, v_colors, v_opacity, v_xy, v_conic, nullptr,
-                              static_cast<cudaStream_t>(stream));
+                              false, false, static_cast<cudaStream_t>(stream));
 }
 
 int splax_rasterize_bwd_depth(const float* colors, int64_t colors_rows, const float* opacities,
@@ -1037,7 +1045,32 @@ int splax_rasterize_bwd_depth(const float* colors, int64_t colors_rows, const fl
                               radii, conics, cum_tiles_hit, geom_rows, final_Ts, final_idx,
                               v_out_img, v_out_rows, v_out_depth, v_out_depth_rows, num_gaussians,
                               img_h, img_w, grad_rows, key_bits, v_colors, v_opacity, v_xy,
-                              v_conic, v_depths, static_cast<cudaStream_t>(stream));
+                              v_conic, v_depths, false, false, static_cast<cudaStream_t>(stream));
+}
+
+int splax_rasterize_bwd_ex(const float* colors, int64_t colors_rows, const float* opacities,
+                           int64_t opacities_rows, const float* map_opacities,
+                           int64_t map_opacities_rows, const float* background,
+                           int64_t background_rows, const float* xys, const float* depths,
+                           const int32_t* radii, const float* conics,
+                           const int32_t* cum_tiles_hit, int64_t geom_rows,
+                           const float* final_Ts, const int32_t* final_idx,
+                           const float* v_out_img, int64_t v_out_rows, const float* v_out_depth,
+                           int64_t v_out_depth_rows, int32_t num_gaussians, int32_t img_h,
+                           int32_t img_w, int64_t grad_rows, int32_t key_bits,
+                           int32_t fold_colors, int32_t fold_opacity, float* v_colors,
+                           float* v_opacity, float* v_xy, float* v_conic, float* v_depths,
+                           void* stream) {
+  if ((v_out_depth == nullptr) != (v_depths == nullptr))
+    return fail(SPLAX_ERR_INVALID_ARGUMENT,
+                "rasterize_bwd_ex: v_out_depth and v_depths must be given together");
+  return rasterize_bwd_common(colors, colors_rows, opacities, opacities_rows, map_opacities,
+                              map_opacities_rows, background, background_rows, xys, depths,
+                              radii, conics, cum_tiles_hit, geom_rows, final_Ts, final_idx,
+                              v_out_img, v_out_rows, v_out_depth, v_out_depth_rows, num_gaussians,
+                              img_h, img_w, grad_rows, key_bits, v_colors, v_opacity, v_xy,
+                              v_conic, v_depths, fold_colors != 0, fold_opacity != 0,
+                              static_cast<cudaStream_t>(stream));
 }
 
 int splax_sort_and_bin(const float* xys, const float* depths, const int32_t* radii,

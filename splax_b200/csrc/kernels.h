@@ -185,6 +185,8 @@ struct RasterBwdArgs {
   float* v_xy;
   float* v_conic;
   float* v_depths;
+  // v_colors / v_opacity hold n rows, each summed over the images (shared operands)
+  bool fold_colors = false, fold_opacity = false;
   unsigned long long* work;  // optional: [0] evaluations, [1] contributions
 };
 void launch_raster_bwd(const RasterBwdArgs& a, cudaStream_t stream);

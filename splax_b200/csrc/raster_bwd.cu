@@ -155,20 +155,28 @@ raster_bwd_kernel(RasterBwdArgs a) {
     }
   }
 
-  // gradient slot this lane owns after a reduce-scatter (fixed by the lane id)
+  // gradient slot this lane owns after a reduce-scatter (fixed by the lane id): output row =
+  // staged flat id + my_add, i.e. the (image, gaussian) row, or the gaussian row for the
+  // colour / opacity gradients summed over the images
   float* my_base = nullptr;
   int my_stride = 0;
+  int64_t my_add = og_base;
   {
     float dummy[K];
 #pragma unroll
     for (int k = 0; k < K; ++k) dummy[k] = 0.0f;
     const int c = warp_reduce_scatter<K>(dummy, lane);
+    const int64_t to_gaussian = a.sel_geom ? -geom_image * a.n : 0;
     if (c >= 0) {
-      if (c < 3) { my_base = a.v_colors + c; my_stride = 3; }
-      else if (c < 6) { my_base = a.v_conic + (c - 3); my_stride = 3; }
+      if (c < 3) {
+        my_base = a.v_colors + c; my_stride = 3;
+        if (a.fold_colors) my_add = to_gaussian;
+      } else if (c < 6) { my_base = a.v_conic + (c - 3); my_stride = 3; }
       else if (c < 8) { my_base = a.v_xy + (c - 6); my_stride = 2; }
-      else if (c == 8) { my_base = a.v_opacity; my_stride = 1; }
-      else { my_base = a.v_depths; my_stride = 1; }
+      else if (c == 8) {
+        my_base = a.v_opacity; my_stride = 1;
+        if (a.fold_opacity) my_add = to_gaussian;
+      } else { my_base = a.v_depths; my_stride = 1; }
     }
   }
 
@@ -254,8 +262,7 @@ raster_bwd_kernel(RasterBwdArgs a) {
       if constexpr (DEPTH) v[9] = acc.d.x + acc.d.y;
       warp_reduce_scatter<K>(v, lane);
       if (my_base != nullptr && v[0] != 0.0f) {
-        const int64_t og = og_base + s_id[t];
-        atomicAdd(my_base + og * my_stride, v[0]);
+        atomicAdd(my_base + (s_id[t] + my_add) * my_stride, v[0]);
       }
     }
   }
