@@ -55,6 +55,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--n", type=int, default=None, help="override the gaussian count (debug)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", type=int, default=CONFIG, choices=[2, 3],
+                    help="2: the headline fwd+bwd step (default); 3: the batched training step")
     return ap.parse_args()
 
 
@@ -165,10 +167,136 @@ def reference_arm(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# Config 3 training step: the reference's per-group learning rates (scripts/train_colmap.py:
+# 867-871), scaled by sqrt(B) for batched training (:609-610), and its D-SSIM weight (:872)
+TRAIN_LRS = {"means": 1.5e-3, "log_scales": 5e-3, "quats": 1e-3, "colors_logit": 1e-2,
+             "opac_logit": 5e-2}
+SSIM_LAMBDA = 0.2
+
+
+def train_bench(args) -> None:
+    """Config 3: one batched training step = render_log fwd+bwd of B views, fused L1 + D-SSIM
+    loss, NCCL all-reduce of the gradients (camera shards), fused per-group Adam."""
+    import torch
+    import torch.distributed as dist
+
+    import splax_b200 as sx
+    from splax_b200 import _lib, utils
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+    scene = utils.synthetic_scene(3, n=args.n)
+    B, H, W, f = scene["B"], scene["H"], scene["W"], scene["f"]
+    n = scene["means"].shape[0]
+    if B % world:
+        raise SystemExit(f"{B} cameras do not split over {world} ranks")
+    per = B // world
+    cams = slice(rank * per, (rank + 1) * per)
+    targets_np = utils.target_images(scene)
+    logit = lambda x: np.log(x) - np.log1p(-x)  # noqa: E731
+    host = {"means": scene["means"], "log_scales": np.log(scene["scales"]),
+            "quats": scene["quats"], "colors_logit": logit(np.clip(scene["colors"], 1e-4, 1 - 1e-4)),
+            "opac_logit": logit(scene["opacities"])}
+    params = [torch.tensor(host[k].astype(np.float32), device=dev).requires_grad_()
+              for k in TRAIN_LRS]
+    opt = sx.Adam(params, [lr * float(np.sqrt(B)) for lr in TRAIN_LRS.values()])
+    views = torch.tensor(scene["viewmats"][cams], device=dev)
+    target = torch.tensor(targets_np[cams], device=dev)
+    bg = torch.tensor(scene["background"], device=dev)
+    kw = dict(background=bg, img_shape=(H, W), f=(f, f))
+
+    def step(vm, tgt):
+        for p in params:
+            p.grad = None
+        imgs, _ = sx.render_log(*params, viewmat=vm, **kw)
+        loss = sx.l1_dssim_loss(imgs, tgt, ssim_lambda=SSIM_LAMBDA, views_total=B)
+        loss.backward()
+        if world > 1:
+            flat = torch.cat([p.grad.reshape(-1) for p in params])
+            dist.all_reduce(flat)
+            grads = list(torch.split(flat, [p.numel() for p in params]))
+            grads = [g.view_as(p) for g, p in zip(grads, params)]
+            dist.all_reduce(loss.detach())
+        else:
+            grads = [p.grad for p in params]
+        opt.step(grads)
+        return loss
+
+    for _ in range(args.warmup):
+        step(views, target)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+    sampler = ClockSampler(uuid) if rank == 0 else None
+    _lib.profile_enable(timing=True, count_work=False)
+    _lib.profile_reset()
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        loss = step(views, target)
+    t1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop() if sampler else None
+    prof = _lib.profile_report()
+    _lib.profile_enable(timing=False, count_work=False)
+    ms_t = torch.tensor([t0.elapsed_time(t1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+    loss_v = float(loss.item())
+    if not np.isfinite(loss_v):
+        raise SystemExit("non-finite training loss")
+    if rank == 0:
+        kern = prof["kernels"]
+        total_ms = {k: v["ms"] for k, v in kern.items()}
+        line = {
+            "metric": "config 3 batched training step frames/s (3M gaussians, 840x1297, 32 cams)",
+            "value": B * args.steps / (ms / 1e3), "unit": "frames/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "steps_per_s": args.steps / (ms / 1e3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded, config 3 distributions)",
+            "config": {"workload": "config 3: render_log fwd+bwd, L1 + 0.2 D-SSIM, all-reduce, "
+                                   "per-group Adam", "gaussians": n, "cams_per_gpu": per,
+                       "parallelism": f"camera-sharded dp{world}"},
+            "loss": loss_v,
+            "kernels": {k: {**v, "share": v["ms"] / max(sum(total_ms.values()), 1e-9)}
+                        for k, v in kern.items()},
+            "clocks": clocks,
+            "gpu_launches": int(sum(k["kernels"] for k in kern.values())),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main() -> None:
     args = parse()
     if args.impl == "reference":
         reference_arm(args)
+        return
+    if args.config == 3:
+        train_bench(args)
         return
 
     import torch

@@ -248,6 +248,34 @@ int splax_mse_loss(const float *img, const float *target, int64_t count, float d
 int splax_mse_loss_bwd(const float *img, const float *target, int64_t count, float denom,
                        const float *v_loss, float *grad, void *stream);
 
+/* Fused photometric loss of the batched training step, (1 - lambda) L1 + lambda D-SSIM, for
+ * B RGB images (B, H, W, 3) against targets of the same shape (device pointers). No
+ * counterpart in the reference, whose training step takes it in JAX with dm_pix.ssim
+ * (scripts/train_colmap.py:202-221): per view mean |img - gt| and 1 - ssim(img, gt), averaged
+ * over views; SSIM with an 11-tap Gaussian window (sigma 1.5, VALID), k1 0.01, k2 0.03,
+ * max_val 1, variances floored at eps_f32^2 and the covariance clamped to sqrt(var var).
+ * views_total is the number of views over all ranks (B on one GPU): the loss written is this
+ * rank's share, so the shares of all ranks add up to the loss. Needs H, W >= 11.
+ * Deterministic (fixed-order fp64 partial sums). */
+int splax_l1_dssim_loss(const float *img, const float *target, int32_t B, int32_t H, int32_t W,
+                        int32_t views_total, float ssim_lambda, float *loss, void *stream);
+
+/* Gradient of splax_l1_dssim_loss with respect to img, scaled by the cotangent v_loss[0] (a
+ * device float, no host synchronisation); grad has img's shape and may alias neither input. */
+int splax_l1_dssim_loss_bwd(const float *img, const float *target, int32_t B, int32_t H,
+                            int32_t W, int32_t views_total, float ssim_lambda,
+                            const float *v_loss, float *grad, void *stream);
+
+/* Fused per-parameter Adam update, in place, of num_arrays fp32 parameter arrays (device
+ * pointers in host arrays: params, grads, first / second moments, element counts, learning
+ * rates). No counterpart in the reference, whose training step uses optax.adam per group
+ * (scripts/train_colmap.py:639-645); the update is optax's scale_by_adam then -lr:
+ * m = (1 - b1) g + b1 m, v = (1 - b2) g^2 + b2 v, p -= lr (m / (1 - b1^step)) /
+ * (sqrt(v / (1 - b2^step)) + eps), with step >= 1 the update count after this step. */
+int splax_adam_step(int32_t num_arrays, float *const *params, const float *const *grads,
+                    float *const *exp_avg, float *const *exp_avg_sq, const int64_t *sizes,
+                    const float *lrs, int32_t step, float b1, float b2, float eps, void *stream);
+
 /* clear_cache, splax/_cache.py:158-164: release the scratch of every device. */
 void splax_clear_cache(void);
 

@@ -32,6 +32,8 @@ SOURCES = {
     "capi.cu": [],
     "project_noalloc.cu": [],
     "loss.cu": [],
+    "ssim.cu": [],
+    "optim.cu": [],
 }
 
 

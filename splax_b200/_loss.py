@@ -1,9 +1,10 @@
 """Fused image losses for training steps around the render.
 
 ``mse_loss`` is the mean-squared-error objective of the benchmark configurations 1 and 2,
-sum((img - target)^2) / denom, as one library kernel per direction (no counterpart in the
-reference, whose callers take the loss in JAX). Differentiable with respect to ``img``; the
-target gets no gradient.
+sum((img - target)^2) / denom; ``l1_dssim_loss`` is the photometric loss of the batched
+training step (config 3; scripts/train_colmap.py:202-221), (1 - lambda) L1 + lambda D-SSIM.
+Each is one library kernel per direction (no counterpart in the reference, whose callers take
+the loss in JAX). Differentiable with respect to the image; the target gets no gradient.
 """
 
 from __future__ import annotations
@@ -52,3 +53,51 @@ def mse_loss(img: torch.Tensor, target: torch.Tensor, *, denom: float | None = N
     if not d > 0:
         raise ValueError(f"denom must be positive, got {d}")
     return _MSELossFn.apply(img, target, d)
+
+
+class _L1DssimFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, img, target, views_total, ssim_lambda):
+        dev = _lib.require_cuda(img, target)
+        if img.shape != target.shape or img.dim() not in (3, 4) or img.shape[-1] != 3:
+            raise ValueError(f"img {tuple(img.shape)} and target {tuple(target.shape)} must be "
+                             "equal (H, W, 3) or (B, H, W, 3)")
+        a = img.detach().to(torch.float32).contiguous()
+        t = target.detach().to(torch.float32).contiguous()
+        B = a.shape[0] if a.dim() == 4 else 1
+        H, W = a.shape[-3], a.shape[-2]
+        loss = torch.empty((), device=dev, dtype=torch.float32)
+        lib = _lib.load()
+        with torch.cuda.device(dev):
+            rc = lib.splax_l1_dssim_loss(_lib.ptr(a), _lib.ptr(t), B, H, W, int(views_total),
+                                         float(ssim_lambda), _lib.ptr(loss), _lib.stream_of(a))
+        _lib.check(rc)
+        ctx.save_for_backward(a, t)
+        ctx.args = (B, H, W, int(views_total), float(ssim_lambda), img.dtype)
+        return loss
+
+    @staticmethod
+    def backward(ctx, v_loss):
+        a, t = ctx.saved_tensors
+        B, H, W, views_total, lam, dtype = ctx.args
+        g = torch.empty_like(a)
+        v = v_loss.detach().to(torch.float32).reshape(()).contiguous()
+        lib = _lib.load()
+        with torch.cuda.device(a.device):
+            rc = lib.splax_l1_dssim_loss_bwd(_lib.ptr(a), _lib.ptr(t), B, H, W, views_total, lam,
+                                             _lib.ptr(v), _lib.ptr(g), _lib.stream_of(a))
+        _lib.check(rc)
+        return g.to(dtype), None, None, None
+
+
+def l1_dssim_loss(img: torch.Tensor, target: torch.Tensor, *, ssim_lambda: float = 0.2,
+                  views_total: int | None = None) -> torch.Tensor:
+    """(1 - ssim_lambda) mean|img - target| + ssim_lambda (1 - SSIM), averaged over the views of
+    a (B, H, W, 3) stack (or one (H, W, 3) view), as the reference's make_step computes it with
+    dm_pix.ssim. With camera shards pass the global view count as ``views_total``: each rank
+    then gets its additive share of the loss and the global gradient of its images."""
+    B = img.shape[0] if img.dim() == 4 else 1
+    V = B if views_total is None else int(views_total)
+    if V < B:
+        raise ValueError(f"views_total={V} is less than the {B} views given")
+    return _L1DssimFn.apply(img, target, V, float(ssim_lambda))

@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <memory>
@@ -81,10 +82,10 @@ std::atomic<bool> g_count_work{false};
 constexpr int kWorkWords = 6;  // device work counters (see DeviceState::work)
 
 enum Kind { kProjectFwd, kProjectBwd, kDepthMinmax, kPairKeys, kPairSort, kPairScan, kEmit,
-            kRadixSort, kTileBins, kRasterFwd, kRasterBwd, kNumKinds };
+            kRadixSort, kTileBins, kRasterFwd, kRasterBwd, kLoss, kOptim, kNumKinds };
 const char* kKindNames[kNumKinds] = {"project_fwd", "project_bwd", "depth_minmax", "pair_keys",
                                      "pair_sort", "pair_scan", "emit_keys", "radix_sort",
-                                     "tile_bins", "raster_fwd", "raster_bwd"};
+                                     "tile_bins", "raster_fwd", "raster_bwd", "loss", "optim"};
 
 // CUDA-event timing of each launch sequence on the stream it runs on, resolved lazily.
 struct KernelTimer {
@@ -207,6 +208,8 @@ struct DeviceState {
   // bwd warp steps with a contribution
   DevBuf work;
   DevBuf loss;  // fused loss: per-CTA fp64 partials, then the completion counter
+  DevBuf ssim_partials;  // fused L1 + D-SSIM loss: per-CTA fp64 partial sums
+  bool ssim_window = false;  // the SSIM window weights are in this device's constant bank
   KernelTimer timer;
   WorkUnits units;
   // the most recent sort_and_bin result, reusable by a backward over the same inputs
@@ -233,7 +236,7 @@ struct DeviceState {
     for (const DevBuf* b : {&keys[0], &keys[1], &vals[0], &vals[1], &records, &tile_bins,
                             &depth_mm, &status, &pkeys[0], &pkeys[1], &pvals[0], &pvals[1],
                             &poffs, &scan_status, &walk, &counts, &misc, &hist,
-                            &proj_status, &loss})
+                            &proj_status, &loss, &ssim_partials})
       s += b->bytes;
     return s;
   }
@@ -1145,8 +1148,10 @@ int splax_mse_loss(const float* img, const float* target, int64_t count, float d
     SPLAX_CUDA(cudaMemsetAsync(st->loss.p, 0, need, stream));
   }
   double* partials = static_cast<double*>(st->loss.p);
+  st->timer.begin(kLoss, 1, stream);
   launch_mse_loss(img, target, count, 1.0 / static_cast<double>(denom), partials,
                   reinterpret_cast<unsigned*>(partials + blocks), loss, blocks, stream);
+  st->timer.end(stream);
   return finish(*st, stream);
 }
 
@@ -1162,9 +1167,129 @@ int splax_mse_loss_bwd(const float* img, const float* target, int64_t count, flo
   std::lock_guard<std::mutex> lk(st->mu);
   rc = st->init();
   if (rc) return rc;
+  st->timer.begin(kLoss, count > 0 ? 1 : 0, stream);
   if (count > 0)
     launch_mse_loss_bwd(img, target, count, 2.0f / denom, v_loss, grad, mse_loss_blocks(),
                         stream);
+  st->timer.end(stream);
+  return finish(*st, stream);
+}
+
+// The 11-tap Gaussian window of sigma 1.5, normalised, in fp32 (the window dm_pix.ssim builds).
+static void ssim_window_weights(float* w) {
+  float sum = 0.0f;
+  for (int i = 0; i < 11; ++i) {
+    const float t = (static_cast<float>(i) - 5.0f) / 1.5f;
+    w[i] = std::exp(-0.5f * (t * t));
+    sum += w[i];
+  }
+  for (int i = 0; i < 11; ++i) w[i] /= sum;
+}
+
+static int l1_dssim_check(const float* img, const float* target, int32_t B, int32_t H,
+                          int32_t W, int32_t views_total, float ssim_lambda, const char* who) {
+  if (B <= 0 || H < 11 || W < 11 || views_total < B || !(ssim_lambda >= 0.0f) ||
+      !(ssim_lambda <= 1.0f) || img == nullptr || target == nullptr)
+    return fail(SPLAX_ERR_INVALID_ARGUMENT,
+                std::string(who) + ": need B >= 1, H, W >= 11, views_total >= B, lambda in [0, 1]");
+  return SPLAX_OK;
+}
+
+int splax_l1_dssim_loss(const float* img, const float* target, int32_t B, int32_t H, int32_t W,
+                        int32_t views_total, float ssim_lambda, float* loss, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  int rc = l1_dssim_check(img, target, B, H, W, views_total, ssim_lambda, "l1_dssim_loss");
+  if (rc) return rc;
+  if (loss == nullptr) return fail(SPLAX_ERR_INVALID_ARGUMENT, "l1_dssim_loss: loss is NULL");
+  DeviceState* st;
+  rc = current_state(&st);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(st->mu);
+  rc = st->init();
+  if (rc) return rc;
+  if (!st->ssim_window) {
+    float w[11];
+    ssim_window_weights(w);
+    ssim_set_window(w);
+    SPLAX_CUDA(cudaGetLastError());
+    st->ssim_window = true;
+  }
+  const int64_t parts = l1_dssim_partials(B, H, W);
+  SPLAX_CUDA(buf_reserve(st->ssim_partials, sizeof(double2) * parts));
+  const double V = views_total, lam = ssim_lambda;
+  const double l1_scale = (1.0 - lam) / (V * H * W * 3.0);
+  const double ssim_scale = lam / (V * (H - 10.0) * (W - 10.0) * 3.0);
+  st->timer.begin(kLoss, 2, stream);
+  launch_l1_dssim(img, target, B, H, W, l1_scale, ssim_scale, lam * B / V,
+                  static_cast<double2*>(st->ssim_partials.p), loss, stream);
+  st->timer.end(stream);
+  return finish(*st, stream);
+}
+
+int splax_l1_dssim_loss_bwd(const float* img, const float* target, int32_t B, int32_t H,
+                            int32_t W, int32_t views_total, float ssim_lambda,
+                            const float* v_loss, float* grad, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  int rc = l1_dssim_check(img, target, B, H, W, views_total, ssim_lambda, "l1_dssim_loss_bwd");
+  if (rc) return rc;
+  if (v_loss == nullptr || grad == nullptr)
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "l1_dssim_loss_bwd: v_loss or grad is NULL");
+  DeviceState* st;
+  rc = current_state(&st);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(st->mu);
+  rc = st->init();
+  if (rc) return rc;
+  if (!st->ssim_window) {
+    float w[11];
+    ssim_window_weights(w);
+    ssim_set_window(w);
+    SPLAX_CUDA(cudaGetLastError());
+    st->ssim_window = true;
+  }
+  const double V = views_total, lam = ssim_lambda;
+  const float l1_scale = static_cast<float>((1.0 - lam) / (V * H * W * 3.0));
+  const float ssim_grad = static_cast<float>(-lam / (V * (H - 10.0) * (W - 10.0) * 3.0));
+  st->timer.begin(kLoss, 1, stream);
+  launch_l1_dssim_bwd(img, target, B, H, W, l1_scale, ssim_grad, v_loss, grad, stream);
+  st->timer.end(stream);
+  return finish(*st, stream);
+}
+
+int splax_adam_step(int32_t num_arrays, float* const* params, const float* const* grads,
+                    float* const* exp_avg, float* const* exp_avg_sq, const int64_t* sizes,
+                    const float* lrs, int32_t step, float b1, float b2, float eps,
+                    void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (num_arrays < 0 || step < 1 || (num_arrays > 0 && (params == nullptr || grads == nullptr ||
+                                                        exp_avg == nullptr ||
+                                                        exp_avg_sq == nullptr ||
+                                                        sizes == nullptr || lrs == nullptr)))
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "adam_step: invalid arrays or step");
+  DeviceState* st;
+  int rc = current_state(&st);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(st->mu);
+  rc = st->init();
+  if (rc) return rc;
+  // bias corrections as optax forms them in fp32: 1 - decay ** count
+  const float bc1 = 1.0f - std::pow(b1, static_cast<float>(step));
+  const float bc2 = 1.0f - std::pow(b2, static_cast<float>(step));
+  for (int32_t j = 0; j < num_arrays; ++j)
+    if (sizes[j] < 0 ||
+        (sizes[j] > 0 && (!params[j] || !grads[j] || !exp_avg[j] || !exp_avg_sq[j])))
+      return fail(SPLAX_ERR_INVALID_ARGUMENT, "adam_step: NULL array or negative size");
+  st->timer.begin(kOptim, (num_arrays + kAdamMaxSegs - 1) / kAdamMaxSegs, stream);
+  for (int32_t k0 = 0; k0 < num_arrays; k0 += kAdamMaxSegs) {
+    AdamSegs s{};
+    const int32_t cnt = num_arrays - k0 < kAdamMaxSegs ? num_arrays - k0 : kAdamMaxSegs;
+    for (int32_t k = 0; k < cnt; ++k) {
+      const int32_t j = k0 + k;
+      s.seg[k] = AdamSeg{params[j], grads[j], exp_avg[j], exp_avg_sq[j], sizes[j], lrs[j]};
+    }
+    launch_adam(s, cnt, b1, b2, bc1, bc2, eps, stream);
+  }
+  st->timer.end(stream);
   return finish(*st, stream);
 }
 

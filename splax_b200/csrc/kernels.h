@@ -203,4 +203,30 @@ void launch_mse_loss(const float* img, const float* tgt, int64_t count, double i
 void launch_mse_loss_bwd(const float* img, const float* tgt, int64_t count, float scale,
                          const float* v_loss, float* grad, int blocks, cudaStream_t stream);
 
+// Fused L1 + D-SSIM loss (ssim.cu). The 11 window weights are set once per device.
+void ssim_set_window(const float* w11);
+int64_t l1_dssim_partials(int32_t B, int32_t H, int32_t W);
+void launch_l1_dssim(const float* img, const float* tgt, int32_t B, int32_t H, int32_t W,
+                     double l1_scale, double ssim_scale, double ssim_const, double2* partials,
+                     float* loss, cudaStream_t stream);
+void launch_l1_dssim_bwd(const float* img, const float* tgt, int32_t B, int32_t H, int32_t W,
+                         float l1_scale, float ssim_grad_scale, const float* v_loss, float* grad,
+                         cudaStream_t stream);
+
+// Fused multi-array Adam (optim.cu): up to kAdamMaxSegs parameter arrays per launch.
+constexpr int kAdamMaxSegs = 8;
+struct AdamSeg {
+  float* p;
+  const float* g;
+  float* m;
+  float* v;
+  int64_t n;
+  float lr;
+};
+struct AdamSegs {
+  AdamSeg seg[kAdamMaxSegs];
+};
+void launch_adam(const AdamSegs& s, int32_t count, float b1, float b2, float bc1, float bc2,
+                 float eps, cudaStream_t stream);
+
 }  // namespace splax
