@@ -230,6 +230,7 @@ struct DeviceState {
   int* sort_counters() { return static_cast<int*>(misc.p) + 2; }
   unsigned* span_word() { return static_cast<unsigned*>(misc.p) + 10; }
   int* scan_ticket() { return static_cast<int*>(misc.p) + 11; }
+  int32_t* vis_word() { return static_cast<int32_t*>(misc.p) + 12; }  // pairs that hit a tile
 
   size_t bytes_held() const {
     size_t s = 0;
@@ -393,7 +394,8 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
   // pair key: image id above the depth key
   const int key_shift = packed ? depth_bits : bit_length(static_cast<uint32_t>(st.pinned[2]));
   const int pair_bits = image_n_bits + key_shift;
-  const bool pair64 = pair_bits > 32;
+  // 64-bit pair keys from 32 significant bits: the all-ones key marks pairs left out
+  const bool pair64 = pair_bits > 31;
   const int bin_bits = upper;
   if (st.isect_cap < count) {
     const int64_t cap = std::max<int64_t>(static_cast<int64_t>(count * kScratchHeadroom) + 1,
@@ -485,14 +487,19 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
   ss.vals[1] = static_cast<int32_t*>(st.pvals[1].p);
   const int pair_passes = (pair_bits + 7) / 8;
   st.timer.begin(kPairSort, total > 1 && pair_passes ? 2 + pair_passes : 0, stream);
+  // only the V pairs that hit a tile are sorted; V stays on the device
+  ss.filter_sentinel = true;
+  ss.vcount = st.vis_word();
   const int pfin = radix_sort_pairs(ss, pair64, total, pair_bits, stream);
+  ss.filter_sentinel = false;
+  ss.vcount = nullptr;
   st.timer.end(stream);
   const int32_t* perm = ss.vals[pfin];
   int32_t* offsets = static_cast<int32_t*>(st.poffs.p);
   st.timer.begin(kPairScan, 1, stream);
-  launch_sorted_offsets(perm, static_cast<const int32_t*>(st.counts.p), total, offsets,
-                        static_cast<unsigned long long*>(st.scan_status.p), st.scan_ticket(),
-                        st.err_word(), stream);
+  launch_sorted_offsets(perm, static_cast<const int32_t*>(st.counts.p), total, st.vis_word(),
+                        offsets, static_cast<unsigned long long*>(st.scan_status.p),
+                        st.scan_ticket(), st.err_word(), stream);
   st.timer.end(stream);
 
   // 2. emission in pair order: (image | tile) keys, flat ids, blend records
@@ -502,6 +509,7 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
   ea.counts = static_cast<const int32_t*>(st.counts.p);
   ea.walk = static_cast<const float4*>(st.walk.p);
   ea.total = total;
+  ea.dtotal = st.vis_word();
   ea.count = count;
   ea.tile_n_bits = tile_n_bits;
   ea.tbx = tbx;
@@ -533,9 +541,18 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
   st.units.key_bytes += count * static_cast<int64_t>(sizeof(uint32_t));
   st.units.sort_passes += count > 1 ? count * passes : 0;
   st.units.bins += bins_len;
-  st.units.pairs_sorted += total;
-  st.units.pair_key_bytes += total * (pair64 ? 8 : 4);
-  st.units.pair_pass_keys += total > 1 ? total * pair_passes : 0;
+  // pairs that entered the depth sort: read back only in the instrumented (work-count) mode
+  int64_t sorted_pairs = total;
+  if (g_count_work.load()) {
+    int32_t v = 0;
+    SPLAX_CUDA(cudaMemcpyAsync(&v, st.vis_word(), sizeof(int32_t), cudaMemcpyDeviceToHost,
+                               stream));
+    SPLAX_CUDA(cudaStreamSynchronize(stream));
+    sorted_pairs = v;
+  }
+  st.units.pairs_sorted += sorted_pairs;
+  st.units.pair_key_bytes += sorted_pairs * (pair64 ? 8 : 4);
+  st.units.pair_pass_keys += sorted_pairs > 1 ? sorted_pairs * pair_passes : 0;
   st.last_valid = true;
   st.last_gen = st.sort_gen;
   st.last_in = in;

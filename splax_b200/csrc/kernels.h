@@ -72,6 +72,7 @@ constexpr int kRecordFloat4 = 3;
 
 struct EmitArgs {
   const int32_t* perm;     // pairs in (image, depth key) order
+  const int32_t* dtotal = nullptr;  // device-side number of sorted pairs (<= total), or nullptr
   const int32_t* offsets;  // exclusive scan of their tile counts in that order
   const int32_t* counts;   // tile count per pair (flat order)
   const float4* walk;      // walk record per pair (flat order)
@@ -124,8 +125,8 @@ void launch_pair_keys(const PairKeyArgs& a, bool key64, void* keys, int32_t* val
                       cudaStream_t stream);
 int64_t sorted_offsets_tiles(int64_t total);
 void launch_sorted_offsets(const int32_t* perm, const int32_t* counts, int64_t total,
-                           int32_t* offsets, unsigned long long* status, int* ticket,
-                           unsigned* err, cudaStream_t stream);
+                           const int32_t* dtotal, int32_t* offsets, unsigned long long* status,
+                           int* ticket, unsigned* err, cudaStream_t stream);
 void launch_emit(const EmitArgs& a, cudaStream_t stream);
 void launch_reference_keys(const uint32_t* bin_keys, const int32_t* gids, int64_t count,
                            const PairKeyArgs& a, int64_t* out, cudaStream_t stream);
@@ -137,6 +138,10 @@ struct SortScratch {
   uint32_t* hist;                 // [passes][256] counts, then [passes][256] offsets
   unsigned long long* status;     // look-back words, status_words entries
   int64_t status_words;
+  // drop all-ones keys (the first pass writes only the others) and write how many keys were
+  // sorted to vcount, which the later passes read
+  bool filter_sentinel = false;
+  int32_t* vcount = nullptr;
   int* tile_counters;             // one per pass
   unsigned* err;
 };

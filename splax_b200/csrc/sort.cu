@@ -104,16 +104,17 @@ __global__ void depth_span_kernel(const int32_t* mm, int32_t B, unsigned* span_o
   }
 }
 
-// Per pair, in flat order (coalesced): the pair key (image | depth key) and value (flat id),
-// the pair's tile count, its 32-byte walk record for the emission, and (when blending) its
-// 48-byte blend record. Depth keys:
+// Per pair, in flat order (coalesced): the pair key (image | depth key), its tile count, its
+// 32-byte walk record for the emission and (when blending) its 48-byte blend record. A pair
+// that hits no tile gets the all-ones key, which no real key reaches (pair keys widen to 64
+// bits from 32 significant bits up): the depth sort's histogram and first pass skip it, so only
+// the V pairs that hit a tile are sorted, and V stays in device memory.
 //  packed keys: the reference's quantised depth (_sort/_kernels.py:116-124)
 //  wide keys:   float bits - the image's minimum visible float bits (orders like the value)
+constexpr int kPrepThreads = 256;
+
 template <typename K>
-__global__ void __launch_bounds__(256)
-pair_prep_kernel(PairKeyArgs a, K* keys, int32_t* vals) {
-  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= a.total) return;
+__device__ __forceinline__ bool prep_one(const PairKeyArgs& a, int64_t idx, K& key) {
   const int64_t bid = idx / a.n;
   const bool live = a.radii[idx] > 0;
   uint64_t dk = 0;
@@ -135,9 +136,7 @@ pair_prep_kernel(PairKeyArgs a, K* keys, int32_t* vals) {
       dk = static_cast<uint32_t>(dbits - a.depth_mm[2 * bid]);
     }
   }
-  keys[idx] = static_cast<K>((static_cast<uint64_t>(bid) << a.key_shift) | dk);
-  vals[idx] = static_cast<int32_t>(idx);
-  if (!a.walk) return;  // the parity key reconstruction reuses this struct without records
+  key = static_cast<K>((static_cast<uint64_t>(bid) << a.key_shift) | dk);
   const int64_t hi = static_cast<uint32_t>(a.cum[idx]);
   const int64_t lo = idx > 0 ? static_cast<int64_t>(static_cast<uint32_t>(a.cum[idx - 1])) : 0;
   int64_t count = hi - lo;
@@ -147,7 +146,7 @@ pair_prep_kernel(PairKeyArgs a, K* keys, int32_t* vals) {
     count = 0;
   }
   a.counts[idx] = static_cast<int32_t>(count);
-  if (!live) return;
+  if (!live) return false;
   const float x = a.xys[2 * idx], y = a.xys[2 * idx + 1];
   const float ca = a.conics[3 * idx], cb = a.conics[3 * idx + 1], cc = a.conics[3 * idx + 2];
   const float mop = a.map_opacities[idx % a.map_opac_rows];
@@ -164,6 +163,18 @@ pair_prep_kernel(PairKeyArgs a, K* keys, int32_t* vals) {
     rec[1] = make_float4(-kHalfLog2e * cc, op, a.colors[3 * ci], a.colors[3 * ci + 1]);
     rec[2] = make_float4(a.colors[3 * ci + 2], depth, 0.0f, 0.0f);
   }
+  return count > 0;
+}
+
+template <typename K>
+__global__ void __launch_bounds__(kPrepThreads) pair_prep_kernel(PairKeyArgs a, K* keys,
+                                                                 int32_t* vals) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * kPrepThreads + threadIdx.x;
+  if (idx >= a.total) return;
+  K kk = K(0);
+  const bool vis = prep_one<K>(a, idx, kk);
+  keys[idx] = vis ? kk : static_cast<K>(~K(0));  // all ones: left out of the depth sort
+  vals[idx] = static_cast<int32_t>(idx);
 }
 
 // Exclusive scan of the tile counts in sorted pair order, one pass with a decoupled look-back
@@ -173,14 +184,16 @@ constexpr int kScanItems = 8;
 
 __global__ void __launch_bounds__(kScanThreads)
 sorted_offsets_kernel(const int32_t* __restrict__ perm, const int32_t* __restrict__ counts,
-                      int64_t total, int32_t* __restrict__ offsets, unsigned long long* status,
-                      int* ticket, unsigned* err) {
+                      int64_t total, const int32_t* dtotal, int32_t* __restrict__ offsets,
+                      unsigned long long* status, int* ticket, unsigned* err) {
   __shared__ int s_tile;
   __shared__ long long s_warp[kScanThreads / 32];
   __shared__ long long s_prefix;
   if (threadIdx.x == 0) s_tile = atomicAdd(ticket, 1);
   __syncthreads();
   const int64_t tile = s_tile;
+  if (dtotal) total = *dtotal;  // grid sized for the largest count; surplus tiles leave
+  if (tile * kScanThreads * kScanItems >= total) return;
   const int64_t base = tile * kScanThreads * kScanItems + static_cast<int64_t>(threadIdx.x) * kScanItems;
   long long c[kScanItems];
   long long tsum = 0;
@@ -236,7 +249,7 @@ constexpr int kEmitThreads = 32;
 
 __global__ void __launch_bounds__(kEmitThreads) emit_sorted_kernel(EmitArgs a) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= a.total) return;
+  if (i >= (a.dtotal ? static_cast<int64_t>(*a.dtotal) : a.total)) return;
   const int64_t idx = a.perm[i];
   if (idx < 0 || idx >= a.total || a.counts[idx] == 0) return;
   const float4 w0 = a.walk[2 * idx], w1 = a.walk[2 * idx + 1];
@@ -313,7 +326,8 @@ constexpr int kHistItems = 32;
 // block-wide set), 16-byte loads, then one global atomic per (pass, digit) and block.
 template <typename K>
 __global__ void __launch_bounds__(kHistThreads)
-radix_hist_kernel(const K* __restrict__ keys, int64_t count, int passes, uint32_t* hist) {
+radix_hist_kernel(const K* __restrict__ keys, int64_t count, bool filter, int passes,
+                  uint32_t* hist) {
   constexpr int kSets = 4;
   constexpr int kVec = 16 / sizeof(K);  // keys per 16-byte load
   __shared__ uint32_t s[kSets][8][256];
@@ -323,6 +337,7 @@ radix_hist_kernel(const K* __restrict__ keys, int64_t count, int passes, uint32_
   const int64_t base = static_cast<int64_t>(blockIdx.x) * kHistThreads * kHistItems;
   const int64_t end = min(count, base + static_cast<int64_t>(kHistThreads) * kHistItems);
   auto add = [&](uint64_t key) {
+    if (filter && key == static_cast<uint64_t>(static_cast<K>(~K(0)))) return;  // left out
     for (int p = 0; p < passes; ++p) atomicAdd(&s[warp][p][(key >> (8 * p)) & 255u], 1u);
   };
   if (end - base == static_cast<int64_t>(kHistThreads) * kHistItems) {
@@ -368,18 +383,23 @@ __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* s
   return wpre + inc - v;
 }
 
-// exclusive scan of each pass's 256-digit histogram: offsets[p][d]
-__global__ void radix_scan_kernel(const uint32_t* hist, uint32_t* offsets) {
+// exclusive scan of each pass's 256-digit histogram: offsets[p][d]; with total_out, pass 0
+// also writes the number of keys sorted
+__global__ void radix_scan_kernel(const uint32_t* hist, uint32_t* offsets, int32_t* total_out) {
   __shared__ uint32_t s_warp[8];
   const int p = blockIdx.x;
   const uint32_t v = hist[p * 256 + threadIdx.x];
-  offsets[p * 256 + threadIdx.x] = block_exclusive_scan<256>(v, s_warp);
+  const uint32_t ex = block_exclusive_scan<256>(v, s_warp);
+  offsets[p * 256 + threadIdx.x] = ex;
+  if (total_out && p == 0 && threadIdx.x == 255) *total_out = static_cast<int32_t>(ex + v);
 }
 
-template <typename K, int ITEMS, int NT>
+// FILTER (first pass of the depth sort): all-ones keys are neither ranked nor written, so the
+// output holds only the other keys, in stable order.
+template <typename K, int ITEMS, int NT, bool FILTER>
 __global__ void __launch_bounds__(NT)
 onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* __restrict__ kout,
-                int32_t* __restrict__ vout, int64_t count, int shift,
+                int32_t* __restrict__ vout, int64_t count, const int32_t* dcount, int shift,
                 const uint32_t* __restrict__ goff, unsigned long long* status, int* tile_counter,
                 unsigned* err) {
   constexpr int TILE = NT * ITEMS;
@@ -389,6 +409,7 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
   __shared__ long long s_gb[256];
   __shared__ uint32_t s_warp[kSortWarps];
   __shared__ int s_tile;
+  __shared__ int s_tile_keys;
   extern __shared__ __align__(16) unsigned char s_raw[];
   K* s_keys = reinterpret_cast<K*>(s_raw);
   int32_t* s_vals = reinterpret_cast<int32_t*>(s_raw + TILE * sizeof(K));
@@ -399,6 +420,8 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
   __syncthreads();
   const int64_t tile = s_tile;
   const int64_t base = tile * TILE;
+  if (dcount) count = *dcount;  // grid sized for the largest count; surplus tiles leave
+  if (base >= count) return;
   const int64_t rem = count - base;
   const int nvalid = rem < TILE ? static_cast<int>(rem) : TILE;
   const int warp_base = warp * 32 * ITEMS;
@@ -421,9 +444,17 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
 #pragma unroll
   for (int it = 0; it < ITEMS; ++it) {
     const int pos = warp_base + it * 32 + lane;
-    const bool valid = pos < nvalid;
+    const bool valid = pos < nvalid && (!FILTER || k[it] != static_cast<K>(~K(0)));
     const uint32_t d = static_cast<uint32_t>(static_cast<uint64_t>(k[it]) >> shift) & 255u;
-    const unsigned peers = __match_any_sync(0xffffffffu, valid ? d : 256u + lane);
+    // lanes holding the same digit: intersect one ballot per digit bit (cheaper than a
+    // match instruction over up to 32 distinct digits); invalid lanes match nobody
+    unsigned peers = __ballot_sync(0xffffffffu, valid);
+#pragma unroll
+    for (int bit = 0; bit < 8; ++bit) {
+      const unsigned b = __ballot_sync(0xffffffffu, (d >> bit) & 1u);
+      peers &= ((d >> bit) & 1u) ? b : ~b;
+    }
+    if (!valid) peers = 1u << lane;
     const int leader = __ffs(peers) - 1;
     uint32_t prev = 0;
     if (valid && lane == leader) prev = atomicAdd(&s_wh[warp][d], __popc(peers));
@@ -447,26 +478,40 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
       st_relaxed(st, kLookbackInc | sum);
     } else {
       st_relaxed(st, kLookbackAgg | sum);
+      // walk back kLookAhead predecessors per round trip: sum aggregates up to the nearest
+      // inclusive prefix; a predecessor that has published nothing yet is re-read (bounded)
+      constexpr int kLookAhead = 4;
       int64_t j = tile - 1;
       long long spins = 0;
-      while (j >= 0) {
-        const unsigned long long s = ld_relaxed(status + j * 256 + dg);
-        const unsigned long long flag = s & ~kLookbackMask;
-        if (flag == 0) {
+      bool done = false;
+      while (!done && j >= 0) {
+        unsigned long long w[kLookAhead];
+#pragma unroll
+        for (int q = 0; q < kLookAhead; ++q)
+          w[q] = j - q >= 0 ? ld_relaxed(status + (j - q) * 256 + dg) : kLookbackInc;
+        int used = 0;
+#pragma unroll
+        for (int q = 0; q < kLookAhead; ++q) {
+          if (done || used < q) continue;  // stopped at an unpublished word
+          const unsigned long long flag = w[q] & ~kLookbackMask;
+          if (flag == 0) continue;
+          prefix += static_cast<long long>(w[q] & kLookbackMask);
+          used = q + 1;
+          if (flag == kLookbackInc) done = true;
+        }
+        j -= used;
+        if (!done && used < kLookAhead) {  // waiting on tile j
           if (++spins > kSpinLimit) {
             atomicOr(err, kErrLookbackTimeout);
             break;
           }
-          continue;
         }
-        prefix += static_cast<long long>(s & kLookbackMask);
-        if (flag == kLookbackInc) break;
-        --j;
       }
       st_relaxed(st, kLookbackInc | (static_cast<unsigned long long>(prefix) + sum));
     }
   }
   const uint32_t excl = block_exclusive_scan<NT>(sum, s_warp);
+  if (tid == 255) s_tile_keys = static_cast<int>(excl + sum);  // keys this tile writes
   if (tid < 256) {
     s_bx[tid] = excl;
     s_gb[tid] = static_cast<long long>(goff[tid]) + prefix - static_cast<long long>(excl);
@@ -475,7 +520,7 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
 #pragma unroll
   for (int it = 0; it < ITEMS; ++it) {
     const int pos = warp_base + it * 32 + lane;
-    if (pos < nvalid) {
+    if (pos < nvalid && (!FILTER || k[it] != static_cast<K>(~K(0)))) {
       const uint32_t d = static_cast<uint32_t>(static_cast<uint64_t>(k[it]) >> shift) & 255u;
       const uint32_t lpos = s_bx[d] + s_wh[warp][d] + rank[it];
       s_keys[lpos] = k[it];
@@ -483,10 +528,11 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
     }
   }
   __syncthreads();
+  const int tile_keys = s_tile_keys;
 #pragma unroll
   for (int j = 0; j < ITEMS; ++j) {
     const int p = j * NT + tid;
-    if (p < nvalid) {
+    if (p < tile_keys) {
       const K kk = s_keys[p];
       const uint32_t d = static_cast<uint32_t>(static_cast<uint64_t>(kk) >> shift) & 255u;
       const long long dst = s_gb[d] + p;
@@ -550,6 +596,20 @@ tile_bins_kernel(const uint32_t* __restrict__ keys, int64_t count, int32_t tile_
   }
 }
 
+template <typename K, int ITEMS, int NT, bool FILTER>
+void set_onesweep_smem() {
+  static bool done = false;  // per instantiation: static + dynamic exceeds 48 KiB
+  if (!done) {
+    cudaFuncSetAttribute(onesweep_kernel<K, ITEMS, NT, FILTER>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(NT * ITEMS * (sizeof(K) + sizeof(int32_t))));
+    done = true;
+  }
+}
+
+// Stable LSD sort of `count` keys. With s.filter_sentinel the all-ones keys are dropped by the
+// histogram and the first pass, s.vcount receives how many keys remain, and the later passes
+// read that device-side count (their grids stay sized for `count`; surplus tiles leave).
 template <typename K, int ITEMS, int NT>
 int sort_impl(const SortScratch& s, int64_t count, int bits, cudaStream_t stream) {
   const int passes = (bits + 7) / 8;
@@ -559,23 +619,28 @@ int sort_impl(const SortScratch& s, int64_t count, int bits, cudaStream_t stream
   cudaMemsetAsync(s.tile_counters, 0, sizeof(int) * 8, stream);
   const int64_t hblocks = (count + kHistThreads * kHistItems - 1) / (kHistThreads * kHistItems);
   radix_hist_kernel<K><<<static_cast<unsigned>(hblocks), kHistThreads, 0, stream>>>(
-      reinterpret_cast<const K*>(s.keys[0]), count, passes, hist);
-  radix_scan_kernel<<<passes, 256, 0, stream>>>(hist, offsets);
+      reinterpret_cast<const K*>(s.keys[0]), count, s.filter_sentinel, passes, hist);
+  radix_scan_kernel<<<passes, 256, 0, stream>>>(hist, offsets,
+                                                 s.filter_sentinel ? s.vcount : nullptr);
   constexpr int TILE = NT * ITEMS;
   const int64_t tiles = (count + TILE - 1) / TILE;
   const size_t smem = TILE * (sizeof(K) + sizeof(int32_t));
-  static bool attr_set = false;  // per instantiation: static + dynamic exceeds 48 KiB
-  if (!attr_set) {
-    cudaFuncSetAttribute(onesweep_kernel<K, ITEMS, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(smem));
-    attr_set = true;
-  }
+  set_onesweep_smem<K, ITEMS, NT, false>();
+  set_onesweep_smem<K, ITEMS, NT, true>();
   int cur = 0;
   for (int p = 0; p < passes; ++p) {
     cudaMemsetAsync(s.status, 0, sizeof(unsigned long long) * tiles * 256, stream);
-    onesweep_kernel<K, ITEMS, NT><<<static_cast<unsigned>(tiles), NT, smem, stream>>>(
-        reinterpret_cast<const K*>(s.keys[cur]), s.vals[cur], reinterpret_cast<K*>(s.keys[cur ^ 1]),
-        s.vals[cur ^ 1], count, 8 * p, offsets + p * 256, s.status, s.tile_counters + p, s.err);
+    const K* kin = reinterpret_cast<const K*>(s.keys[cur]);
+    K* kout = reinterpret_cast<K*>(s.keys[cur ^ 1]);
+    if (s.filter_sentinel && p == 0)
+      onesweep_kernel<K, ITEMS, NT, true><<<static_cast<unsigned>(tiles), NT, smem, stream>>>(
+          kin, s.vals[cur], kout, s.vals[cur ^ 1], count, nullptr, 8 * p, offsets + p * 256,
+          s.status, s.tile_counters + p, s.err);
+    else
+      onesweep_kernel<K, ITEMS, NT, false><<<static_cast<unsigned>(tiles), NT, smem, stream>>>(
+          kin, s.vals[cur], kout, s.vals[cur ^ 1], count,
+          s.filter_sentinel ? s.vcount : nullptr, 8 * p, offsets + p * 256, s.status,
+          s.tile_counters + p, s.err);
     cur ^= 1;
   }
   return cur;
@@ -600,13 +665,13 @@ void launch_depth_span(const int32_t* depth_mm, int32_t B, unsigned* span_out,
 
 void launch_pair_keys(const PairKeyArgs& a, bool key64, void* keys, int32_t* vals,
                       cudaStream_t stream) {
-  const int64_t blocks = (a.total + 255) / 256;
+  const int64_t blocks = (a.total + kPrepThreads - 1) / kPrepThreads;
   if (blocks == 0) return;
   if (key64)
-    pair_prep_kernel<uint64_t><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+    pair_prep_kernel<uint64_t><<<static_cast<unsigned>(blocks), kPrepThreads, 0, stream>>>(
         a, static_cast<uint64_t*>(keys), vals);
   else
-    pair_prep_kernel<uint32_t><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+    pair_prep_kernel<uint32_t><<<static_cast<unsigned>(blocks), kPrepThreads, 0, stream>>>(
         a, static_cast<uint32_t*>(keys), vals);
 }
 
@@ -615,14 +680,14 @@ int64_t sorted_offsets_tiles(int64_t total) {
 }
 
 void launch_sorted_offsets(const int32_t* perm, const int32_t* counts, int64_t total,
-                           int32_t* offsets, unsigned long long* status, int* ticket,
-                           unsigned* err, cudaStream_t stream) {
+                           const int32_t* dtotal, int32_t* offsets, unsigned long long* status,
+                           int* ticket, unsigned* err, cudaStream_t stream) {
   const int64_t tiles = sorted_offsets_tiles(total);
   if (tiles == 0) return;
   cudaMemsetAsync(ticket, 0, sizeof(int), stream);
   cudaMemsetAsync(status, 0, sizeof(unsigned long long) * tiles, stream);
   sorted_offsets_kernel<<<static_cast<unsigned>(tiles), kScanThreads, 0, stream>>>(
-      perm, counts, total, offsets, status, ticket, err);
+      perm, counts, total, dtotal, offsets, status, ticket, err);
 }
 
 void launch_emit(const EmitArgs& a, cudaStream_t stream) {
@@ -643,7 +708,12 @@ int sort_tile_items(bool key64) { return kSortThreads * (key64 ? kItems64 : kIte
 
 int radix_sort_pairs(const SortScratch& s, bool key64, int64_t count, int bits,
                      cudaStream_t stream) {
-  if (count <= 1) return 0;
+  if (s.filter_sentinel && count <= 0) {
+    cudaMemsetAsync(s.vcount, 0, sizeof(int32_t), stream);
+    return 0;
+  }
+  // with the filter even a single key goes through, so that vcount is written
+  if (count <= 1 && !s.filter_sentinel) return 0;
   return key64 ? sort_impl<uint64_t, kItems64, kSortThreads>(s, count, bits, stream)
                : sort_impl<uint32_t, kItems32, kSortThreads>(s, count, bits, stream);
 }
