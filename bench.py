@@ -39,8 +39,8 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 # the reference blend loop (splax/_rasterize/_kernels.py:185-197) and vjp (:1235-1253)
 # DRAM bytes (read + write) per launch of the full config-2 workload from single-pass ncu
 # captures (dram__bytes_read.sum + dram__bytes_write.sum), summarised in profiles/*.md
-TRAFFIC_BYTES_PER_LAUNCH = {"raster_bwd": 620.40e6, "raster_fwd": 491.68e6,
-                            "emit_keys": 985.57e6}
+TRAFFIC_BYTES_PER_LAUNCH = {"raster_bwd": 574.82e6, "raster_fwd": 490.61e6,
+                            "emit_keys": 974.66e6}
 FWD_FLOPS_PER_EVAL = 22
 BWD_FLOPS_PER_EVAL = 12
 BWD_FLOPS_PER_CONTRIB = 45
@@ -482,19 +482,27 @@ def main() -> None:
         kb = work["key_bytes"] / max(I, 1)
         passes = work["sort_pass_keys"] / max(I, 1)
         pairs = per_launch("pairs_fwd", "project_fwd")
+        V = work["pairs_sorted"]  # pairs that hit a tile (exact, from the instrumented step)
+        kbp = work["pair_key_bytes"] / max(V, 1)
+        pp = work["pair_pass_keys"] / max(V, 1)
         bytes_est = {
             "project_fwd": 44 * n + 36 * pairs,
             "emit_keys": per_launch("intersections", "emit_keys") * (kb + 4) + 36 * pairs,
             "radix_sort": per_launch("intersections", "radix_sort") * kb
             + 2 * passes * per_launch("intersections", "radix_sort") * (kb + 4),
             "tile_bins": per_launch("key_bytes", "tile_bins") + 8 * per_launch("bins", "tile_bins"),
-            # depth-order sort of the B*n pairs and the scan of their counts in that order
-            "pair_sort": per_launch("pair_key_bytes", "pair_sort")
-            + 2 * per_launch("pair_pass_keys", "pair_sort")
-            * (work["pair_key_bytes"] / max(work["pairs_sorted"], 1) + 4),
-            "pair_keys": 12 * per_launch("pairs_sorted", "pair_keys"),
-            "pair_scan": 12 * per_launch("pairs_sorted", "pair_scan"),
-            "project_bwd": 120 * per_launch("pairs_bwd", "project_bwd"),
+            # depth-order sort: the histogram and first pass read all P pair keys and keep the
+            # V that hit a tile; the other passes move V keys and values
+            "pair_sort": pairs * kbp + pairs * (kbp + 4) + V * (kbp + 4)
+            + 2 * max(pp - 1, 0) * V * (kbp + 4),
+            # prep pass: reads depth, radius, cum pair, xy, conic, both opacities, colour
+            # (56 B); writes key, value, walk record, blend record (88 B)
+            "pair_keys": 144 * pairs,
+            # the scan of the V sorted pairs' counts: perm, gathered count, offset
+            "pair_scan": 12 * V,
+            # per pair: radius, conic, v_xy, v_conic (36 B); per gaussian: means, scales,
+            # quats read and their cotangents written once, summed over the cameras (80 B)
+            "project_bwd": 36 * per_launch("pairs_bwd", "project_bwd") + 80 * n,
             "depth_minmax": 8 * pairs,
         }
         for name, b in bytes_est.items():
