@@ -276,6 +276,18 @@ int splax_adam_step(int32_t num_arrays, float *const *params, const float *const
                     float *const *exp_avg, float *const *exp_avg_sq, const int64_t *sizes,
                     const float *lrs, int32_t step, float b1, float b2, float eps, void *stream);
 
+/* load_ply, splax/io.py:78-98, first half: parse a 3DGS .ply header and report its vertex
+ * count (host only, no GPU work). Binary little-endian files whose first element is `vertex`
+ * with scalar properties, the fields x y z scale_0..2 rot_0..3 f_dc_0..2 opacity in float32. */
+int splax_ply_info(const char *path, int64_t *num_vertices);
+
+/* load_ply, second half: stream the vertex records to the GPU and decode them into the five
+ * render-space arrays (device pointers): means (n,3), scales = exp(scale) (n,3), quats =
+ * rot / |rot| wxyz (n,4), colors = clip(f_dc * C0 + 0.5, 0, 1) (n,3), opacities =
+ * sigmoid(opacity) (n,). num_vertices must be splax_ply_info's count. */
+int splax_ply_load(const char *path, int64_t num_vertices, float *means, float *scales,
+                   float *quats, float *colors, float *opacities, void *stream);
+
 /* clear_cache, splax/_cache.py:158-164: release the scratch of every device. */
 void splax_clear_cache(void);
 

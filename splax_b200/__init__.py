@@ -6,14 +6,15 @@ behind a C ABI, include/splax_b200.h). This package mirrors the reference's publ
 (splax/__init__.py:30-47) over torch tensors: ``render`` and ``render_log`` are differentiable
 with torch.autograd with respect to the gaussian parameters, the camera pose and per-object
 rigid transforms. ``mse_loss`` and ``l1_dssim_loss`` are fused loss-and-gradient kernels
-for the training step around the render; ``Adam`` is its fused optimiser update. There is no
-CPU fallback.
+for the training step around the render; ``Adam`` is its fused optimiser update;
+``load_ply`` streams a 3DGS scene file onto the GPU. There is no CPU fallback.
 """
 
 __version__ = "0.1.0"
 
 from splax_b200 import utils
 from splax_b200._cache import clear_cache, scratch_info
+from splax_b200._io import load_ply, write_ply
 from splax_b200._loss import l1_dssim_loss, mse_loss
 from splax_b200._optim import Adam
 from splax_b200._project import opacity_compensation, project, transform_ids
@@ -24,6 +25,7 @@ __all__ = [
     "Adam",
     "clear_cache",
     "l1_dssim_loss",
+    "load_ply",
     "mse_loss",
     "opacity_compensation",
     "project",
@@ -34,4 +36,5 @@ __all__ = [
     "scratch_info",
     "transform_ids",
     "utils",
+    "write_ply",
 ]

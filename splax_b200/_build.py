@@ -34,6 +34,7 @@ SOURCES = {
     "loss.cu": [],
     "ssim.cu": [],
     "optim.cu": [],
+    "ply.cu": [],
 }
 
 

@@ -209,6 +209,11 @@ struct DeviceState {
   DevBuf work;
   DevBuf loss;  // fused loss: per-CTA fp64 partials, then the completion counter
   DevBuf ssim_partials;  // fused L1 + D-SSIM loss: per-CTA fp64 partial sums
+  // .ply loading: two pinned host chunks, two device staging chunks, copy-done events
+  void* ply_host[2] = {nullptr, nullptr};
+  DevBuf ply_dev[2];
+  size_t ply_chunk = 0;
+  cudaEvent_t ply_ev[2] = {nullptr, nullptr};
   bool ssim_window = false;  // the SSIM window weights are in this device's constant bank
   KernelTimer timer;
   WorkUnits units;
@@ -1307,6 +1312,80 @@ int splax_adam_step(int32_t num_arrays, float* const* params, const float* const
     launch_adam(s, cnt, b1, b2, bc1, bc2, eps, stream);
   }
   st->timer.end(stream);
+  return finish(*st, stream);
+}
+
+int splax_ply_info(const char* path, int64_t* num_vertices) {
+  if (path == nullptr || num_vertices == nullptr)
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "ply_info: NULL argument");
+  FILE* f = std::fopen(path, "rb");
+  if (!f) return fail(SPLAX_ERR_INVALID_ARGUMENT, std::string("ply_info: cannot open ") + path);
+  PlyLayout L;
+  int64_t n = 0, body = 0;
+  std::string why;
+  const int rc = ply_parse_header(f, &L, &n, &body, &why);
+  std::fclose(f);
+  if (rc) return fail(SPLAX_ERR_INVALID_ARGUMENT, "ply_info: " + why);
+  *num_vertices = n;
+  return SPLAX_OK;
+}
+
+int splax_ply_load(const char* path, int64_t num_vertices, float* means, float* scales,
+                   float* quats, float* colors, float* opacities, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (path == nullptr || num_vertices < 0 ||
+      (num_vertices > 0 && (!means || !scales || !quats || !colors || !opacities)))
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "ply_load: invalid arguments");
+  FILE* f = std::fopen(path, "rb");
+  if (!f) return fail(SPLAX_ERR_INVALID_ARGUMENT, std::string("ply_load: cannot open ") + path);
+  struct Closer {
+    FILE* f;
+    ~Closer() { std::fclose(f); }
+  } closer{f};
+  PlyLayout L;
+  int64_t n = 0, body = 0;
+  std::string why;
+  if (ply_parse_header(f, &L, &n, &body, &why))
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "ply_load: " + why);
+  if (n != num_vertices)
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "ply_load: num_vertices does not match the file");
+  DeviceState* st;
+  int rc = current_state(&st);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(st->mu);
+  rc = st->init();
+  if (rc) return rc;
+  constexpr size_t kChunk = size_t(32) << 20;
+  const size_t chunk = std::max<size_t>(kChunk, static_cast<size_t>(L.stride));
+  if (st->ply_chunk < chunk) {
+    SPLAX_CUDA(cudaStreamSynchronize(stream));
+    for (int b = 0; b < 2; ++b) {
+      if (st->ply_host[b]) cudaFreeHost(st->ply_host[b]);
+      st->ply_host[b] = nullptr;
+      buf_free(st->ply_dev[b]);
+    }
+    st->ply_chunk = 0;
+    for (int b = 0; b < 2; ++b) {
+      SPLAX_CUDA(cudaMallocHost(&st->ply_host[b], chunk));
+      SPLAX_CUDA(buf_reserve(st->ply_dev[b], chunk));
+      if (!st->ply_ev[b]) SPLAX_CUDA(cudaEventCreateWithFlags(&st->ply_ev[b], cudaEventDisableTiming));
+    }
+    st->ply_chunk = chunk;
+  }
+  const int64_t per = static_cast<int64_t>(chunk / static_cast<size_t>(L.stride));
+  int b = 0;
+  for (int64_t first = 0; first < n; first += per, b ^= 1) {
+    const int64_t cnt = std::min<int64_t>(per, n - first);
+    const size_t bytes = static_cast<size_t>(cnt * L.stride);
+    SPLAX_CUDA(cudaEventSynchronize(st->ply_ev[b]));  // the copy out of this buffer is done
+    if (std::fread(st->ply_host[b], 1, bytes, f) != bytes)
+      return fail(SPLAX_ERR_INVALID_ARGUMENT, "ply_load: the file is shorter than its header says");
+    SPLAX_CUDA(cudaMemcpyAsync(st->ply_dev[b].p, st->ply_host[b], bytes, cudaMemcpyHostToDevice,
+                               stream));
+    SPLAX_CUDA(cudaEventRecord(st->ply_ev[b], stream));
+    launch_ply_decode(static_cast<const unsigned char*>(st->ply_dev[b].p), cnt, L, first, means,
+                      scales, quats, colors, opacities, stream);
+  }
   return finish(*st, stream);
 }
 

@@ -3,6 +3,8 @@
 #pragma once
 
 #include <cstdint>
+#include <cstdio>
+#include <string>
 #include <cuda_runtime.h>
 
 namespace splax {
@@ -233,5 +235,18 @@ struct AdamSegs {
 };
 void launch_adam(const AdamSegs& s, int32_t count, float b1, float b2, float bc1, float bc2,
                  float eps, cudaStream_t stream);
+
+// 3DGS .ply loading (ply.cu): byte offsets of x y z, scale_0..2, rot_0..3, f_dc_0..2, opacity
+// in a vertex record of `stride` bytes.
+struct PlyLayout {
+  int32_t off[14];
+  int64_t stride;
+  bool aligned;  // every needed offset and the stride are multiples of 4
+};
+int ply_parse_header(FILE* f, PlyLayout* L, int64_t* count, int64_t* body_offset,
+                     std::string* why);
+void launch_ply_decode(const unsigned char* body, int64_t count, const PlyLayout& L,
+                       int64_t first, float* means, float* scales, float* quats, float* colors,
+                       float* opacities, cudaStream_t stream);
 
 }  // namespace splax
