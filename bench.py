@@ -34,7 +34,21 @@ sys.path.insert(0, str(ROOT))
 METRIC = "fwd+bwd frames/s (1M gaussians, 1080p, 8 cams) at 1/2/4/8 B200; % roofline"
 CONFIG = 2
 WORKLOAD = "config 2: 1M gaussians, 8 ring cams, 1080x1920, MSE fwd+bwd, grads of 5 param arrays"
+# the other fwd+bwd configurations of BASELINE (not the headline): metric, workload, options
+FWD_BWD = {
+    0: ("config 0 forward frames/s (10k gaussians, 256x256, 1 cam)",
+        "config 0: 10k gaussians, 1 cam, 256x256, white background, forward render only",
+        dict(viewmat_grad=False, antialiased=False, forward_only=True)),
+    1: ("config 1 fwd+bwd frames/s (200k gaussians, 800x800, 1 cam)",
+        "config 1: 200k gaussians, 1 cam, 800x800, MSE fwd+bwd, grads of 5 param arrays + "
+        "viewmat", dict(viewmat_grad=True, antialiased=False)),
+    2: (METRIC, WORKLOAD, dict(viewmat_grad=False, antialiased=False)),
+    4: ("config 4 fwd+bwd frames/s (6M gaussians, 2160x3840, 64 cams, antialiased)",
+        "config 4: 6M gaussians, 64 sphere cams, 2160x3840, antialiased, MSE fwd+bwd, grads of "
+        "5 param arrays + viewmats", dict(viewmat_grad=True, antialiased=True)),
+}
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+L2_BYTES = 126 << 20
 # algorithmic work per unit: FLOPs per blend evaluation / contribution (FMA = 2), restated from
 # the reference blend loop (splax/_rasterize/_kernels.py:185-197) and vjp (:1235-1253)
 # DRAM bytes (read + write) per launch of the full config-2 workload from single-pass ncu
@@ -55,8 +69,11 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--n", type=int, default=None, help="override the gaussian count (debug)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", type=int, default=CONFIG, choices=[2, 3],
-                    help="2: the headline fwd+bwd step (default); 3: the batched training step")
+    ap.add_argument("--config", type=int, default=CONFIG, choices=[0, 1, 2, 3, 4],
+                    help="2: the headline fwd+bwd step (default); 0: forward render only; 1: one "
+                         "camera with the viewmat "
+                         "gradient; 3: the batched training step; 4: the antialiased 64-camera "
+                         "4K stress step (8 GPUs)")
     return ap.parse_args()
 
 
@@ -110,8 +127,9 @@ class ClockSampler:
                 "samples": len(rows)}
 
 
-def cpu_baseline(scene: dict, threads: int) -> dict:
-    """One camera of the workload, forward + backward, through the C oracle."""
+def cpu_baseline(scene: dict, threads: int, forward_only: bool = False) -> dict:
+    """One camera of the workload, forward + backward (or forward only), through the C
+    oracle."""
     import oracle
 
     oracle.build()
@@ -126,6 +144,8 @@ def cpu_baseline(scene: dict, threads: int) -> dict:
     op = scene["opacities"]
     fT, fi, img, _, _ = oracle.rasterize(scene["colors"], op, op, scene["background"], xys, d, r,
                                          cn, cum, n=n, B=1, img_shape=(H, W), nthreads=threads)
+    if forward_only:
+        return {"seconds": time.perf_counter() - t0, "counters": oracle.counters()}
     v_img = 2.0 * (img.reshape(H * W, 3) - target) / (scene["B"] * H * W * 3)
     vc, vo, vxy, vcon, _ = oracle.rasterize_bwd(scene["colors"], op, op, scene["background"], xys,
                                                 d, r, cn, cum, fT, fi, v_img, n=n, B_out=1,
@@ -143,7 +163,7 @@ def reference_arm(args) -> None:
     if rank != 0:
         return
     scene = utils.synthetic_scene(CONFIG, n=args.n)
-    scene["target"] = utils.target_images(scene)[:1]
+    scene["target"] = utils.target_images(scene, [0])
     threads = os.cpu_count() or 1
     for _ in range(min(args.warmup, 1)):
         cpu_baseline(scene, threads)
@@ -197,7 +217,7 @@ def train_bench(args) -> None:
         raise SystemExit(f"{B} cameras do not split over {world} ranks")
     per = B // world
     cams = slice(rank * per, (rank + 1) * per)
-    targets_np = utils.target_images(scene)
+    targets_np = utils.target_images(scene, range(rank * per, (rank + 1) * per))
     logit = lambda x: np.log(x) - np.log1p(-x)  # noqa: E731
     host = {"means": scene["means"], "log_scales": np.log(scene["scales"]),
             "quats": scene["quats"], "colors_logit": logit(np.clip(scene["colors"], 1e-4, 1 - 1e-4)),
@@ -206,7 +226,7 @@ def train_bench(args) -> None:
               for k in TRAIN_LRS]
     opt = sx.Adam(params, [lr * float(np.sqrt(B)) for lr in TRAIN_LRS.values()])
     views = torch.tensor(scene["viewmats"][cams], device=dev)
-    target = torch.tensor(targets_np[cams], device=dev)
+    target = torch.tensor(targets_np, device=dev)
     bg = torch.tensor(scene["background"], device=dev)
     kw = dict(background=bg, img_shape=(H, W), f=(f, f))
 
@@ -313,25 +333,34 @@ def main() -> None:
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
 
-    scene = utils.synthetic_scene(CONFIG, n=args.n)
+    metric, workload, opts = FWD_BWD[args.config]
+    scene = utils.synthetic_scene(args.config, n=args.n)
     B, H, W, f = scene["B"], scene["H"], scene["W"], scene["f"]
     n = scene["means"].shape[0]
     if B % world:
         raise SystemExit(f"{B} cameras do not split over {world} ranks")
     per = B // world
     cams = slice(rank * per, (rank + 1) * per)
-    targets_np = utils.target_images(scene)
+    targets_np = utils.target_images(scene, range(rank * per, (rank + 1) * per))
     host = {k: scene[k] for k in ("means", "scales", "quats", "colors", "opacities")}
     params = [torch.tensor(host[k], device=dev).requires_grad_() for k in host]
     views = torch.tensor(scene["viewmats"][cams], device=dev)
-    target = torch.tensor(targets_np[cams], device=dev)
+    if opts["viewmat_grad"]:
+        views.requires_grad_()
+    target = torch.tensor(targets_np, device=dev)
     bg = torch.tensor(scene["background"], device=dev)
-    kw = dict(background=bg, img_shape=(H, W), f=(f, f))
+    kw = dict(background=bg, img_shape=(H, W), f=(f, f), antialiased=opts["antialiased"])
     denom = float(B * H * W * 3)
 
     def step(vm, tgt, ps=params):
+        if opts.get("forward_only"):
+            with torch.no_grad():
+                imgs, _ = sx.render(*ps, viewmat=vm, **kw)
+            return imgs.sum()  # the step's result read back end to end
         for p in ps:
             p.grad = None
+        if vm.requires_grad:
+            vm.grad = None
         imgs, _ = sx.render(*ps, viewmat=vm, **kw)
         loss = sx.mse_loss(imgs, tgt, denom=denom)
         loss.backward()
@@ -361,17 +390,33 @@ def main() -> None:
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for _ in range(args.steps):
-        step(views, target)
-    t1.record()
-    torch.cuda.synchronize()
+    # Inputs smaller than L2 (config 1): time each step alone and flush L2 between steps by
+    # writing a 256 MB buffer outside the timed events; otherwise one event pair around all.
+    input_bytes = 4 * (sum(p.numel() for p in params) + target.numel())
+    flush = input_bytes < 2 * L2_BYTES
+    if flush:
+        scratch = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        for a, b in evs:
+            scratch.fill_(1)
+            a.record()
+            step(views, target)
+            b.record()
+        torch.cuda.synchronize()
+        ms = sum(a.elapsed_time(b) for a, b in evs)
+    else:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.steps):
+            step(views, target)
+        t1.record()
+        torch.cuda.synchronize()
+        ms = t0.elapsed_time(t1)
     if world > 1:
         dist.barrier()
     clocks = sampler.stop() if sampler else None
-    ms = t0.elapsed_time(t1)
     prof = _lib.profile_report()
     _lib.profile_enable(timing=False, count_work=False)
     ms_t = torch.tensor([ms], device=dev, dtype=torch.float64)
@@ -397,9 +442,10 @@ def main() -> None:
     if not args.no_e2e:
         pinned = [torch.from_numpy(host[k]).pin_memory() for k in host]
         v_host = torch.from_numpy(np.ascontiguousarray(scene["viewmats"][cams])).pin_memory()
-        t_host = torch.from_numpy(np.ascontiguousarray(targets_np[cams])).pin_memory()
+        t_host = torch.from_numpy(np.ascontiguousarray(targets_np)).pin_memory()
         loss_host = torch.empty((args.steps + 1,), dtype=torch.float32).pin_memory()
-        slots = [([torch.empty_like(p) for p in params], torch.empty_like(views),
+        slots = [([torch.empty_like(p) for p in params],
+                  torch.empty_like(views).requires_grad_(views.requires_grad),
                   torch.empty_like(target)) for _ in range(2)]
         slot_params = [[sp.requires_grad_() for sp in sl[0]] for sl in slots]
         h2d = sum(t.numel() * 4 for t in pinned) + v_host.numel() * 4 + t_host.numel() * 4
@@ -453,14 +499,16 @@ def main() -> None:
                "pipelining": "copy stream, two input slots"}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config in (0, 1, 2):
         sc = dict(scene)
         sc["target"] = targets_np[:1]
         threads = os.cpu_count() or 1
-        res = cpu_baseline(sc, threads)
+        fo = bool(opts.get("forward_only"))
+        res = cpu_baseline(sc, threads, forward_only=fo)
         cpu = {"value": 1.0 / res["seconds"], "unit": "frames/s", "cores": threads,
                "kind": "port",
-               "sample": f"camera 0 of {B} (one frame), N={n}, {H}x{W}, fwd+bwd, C oracle"}
+               "sample": f"camera 0 of {B} (one frame), N={n}, {H}x{W}, "
+                         f"{'forward' if fo else 'fwd+bwd'}, C oracle"}
 
     if rank == 0:
         peaks, peak_src = load_peaks()
@@ -522,7 +570,7 @@ def main() -> None:
         total_ms = {k: v["ms"] for k, v in kern.items()}
         dom = max(total_ms, key=total_ms.get)
         for name, t in TRAFFIC_BYTES_PER_LAUNCH.items():
-            if name in rows and CONFIG == 2 and args.n is None and world == 1:
+            if name in rows and args.config == 2 and args.n is None and world == 1:
                 rows[name]["traffic"] = t
         roof = dict(rows.get(dom, {}))
         roof.pop("ms", None)
@@ -532,13 +580,17 @@ def main() -> None:
                           f"{sm_mhz:.0f} MHz sampled SM clock"})
         launches = sum(k["kernels"] for k in kern.values())
         line = {
-            "metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": world,
+            "metric": metric, "value": value, "unit": "frames/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded, config 2 distributions)",
-            "config": {"workload": WORKLOAD,
-                       "cams_per_gpu": per, "gaussians": n, "l2": "inputs larger than L2 "
-                       "(targets 199 MB + params 56 MB + sort scratch per step)",
+            "data": f"synthetic (seeded, config {args.config} distributions)",
+            "config": {"workload": workload,
+                       "cams_per_gpu": per, "gaussians": n,
+                       "l2": (f"inputs {input_bytes / 1e6:.0f} MB per rank, below 2x the "
+                              "126 MB L2: L2 flushed (256 MB write) between timed steps"
+                              if flush else
+                              f"inputs {input_bytes / 1e6:.0f} MB per rank (targets + "
+                              "parameters) plus the per-step sort scratch exceed the 126 MB L2"),
                        "parallelism": f"camera-sharded dp{world}"},
             "roofline": roof,
             "kernels": {k: {**v, "share": v["ms"] / max(sum(total_ms.values()), 1e-9)}

@@ -95,7 +95,12 @@ def synthetic_scene(config: int, seed: int = 0, n: int | None = None) -> dict:
                 target_seed=seed + 1, target=target)
 
 
-def target_images(scene: dict) -> np.ndarray:
-    """Seeded uniform-[0,1] target stack (B, H, W, 3) for the MSE / L1 losses."""
-    rng = np.random.default_rng(scene["target_seed"])
-    return rng.uniform(size=(scene["B"], scene["H"], scene["W"], 3)).astype(np.float32)
+def target_images(scene: dict, cams=None) -> np.ndarray:
+    """Seeded uniform-[0,1] targets (len(cams), H, W, 3) for the MSE / L1 losses; camera k's
+    image depends on (target_seed, k) only, so a rank can make just the cameras it renders."""
+    ks = range(scene["B"]) if cams is None else cams
+    out = np.empty((len(ks), scene["H"], scene["W"], 3), np.float32)
+    for i, k in enumerate(ks):
+        rng = np.random.default_rng((scene["target_seed"], k))
+        out[i] = rng.uniform(size=(scene["H"], scene["W"], 3))
+    return out
