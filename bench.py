@@ -69,6 +69,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--n", type=int, default=None, help="override the gaussian count (debug)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--forward-only", action="store_true",
+                    help="time the forward render alone (configs 1, 2, 4)")
     ap.add_argument("--config", type=int, default=CONFIG, choices=[0, 1, 2, 3, 4],
                     help="2: the headline fwd+bwd step (default); 0: forward render only; 1: one "
                          "camera with the viewmat "
@@ -334,6 +336,10 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
 
     metric, workload, opts = FWD_BWD[args.config]
+    if args.forward_only and not opts.get("forward_only"):
+        opts = dict(opts, forward_only=True, viewmat_grad=False)
+        metric = metric.replace("fwd+bwd", "forward")
+        workload += " (forward render only)"
     scene = utils.synthetic_scene(args.config, n=args.n)
     B, H, W, f = scene["B"], scene["H"], scene["W"], scene["f"]
     n = scene["means"].shape[0]
