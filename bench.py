@@ -238,15 +238,12 @@ def train_bench(args) -> None:
         imgs, _ = sx.render_log(*params, viewmat=vm, **kw)
         loss = sx.l1_dssim_loss(imgs, tgt, ssim_lambda=SSIM_LAMBDA, views_total=B)
         loss.backward()
-        if world > 1:
-            flat = torch.cat([p.grad.reshape(-1) for p in params])
-            dist.all_reduce(flat)
-            grads = list(torch.split(flat, [p.numel() for p in params]))
-            grads = [g.view_as(p) for g, p in zip(grads, params)]
+        if world > 1:  # the shared gradients, summed in place in one group
+            with dist._coalescing_manager(device=dev):
+                for p in params:
+                    dist.all_reduce(p.grad)
             dist.all_reduce(loss.detach())
-        else:
-            grads = [p.grad for p in params]
-        opt.step(grads)
+        opt.step([p.grad for p in params])
         return loss
 
     for _ in range(args.warmup):
@@ -359,10 +356,11 @@ def main() -> None:
     denom = float(B * H * W * 3)
 
     def step(vm, tgt, ps=params):
+        """One step; returns the rendered images (forward only) or the loss."""
         if opts.get("forward_only"):
             with torch.no_grad():
                 imgs, _ = sx.render(*ps, viewmat=vm, **kw)
-            return imgs.sum()  # the step's result read back end to end
+            return imgs
         for p in ps:
             p.grad = None
         if vm.requires_grad:
@@ -370,9 +368,10 @@ def main() -> None:
         imgs, _ = sx.render(*ps, viewmat=vm, **kw)
         loss = sx.mse_loss(imgs, tgt, denom=denom)
         loss.backward()
-        if world > 1:
-            flat = torch.cat([p.grad.reshape(-1) for p in ps])
-            dist.all_reduce(flat)
+        if world > 1:  # the gradients of the shared gaussians, summed in place in one group
+            with dist._coalescing_manager(device=dev):
+                for p in ps:
+                    dist.all_reduce(p.grad)
             dist.all_reduce(loss.detach())
         return loss
 
@@ -439,22 +438,25 @@ def main() -> None:
     work = _lib.profile_report()["units"]
     _lib.profile_enable(timing=False, count_work=False)
 
-    # end to end through the public API from pinned host buffers. Every step copies its inputs
-    # (the five parameter arrays, its cameras and its target images) from pinned host memory
-    # and reads its loss back. A copy stream fills one of two device slots with step k+1's
-    # inputs while step k computes, as a prefetching data loader does; all K copies are inside
-    # the timed region.
+    # end to end through the public API from pinned host buffers. Every step copies its batch
+    # from pinned host memory -- its cameras and, with a backward, its target images -- and
+    # reads its result back: the loss, or for a forward-only step the rendered images. The
+    # gaussians are the model: like a training loop, the step keeps them resident on the device.
+    # A copy stream fills one of two device slots with step k+1's batch while step k computes
+    # (a prefetching data loader) and drains the images of forward-only steps; every copy is
+    # inside the timed region.
     e2e = None
     if not args.no_e2e:
-        pinned = [torch.from_numpy(host[k]).pin_memory() for k in host]
+        fwd_only = bool(opts.get("forward_only"))
         v_host = torch.from_numpy(np.ascontiguousarray(scene["viewmats"][cams])).pin_memory()
         t_host = torch.from_numpy(np.ascontiguousarray(targets_np)).pin_memory()
         loss_host = torch.empty((args.steps + 1,), dtype=torch.float32).pin_memory()
-        slots = [([torch.empty_like(p) for p in params],
-                  torch.empty_like(views).requires_grad_(views.requires_grad),
+        img_host = ([torch.empty((per, H, W, 3), dtype=torch.float32).pin_memory()
+                     for _ in range(2)] if fwd_only else None)
+        slots = [(torch.empty_like(views).requires_grad_(views.requires_grad),
                   torch.empty_like(target)) for _ in range(2)]
-        slot_params = [[sp.requires_grad_() for sp in sl[0]] for sl in slots]
-        h2d = sum(t.numel() * 4 for t in pinned) + v_host.numel() * 4 + t_host.numel() * 4
+        h2d = v_host.numel() * 4 + (0 if fwd_only else t_host.numel() * 4)
+        d2h = per * H * W * 3 * 4 if fwd_only else 4
         compute = torch.cuda.current_stream(dev)
         copier = torch.cuda.Stream(dev)
         copied = [torch.cuda.Event() for _ in range(2)]
@@ -464,17 +466,24 @@ def main() -> None:
             s = k % 2
             with torch.cuda.stream(copier), torch.no_grad():
                 copier.wait_event(released[s])
-                for sp, hp in zip(slot_params[s], pinned):
-                    sp.copy_(hp, non_blocking=True)
-                slots[s][1].copy_(v_host, non_blocking=True)
-                slots[s][2].copy_(t_host, non_blocking=True)
+                slots[s][0].copy_(v_host, non_blocking=True)
+                if not fwd_only:
+                    slots[s][1].copy_(t_host, non_blocking=True)
                 copied[s].record(copier)
 
         def run(k):
             s = k % 2
             compute.wait_event(copied[s])
-            loss = step(slots[s][1], slots[s][2], slot_params[s])
-            loss_host[k].copy_(loss.detach(), non_blocking=True)
+            out = step(slots[s][0], slots[s][1])
+            if fwd_only:
+                rendered = torch.cuda.Event()
+                rendered.record(compute)
+                with torch.cuda.stream(copier):
+                    copier.wait_event(rendered)
+                    img_host[s].copy_(out, non_blocking=True)
+                    out.record_stream(copier)
+            else:
+                loss_host[k].copy_(out.detach(), non_blocking=True)
             released[s].record(compute)
 
         for s in range(2):
@@ -493,15 +502,22 @@ def main() -> None:
             if k + 1 <= args.steps:
                 load(k + 1)
             run(k)
+        compute.wait_stream(copier)  # the last images are on the host
         e1.record(compute)
         torch.cuda.synchronize()
         ems = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
         if world > 1:
             dist.all_reduce(ems, op=dist.ReduceOp.MAX)
-        if not bool(torch.isfinite(loss_host[1:]).all()):
+        if fwd_only:
+            if not bool(torch.isfinite(img_host[args.steps % 2]).all()):
+                raise SystemExit("non-finite image in the end-to-end steps")
+        elif not bool(torch.isfinite(loss_host[1:]).all()):
             raise SystemExit("non-finite loss in the end-to-end steps")
         e2e = {"value": B * args.steps / (float(ems.item()) / 1e3), "unit": "frames/s",
-               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+               "inputs": "per-step cameras" + ("" if fwd_only else " and target images") +
+                         " from pinned host memory; gaussians resident (the model)",
+               "result": "rendered images to pinned host memory" if fwd_only else "loss",
                "pipelining": "copy stream, two input slots"}
 
     cpu = None
