@@ -54,7 +54,7 @@ L2_BYTES = 126 << 20
 # DRAM bytes (read + write) per launch of the full config-2 workload from single-pass ncu
 # captures (dram__bytes_read.sum + dram__bytes_write.sum), summarised in profiles/*.md
 TRAFFIC_BYTES_PER_LAUNCH = {"raster_bwd": 574.82e6, "raster_fwd": 490.61e6,
-                            "emit_keys": 974.66e6}
+                            "emit_keys": 811.68e6}
 FWD_FLOPS_PER_EVAL = 22
 BWD_FLOPS_PER_EVAL = 12
 BWD_FLOPS_PER_CONTRIB = 45
@@ -68,6 +68,9 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--impl", default="splax_b200", choices=["splax_b200", "reference"])
     ap.add_argument("--n", type=int, default=None, help="override the gaussian count (debug)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--collective", default="nccl", choices=["nccl", "nvls", "auto"],
+                    help="gradient all-reduce for N>1: NCCL, the library's NVLS kernel, or NVLS "
+                         "when the fabric offers multicast")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--forward-only", action="store_true",
                     help="time the forward render alone (configs 1, 2, 4)")
@@ -196,6 +199,37 @@ TRAIN_LRS = {"means": 1.5e-3, "log_scales": 5e-3, "quats": 1e-3, "colors_logit":
 SSIM_LAMBDA = 0.2
 
 
+def make_reducer(args, params, dev, world):
+    """The NVLS gradient all-reduce over the parameters' gradients plus the loss, or None for
+    NCCL (one rank, --collective nccl, or auto on a fabric without multicast)."""
+    if world == 1 or args.collective == "nccl":
+        return None
+    from splax_b200._collective import GradAllReduce
+
+    try:
+        return GradAllReduce([p.shape for p in params] + [(1,)], dev)
+    except RuntimeError:
+        if args.collective == "nvls":
+            raise
+        return None
+
+
+def reduce_grads(reducer, params, loss, dev):
+    """Sum the gradients (in place into p.grad) and the loss over the ranks; returns the loss."""
+    import torch.distributed as dist
+
+    if reducer is None:
+        with dist._coalescing_manager(device=dev):
+            for p in params:
+                dist.all_reduce(p.grad)
+        dist.all_reduce(loss.detach())
+        return loss
+    sums = reducer.reduce([p.grad for p in params] + [loss.detach().reshape(1)])
+    for p, g in zip(params, sums):
+        p.grad = g
+    return sums[-1].reshape(())
+
+
 def train_bench(args) -> None:
     """Config 3: one batched training step = render_log fwd+bwd of B views, fused L1 + D-SSIM
     loss, NCCL all-reduce of the gradients (camera shards), fused per-group Adam."""
@@ -231,6 +265,7 @@ def train_bench(args) -> None:
     target = torch.tensor(targets_np, device=dev)
     bg = torch.tensor(scene["background"], device=dev)
     kw = dict(background=bg, img_shape=(H, W), f=(f, f))
+    reducer = make_reducer(args, params, dev, world)
 
     def step(vm, tgt):
         for p in params:
@@ -238,11 +273,8 @@ def train_bench(args) -> None:
         imgs, _ = sx.render_log(*params, viewmat=vm, **kw)
         loss = sx.l1_dssim_loss(imgs, tgt, ssim_lambda=SSIM_LAMBDA, views_total=B)
         loss.backward()
-        if world > 1:  # the shared gradients, summed in place in one group
-            with dist._coalescing_manager(device=dev):
-                for p in params:
-                    dist.all_reduce(p.grad)
-            dist.all_reduce(loss.detach())
+        if world > 1:  # the shared gradients (and the loss) summed over the ranks
+            loss = reduce_grads(reducer, params, loss, dev)
         opt.step([p.grad for p in params])
         return loss
 
@@ -296,7 +328,9 @@ def train_bench(args) -> None:
             "data": "synthetic (seeded, config 3 distributions)",
             "config": {"workload": "config 3: render_log fwd+bwd, L1 + 0.2 D-SSIM, all-reduce, "
                                    "per-group Adam", "gaussians": n, "cams_per_gpu": per,
-                       "parallelism": f"camera-sharded dp{world}"},
+                       "parallelism": f"camera-sharded dp{world}",
+                       "collective": None if world == 1 else
+                       ("nvls (library kernel)" if reducer is not None else "nccl")},
             "loss": loss_v,
             "kernels": {k: {**v, "share": v["ms"] / max(sum(total_ms.values()), 1e-9)}
                         for k, v in kern.items()},
@@ -305,6 +339,8 @@ def train_bench(args) -> None:
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        if reducer is not None:
+            reducer.close()
         dist.barrier()
         dist.destroy_process_group()
 
@@ -354,6 +390,7 @@ def main() -> None:
     bg = torch.tensor(scene["background"], device=dev)
     kw = dict(background=bg, img_shape=(H, W), f=(f, f), antialiased=opts["antialiased"])
     denom = float(B * H * W * 3)
+    reducer = None if opts.get("forward_only") else make_reducer(args, params, dev, world)
 
     def step(vm, tgt, ps=params):
         """One step; returns the rendered images (forward only) or the loss."""
@@ -368,11 +405,8 @@ def main() -> None:
         imgs, _ = sx.render(*ps, viewmat=vm, **kw)
         loss = sx.mse_loss(imgs, tgt, denom=denom)
         loss.backward()
-        if world > 1:  # the gradients of the shared gaussians, summed in place in one group
-            with dist._coalescing_manager(device=dev):
-                for p in ps:
-                    dist.all_reduce(p.grad)
-            dist.all_reduce(loss.detach())
+        if world > 1:  # the gradients of the shared gaussians (and the loss) summed over ranks
+            loss = reduce_grads(reducer, ps, loss, dev)
         return loss
 
     for _ in range(args.warmup):
@@ -613,7 +647,9 @@ def main() -> None:
                               if flush else
                               f"inputs {input_bytes / 1e6:.0f} MB per rank (targets + "
                               "parameters) plus the per-step sort scratch exceed the 126 MB L2"),
-                       "parallelism": f"camera-sharded dp{world}"},
+                       "parallelism": f"camera-sharded dp{world}",
+                       "collective": None if world == 1 else
+                       ("nvls (library kernel)" if reducer is not None else "nccl")},
             "roofline": roof,
             "kernels": {k: {**v, "share": v["ms"] / max(sum(total_ms.values()), 1e-9)}
                         for k, v in kern.items()},
@@ -626,6 +662,8 @@ def main() -> None:
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        if reducer is not None:
+            reducer.close()
         dist.barrier()
         dist.destroy_process_group()
 

@@ -276,6 +276,20 @@ int splax_adam_step(int32_t num_arrays, float *const *params, const float *const
                     float *const *exp_avg, float *const *exp_avg_sq, const int64_t *sizes,
                     const float *lrs, int32_t step, float b1, float b2, float eps, void *stream);
 
+/* Sum all-reduce, in place, of n fp32 values held in a symmetric buffer by each of `world`
+ * ranks (one process per GPU, all on one NVSwitch fabric), through NVLink SHARP: multicast is
+ * the buffer's multicast address (16-byte aligned); flag_ptrs is a host array of `world`
+ * device pointers, rank q's uint64[world] barrier flags inside its copy of the buffer (zero
+ * before the first call). One call runs an entry barrier with `epoch`, the reduction of this
+ * rank's shard (multimem.ld_reduce + multimem.st) and an exit barrier with epoch + 1, so epochs
+ * advance by 2 per call, identically on every rank. A barrier that waits past its bound sets
+ * bit 5 in *err (device word) and returns. No counterpart in the reference, which has no
+ * multi-device path: it replaces the psum of the gaussian gradients over a camera mesh that
+ * a shard_map data-parallel training step would issue. */
+int splax_nvls_allreduce_f32(float *multicast, void *const *flag_ptrs, int32_t rank,
+                             int32_t world, int64_t n, uint64_t epoch, uint32_t *err,
+                             void *stream);
+
 /* load_ply, splax/io.py:78-98, first half: parse a 3DGS .ply header and report its vertex
  * count (host only, no GPU work). Binary little-endian files whose first element is `vertex`
  * with scalar properties, the fields x y z scale_0..2 rot_0..3 f_dc_0..2 opacity in float32. */

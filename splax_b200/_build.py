@@ -35,6 +35,7 @@ SOURCES = {
     "ssim.cu": [],
     "optim.cu": [],
     "ply.cu": [],
+    "collective.cu": [],
 }
 
 

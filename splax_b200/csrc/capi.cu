@@ -82,10 +82,12 @@ std::atomic<bool> g_count_work{false};
 constexpr int kWorkWords = 6;  // device work counters (see DeviceState::work)
 
 enum Kind { kProjectFwd, kProjectBwd, kDepthMinmax, kPairKeys, kPairSort, kPairScan, kEmit,
-            kRadixSort, kTileBins, kRasterFwd, kRasterBwd, kLoss, kOptim, kNumKinds };
+            kRadixSort, kTileBins, kRasterFwd, kRasterBwd, kLoss, kOptim, kAllReduce,
+            kNumKinds };
 const char* kKindNames[kNumKinds] = {"project_fwd", "project_bwd", "depth_minmax", "pair_keys",
                                      "pair_sort", "pair_scan", "emit_keys", "radix_sort",
-                                     "tile_bins", "raster_fwd", "raster_bwd", "loss", "optim"};
+                                     "tile_bins", "raster_fwd", "raster_bwd", "loss", "optim",
+                                     "allreduce"};
 
 // CUDA-event timing of each launch sequence on the stream it runs on, resolved lazily.
 struct KernelTimer {
@@ -1310,6 +1312,34 @@ int splax_adam_step(int32_t num_arrays, float* const* params, const float* const
       s.seg[k] = AdamSeg{params[j], grads[j], exp_avg[j], exp_avg_sq[j], sizes[j], lrs[j]};
     }
     launch_adam(s, cnt, b1, b2, bc1, bc2, eps, stream);
+  }
+  st->timer.end(stream);
+  return finish(*st, stream);
+}
+
+int splax_nvls_allreduce_f32(float* multicast, void* const* flag_ptrs, int32_t rank,
+                             int32_t world, int64_t n, uint64_t epoch, uint32_t* err,
+                             void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (multicast == nullptr || flag_ptrs == nullptr || err == nullptr || world < 1 ||
+      world > 8 || rank < 0 || rank >= world || n < 0 || epoch == 0 ||
+      reinterpret_cast<uintptr_t>(multicast) % 16 != 0)
+    return fail(SPLAX_ERR_INVALID_ARGUMENT,
+                "nvls_allreduce: NULL pointer, rank / world out of range, n < 0, epoch 0 or a "
+                "multicast address not 16-byte aligned");
+  DeviceState* st;
+  int rc = current_state(&st);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(st->mu);
+  rc = st->init();
+  if (rc) return rc;
+  auto* const* flags = reinterpret_cast<unsigned long long* const*>(flag_ptrs);
+  st->timer.begin(kAllReduce, 3, stream);
+  if (launch_nvls_barrier(flags, rank, world, epoch, err, stream) ||
+      launch_nvls_allreduce(multicast, n, rank, world, stream) ||
+      launch_nvls_barrier(flags, rank, world, epoch + 1, err, stream)) {
+    st->timer.end(stream);
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "nvls_allreduce: invalid flag array");
   }
   st->timer.end(stream);
   return finish(*st, stream);

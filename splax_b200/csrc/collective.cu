@@ -1,0 +1,154 @@
+// Sum all-reduce of the fp32 gaussian gradients across the ranks of a camera-sharded step,
+// through NVLink SHARP (NVLS) on the NVSwitch fabric. The reference has no multi-device path;
+// the exchange it stands for is the psum of the 14 per-gaussian gradient floats (means 3,
+// scales 3, quats 4, colors 3, opacity 1) that a shard_map over cameras would lower to an NCCL
+// all-reduce.
+//
+// The gradient buffer is a symmetric allocation: every rank holds a copy at the same offset,
+// and one multicast address covers all copies. Rank r owns the r-th shard of the buffer's
+// 16-byte vectors. For each vector of its shard it issues one multimem.ld_reduce (the switch
+// reads the vector from every rank and returns the sum) and one multimem.st of the sum (the
+// switch writes it to every rank's copy). Each GPU's NVLink then carries its whole buffer once
+// out (the reads of all shards) and once in (the multicast stores): 2 x 4 x n bytes whatever
+// the rank count, with no local reduction pass.
+//
+// The step runs as three launches on the caller's stream: an entry barrier (every rank's
+// gradients are complete), the shard reduction, an exit barrier (every shard's sums have
+// landed everywhere). The barriers exchange epoch numbers through a flag array that lives in
+// each rank's copy of the buffer: rank r stores the epoch into slot r of every peer's array
+// (plain peer stores, release at system scope) and waits until its own array holds the epoch
+// in every slot (acquire loads). Waits are bounded; on expiry the kernel sets an error bit and
+// returns.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace splax {
+namespace {
+
+constexpr int kMaxRanks = 8;
+constexpr long long kBarrierSpinLimit = 1ll << 24;  // with a 64 ns back-off: ~1-2 s
+constexpr int kReduceThreads = 512;
+constexpr int kReduceUnroll = 1;  // 4 and 8 loads in flight per thread measured no faster
+
+struct PeerFlags {
+  unsigned long long* p[kMaxRanks];
+};
+
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Lane q < world signals peer q and then waits for peer q's signal.
+__global__ void __launch_bounds__(32)
+nvls_barrier_kernel(PeerFlags peers, int rank, int world, unsigned long long epoch,
+                    unsigned* err) {
+  const int q = threadIdx.x;
+  if (q >= world) return;
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+  st_release_sys(peers.p[q] + rank, epoch);
+  const unsigned long long* mine = peers.p[rank] + q;
+  long long spins = 0;
+  while (ld_acquire_sys(mine) < epoch) {
+    if (++spins > kBarrierSpinLimit) {
+      atomicOr(err, kErrBarrierTimeout);
+      break;
+    }
+    __nanosleep(64);
+  }
+}
+
+__device__ __forceinline__ float4 mm_ld_reduce(const float* a) {
+  float4 r;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+               : "l"(a)
+               : "memory");
+  return r;
+}
+__device__ __forceinline__ void mm_st(float* a, float4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(a), "f"(v.x),
+               "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+
+// Each thread keeps kReduceUnroll loads in flight (consecutive threads, consecutive vectors).
+__global__ void __launch_bounds__(kReduceThreads)
+nvls_reduce_kernel(float* mc, int64_t n, int rank, int world) {
+  const int64_t nv = n >> 2;
+  const int64_t per = (nv + world - 1) / world;
+  const int64_t v0 = min(nv, static_cast<int64_t>(rank) * per);
+  const int64_t v1 = min(nv, v0 + per);
+  constexpr int64_t kChunk = static_cast<int64_t>(kReduceThreads) * kReduceUnroll;
+  for (int64_t c = v0 + static_cast<int64_t>(blockIdx.x) * kChunk; c < v1;
+       c += static_cast<int64_t>(gridDim.x) * kChunk) {
+    float4 r[kReduceUnroll];
+#pragma unroll
+    for (int u = 0; u < kReduceUnroll; ++u) {
+      const int64_t v = c + u * kReduceThreads + threadIdx.x;
+      if (v < v1) r[u] = mm_ld_reduce(mc + 4 * v);
+    }
+#pragma unroll
+    for (int u = 0; u < kReduceUnroll; ++u) {
+      const int64_t v = c + u * kReduceThreads + threadIdx.x;
+      if (v < v1) mm_st(mc + 4 * v, r[u]);
+    }
+  }
+  // the n % 4 trailing floats: the last rank, first block
+  if (rank == world - 1 && blockIdx.x == 0) {
+    const int64_t i = 4 * nv + threadIdx.x;
+    if (i < n) {
+      float x;
+      asm volatile("multimem.ld_reduce.relaxed.sys.global.add.f32 %0, [%1];"
+                   : "=f"(x)
+                   : "l"(mc + i)
+                   : "memory");
+      asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(mc + i), "f"(x)
+                   : "memory");
+    }
+  }
+  // this thread's multicast stores are performed system-wide before the kernel retires, so the
+  // exit barrier's release store (next launch) follows them
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
+}  // namespace
+
+int launch_nvls_barrier(unsigned long long* const* flags, int rank, int world,
+                        unsigned long long epoch, unsigned* err, cudaStream_t stream) {
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world) return -1;
+  PeerFlags pf{};
+  for (int q = 0; q < world; ++q) {
+    if (flags[q] == nullptr) return -1;
+    pf.p[q] = flags[q];
+  }
+  nvls_barrier_kernel<<<1, 32, 0, stream>>>(pf, rank, world, epoch, err);
+  return 0;
+}
+
+int launch_nvls_allreduce(float* multicast, int64_t n, int rank, int world,
+                          cudaStream_t stream) {
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || n < 0) return -1;
+  if (n == 0 || world == 1) return 0;
+  if (reinterpret_cast<uintptr_t>(multicast) % 16 != 0) return -1;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t per = ((n >> 2) + world - 1) / world;
+  const int64_t chunk = static_cast<int64_t>(kReduceThreads) * kReduceUnroll;
+  int64_t blocks = (per + chunk - 1) / chunk;
+  blocks = blocks < 1 ? 1 : (blocks > 4 * sms ? 4 * sms : blocks);
+  nvls_reduce_kernel<<<static_cast<unsigned>(blocks), kReduceThreads, 0, stream>>>(multicast, n,
+                                                                                   rank, world);
+  return 0;
+}
+
+}  // namespace splax

@@ -25,6 +25,7 @@ constexpr unsigned kErrEmitCount = 1u << 1;        // emission disagreed with cu
 constexpr unsigned kErrNegativeDepthKey = 1u << 2; // 64-bit key of a negative depth
 constexpr unsigned kErrCountOverflow = 1u << 3;    // intersections exceed int32
 constexpr unsigned kErrBinRange = 1u << 4;         // a sorted key decoded outside B*T bins
+constexpr unsigned kErrBarrierTimeout = 1u << 5;   // a cross-rank barrier wait gave up
 
 constexpr long long kSpinLimit = 1ll << 24;  // iterations before a look-back wait gives up
 

@@ -243,6 +243,13 @@ struct PlyLayout {
   int64_t stride;
   bool aligned;  // every needed offset and the stride are multiples of 4
 };
+// collective.cu: NVLS gradient all-reduce. flags: host array of `world` device pointers, each
+// rank's u64[world] flag array (all zero before the first epoch; epochs increase per call).
+int launch_nvls_barrier(unsigned long long* const* flags, int rank, int world,
+                        unsigned long long epoch, unsigned* err, cudaStream_t stream);
+// In-place sum over the ranks of n floats at the multicast address (16-byte aligned).
+int launch_nvls_allreduce(float* multicast, int64_t n, int rank, int world, cudaStream_t stream);
+
 int ply_parse_header(FILE* f, PlyLayout* L, int64_t* count, int64_t* body_offset,
                      std::string* why);
 void launch_ply_decode(const unsigned char* body, int64_t count, const PlyLayout& L,

@@ -172,3 +172,21 @@ def test_synthetic_scenes_are_seeded():
     assert all(np.array_equal(a[k], b[k]) for k in ("means", "scales", "quats", "colors",
                                                      "opacities", "viewmats"))
     assert a["viewmats"].shape == (8, 4, 4) and a["H"] == 1080 and a["W"] == 1920
+
+
+def test_nvls_allreduce_argument_checks(lib):
+    """The gradient all-reduce refuses bad ranks, sizes, epochs and alignment before any launch."""
+    import ctypes
+
+    from splax_b200 import _lib
+
+    flags = (ctypes.c_void_p * 2)(16, 32)
+    err = ctypes.c_void_p(64)
+    f = lib.splax_nvls_allreduce_f32
+    ok = dict(mc=ctypes.c_void_p(1 << 20), rank=0, world=2, n=8, epoch=1)
+    for bad in (dict(world=9), dict(world=0), dict(rank=2), dict(rank=-1), dict(n=-1),
+                dict(epoch=0), dict(mc=ctypes.c_void_p((1 << 20) + 4)), dict(mc=None)):
+        a = {**ok, **bad}
+        rc = f(a["mc"], flags, a["rank"], a["world"], a["n"], ctypes.c_uint64(a["epoch"]), err,
+               None)
+        assert rc == _lib.SPLAX_ERR_INVALID_ARGUMENT, bad
