@@ -68,9 +68,9 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--impl", default="splax_b200", choices=["splax_b200", "reference"])
     ap.add_argument("--n", type=int, default=None, help="override the gaussian count (debug)")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--collective", default="nccl", choices=["nccl", "nvls", "auto"],
-                    help="gradient all-reduce for N>1: NCCL, the library's NVLS kernel, or NVLS "
-                         "when the fabric offers multicast")
+    ap.add_argument("--collective", default="auto", choices=["nccl", "nvls", "auto"],
+                    help="gradient all-reduce for N>1: NCCL, the library's NVLS kernel, or auto "
+                         "(NVLS from 4 ranks when the fabric offers multicast, else NCCL)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--forward-only", action="store_true",
                     help="time the forward render alone (configs 1, 2, 4)")
@@ -200,9 +200,10 @@ SSIM_LAMBDA = 0.2
 
 
 def make_reducer(args, params, dev, world):
-    """The NVLS gradient all-reduce over the parameters' gradients plus the loss, or None for
-    NCCL (one rank, --collective nccl, or auto on a fabric without multicast)."""
-    if world == 1 or args.collective == "nccl":
+    """The library's NVLS gradient all-reduce over the parameters' gradients plus the loss, or
+    None for NCCL. auto: NVLS from 4 ranks on a fabric with multicast (at 2 ranks NCCL's ring
+    moves the same bytes and measured faster here)."""
+    if world == 1 or args.collective == "nccl" or (args.collective == "auto" and world < 4):
         return None
     from splax_b200._collective import GradAllReduce
 
@@ -215,16 +216,21 @@ def make_reducer(args, params, dev, world):
 
 
 def reduce_grads(reducer, params, loss, dev):
-    """Sum the gradients (in place into p.grad) and the loss over the ranks; returns the loss."""
+    """Sum the gradients and the loss over the ranks in one collective; p.grad becomes a view of
+    the summed buffer. Returns the summed loss."""
+    import torch
     import torch.distributed as dist
 
     if reducer is None:
-        with dist._coalescing_manager(device=dev):
-            for p in params:
-                dist.all_reduce(p.grad)
-        dist.all_reduce(loss.detach())
-        return loss
-    sums = reducer.reduce([p.grad for p in params] + [loss.detach().reshape(1)])
+        flat = torch.cat([p.grad.reshape(-1) for p in params] + [loss.detach().reshape(1)])
+        dist.all_reduce(flat)
+        sums, o = [], 0
+        for p in params:
+            sums.append(flat[o:o + p.numel()].view_as(p))
+            o += p.numel()
+        sums.append(flat[o:])
+    else:
+        sums = reducer.reduce([p.grad for p in params] + [loss.detach().reshape(1)])
     for p, g in zip(params, sums):
         p.grad = g
     return sums[-1].reshape(())
