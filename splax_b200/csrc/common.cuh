@@ -179,6 +179,128 @@ __device__ __forceinline__ int32_t ellipse_tile_count(const Ellipse& s) {
   return count;
 }
 
+// ---------------------------------------------------------------- warp-cooperative walk
+// The ellipse walks of the 32 pairs of a warp (one pair per lane), taken row by row with one
+// row per lane instead of one pair per lane: a warp's cost follows the rows of its 32 pairs,
+// not its largest pair. A row is one outer-axis tile line u of a pair's walk. Its start state is
+// the walk's rolling intersect pair at the row's lower line, computed directly from its
+// definition (the intersect at the last line <= bmax0 above rmin0, or the initial span); its end
+// state is the next row's start state, taken from the next lane by shuffle when that lane holds
+// the same pair's next row. Every float operation is the sequential walk's (ellipse_column), so
+// [mn, mx) is bit-identical to it.
+
+// ellipse_intersect on the shared fields
+__device__ __forceinline__ void walk_intersect(float B, float disc, float t, float coeff, float pu,
+                                               float pv, float coord, float& lo, float& hi) {
+  float h = coord - pu;
+  float sq = sqrtf(disc * h * h + t * coeff);
+  float bh = (-B) * h;
+  lo = (bh - sq) / coeff + pv;
+  hi = (bh + sq) / coeff + pv;
+}
+
+// Largest lane whose (non-decreasing across lanes) v is <= key.
+__device__ __forceinline__ int lift_find(int v, int key) {
+  int pos = 0;
+#pragma unroll
+  for (int st = 16; st > 0; st >>= 1) {
+    const int c = __shfl_sync(0xffffffffu, v, pos + st);
+    if (c <= key) pos += st;
+  }
+  return pos;
+}
+
+struct WarpWalk {
+  // per lane: B, disc, t, coeff, pu, pv, bmax0, amin1, amax1, bmin1, bmax1, i0, i1
+  float f[13][32];
+  // per lane: rmin0, rmin1, rmax1, isY, first row (exclusive scan of the row counts)
+  int32_t n[5][32];
+};
+
+// Shares this lane's walk (e.valid false: no rows). Returns the warp's row count; rexc = this
+// lane's first row. Ends with __syncwarp.
+__device__ __forceinline__ int warp_walk_share(WarpWalk& w, int lane, const Ellipse& e,
+                                               int& rexc) {
+  float i0 = 0.0f, i1 = 0.0f;
+  int R = 0;
+  if (e.valid) {
+    ellipse_init_span(e, i0, i1);
+    R = e.rmax0 > e.rmin0 ? e.rmax0 - e.rmin0 : 0;
+  }
+  int rinc = R;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, rinc, o);
+    if (lane >= o) rinc += v;
+  }
+  rexc = rinc - R;
+  w.f[0][lane] = e.B;
+  w.f[1][lane] = e.disc;
+  w.f[2][lane] = e.t;
+  w.f[3][lane] = e.isY ? e.A : e.C;
+  w.f[4][lane] = e.isY ? e.py : e.px;
+  w.f[5][lane] = e.isY ? e.px : e.py;
+  w.f[6][lane] = e.bmax0;
+  w.f[7][lane] = e.amin1;
+  w.f[8][lane] = e.amax1;
+  w.f[9][lane] = e.bmin1;
+  w.f[10][lane] = e.bmax1;
+  w.f[11][lane] = i0;
+  w.f[12][lane] = i1;
+  w.n[0][lane] = e.rmin0;
+  w.n[1][lane] = e.rmin1;
+  w.n[2][lane] = e.rmax1;
+  w.n[3][lane] = e.isY ? 1 : 0;
+  w.n[4][lane] = rexc;
+  __syncwarp();
+  return __shfl_sync(0xffffffffu, rinc, 31);
+}
+
+// Row r of the shared walk (all 32 lanes call together; rows = the warp's row count, rexc = this
+// lane's warp_walk_share value). For r < rows: ow = the pair's lane, u = the outer line, [mn, mx)
+// = ellipse_column's cross-axis range. For r >= rows: mn = mx = 0.
+__device__ __forceinline__ void warp_walk_row(const WarpWalk& w, int lane, int rexc, int r,
+                                              int rows, int& ow, int& u, int32_t& mn,
+                                              int32_t& mx) {
+  const bool has = r < rows;
+  ow = lift_find(rexc, has ? r : rows);
+  const float B = w.f[0][ow], disc = w.f[1][ow], t = w.f[2][ow];
+  const float coeff = w.f[3][ow], pu = w.f[4][ow], pv = w.f[5][ow];
+  const float bmax0 = w.f[6][ow], amin1 = w.f[7][ow], amax1 = w.f[8][ow];
+  const float bmin1 = w.f[9][ow], bmax1 = w.f[10][ow];
+  const int32_t rmin0 = w.n[0][ow], rmin1 = w.n[1][ow], rmax1 = w.n[2][ow];
+  u = rmin0 + (r - w.n[4][ow]);
+  float s0 = w.f[11][ow], s1 = w.f[12][ow];
+  if (has && u > rmin0) {
+    int m = u;  // the last line (m * 16, the previous row's upper line) the walk intersected
+    while (m > rmin0 && !(static_cast<float>(m - 1) * 16.0f + 16.0f <= bmax0)) --m;
+    if (m > rmin0)
+      walk_intersect(B, disc, t, coeff, pu, pv, static_cast<float>(m - 1) * 16.0f + 16.0f, s0,
+                     s1);
+  }
+  const float n0 = __shfl_down_sync(0xffffffffu, s0, 1);
+  const float n1 = __shfl_down_sync(0xffffffffu, s1, 1);
+  const int now = __shfl_down_sync(0xffffffffu, ow, 1);
+  const bool next_same = lane < 31 && r + 1 < rows && now == ow;
+  const float min_line = static_cast<float>(u) * 16.0f;
+  const float max_line = min_line + 16.0f;
+  float j0 = s0, j1 = s1;
+  if (next_same) {
+    j0 = n0;
+    j1 = n1;
+  } else if (has && max_line <= bmax0) {
+    walk_intersect(B, disc, t, coeff, pu, pv, max_line, j0, j1);
+  }
+  mn = 0;
+  mx = 0;
+  if (has) {
+    const float emin = (min_line <= amin1 && amin1 < max_line) ? bmin1 : fmin_w(s0, j0);
+    const float emax = (min_line <= amax1 && amax1 < max_line) ? bmax1 : fmax_w(s1, j1);
+    mn = imax(rmin1, imin(rmax1, f2i(emin / 16.0f)));
+    mx = imin(rmax1, imax(rmin1, f2i(emax / 16.0f + 1.0f)));
+  }
+}
+
 // Hardware base-2 exponential (MUFU): the blend kernels' exponent is pre-scaled by log2(e).
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;

@@ -127,9 +127,17 @@ __device__ __forceinline__ float aa_rho(float a, float b, float c, float eps, fl
   return sqrtf(r2);
 }
 
-// Projection of one pair; returns its tile count (0 when culled), writing every output row.
+// Projection of one pair up to its tile count: writes the culled (zero) outputs, and for a pair
+// that passes every cull returns true with its outputs in o and its ellipse walk in e (the count
+// is taken warp-cooperatively by the caller, then project_store writes the outputs).
+struct PairOut {
+  float cx, cy, ca, cb, cc, depth, rho;
+  int32_t radius;
+};
+
 template <bool AA>
-__device__ __forceinline__ int32_t project_one(const ProjectArgs& a, int64_t idx) {
+__device__ __forceinline__ bool project_setup(const ProjectArgs& a, int64_t idx, PairOut& o,
+                                              Ellipse& e) {
   int64_t bid = idx / a.n, gid = idx % a.n;
   a.xys[2 * idx] = 0.0f;
   a.xys[2 * idx + 1] = 0.0f;
@@ -143,7 +151,7 @@ __device__ __forceinline__ int32_t project_one(const ProjectArgs& a, int64_t idx
   Geom g;
   float q[4], sc[3];
   project_geom(a, idx, bid, gid, g, q, sc);
-  if (g.p[2] <= a.clip_thresh) return 0;
+  if (g.p[2] <= a.clip_thresh) return false;
   float Mt[9], V3[9];
   mat_T(g.M, Mt);
   mat_mul(g.M, Mt, V3);
@@ -166,7 +174,7 @@ __device__ __forceinline__ int32_t project_one(const ProjectArgs& a, int64_t idx
   float c11 = (TV[3] * T[3] + TV[4] * T[4]) + TV[5] * T[5];
   float cxx = c00 + 0.3f, cxy = c01, cyy = c11 + 0.3f;
   float det = cxx * cyy - cxy * cxy;
-  if (det == 0.0f) return 0;
+  if (det == 0.0f) return false;
   float inv_det = 1.0f / det;
   float ca = cyy * inv_det, cb = -cxy * inv_det, cc = cxx * inv_det;
   float rw = 1.0f / (g.p[2] + 1e-6f);
@@ -175,29 +183,39 @@ __device__ __forceinline__ int32_t project_one(const ProjectArgs& a, int64_t idx
   int32_t tbx = (a.img_w + kBlockWidth - 1) / kBlockWidth;
   int32_t tby = (a.img_h + kBlockWidth - 1) / kBlockWidth;
   float opac = a.opacities[a.sel_opac ? idx : gid];
-  if (opac < kAlphaThreshold) return 0;
+  if (opac < kAlphaThreshold) return false;
   float t = iso_level(opac);
   float ext = sqrtf(t);
   float radius_x = ceilf(ext * sqrtf(cxx));
   float radius_y = ceilf(ext * sqrtf(cyy));
-  if (radius_x <= 0.0f && radius_y <= 0.0f) return 0;
+  if (radius_x <= 0.0f && radius_y <= 0.0f) return false;
   if (center_x + radius_x <= 0.0f || center_x - radius_x >= static_cast<float>(a.img_w) ||
       center_y + radius_y <= 0.0f || center_y - radius_y >= static_cast<float>(a.img_h))
-    return 0;
-  Ellipse e;
+    return false;
   ellipse_init(ca, cb, cc, t, center_x, center_y, tbx, tby, e);
-  int32_t count = ellipse_tile_count(e);
-  if (count <= 0) return 0;
+  o.cx = center_x;
+  o.cy = center_y;
+  o.ca = ca;
+  o.cb = cb;
+  o.cc = cc;
+  o.depth = g.p[2];
+  o.radius = f2i(fmax_w(radius_x, radius_y));
+  if constexpr (AA) o.rho = aa_rho(ca, cb, cc, a.aa_eps, a.aa_eps2);
+  return true;
+}
+
+template <bool AA>
+__device__ __forceinline__ void project_store(const ProjectArgs& a, int64_t idx, const PairOut& o,
+                                              int32_t count) {
   a.num_tiles_hit[idx] = count;
-  a.depths[idx] = g.p[2];
-  a.radii[idx] = f2i(fmax_w(radius_x, radius_y));
-  a.xys[2 * idx] = center_x;
-  a.xys[2 * idx + 1] = center_y;
-  a.conics[3 * idx] = ca;
-  a.conics[3 * idx + 1] = cb;
-  a.conics[3 * idx + 2] = cc;
-  if constexpr (AA) a.rho[idx] = aa_rho(ca, cb, cc, a.aa_eps, a.aa_eps2);
-  return count;
+  a.depths[idx] = o.depth;
+  a.radii[idx] = o.radius;
+  a.xys[2 * idx] = o.cx;
+  a.xys[2 * idx + 1] = o.cy;
+  a.conics[3 * idx] = o.ca;
+  a.conics[3 * idx + 1] = o.cb;
+  a.conics[3 * idx + 2] = o.cc;
+  if constexpr (AA) a.rho[idx] = o.rho;
 }
 
 constexpr int kProjThreads = 256;
@@ -211,15 +229,35 @@ project_fwd_kernel(ProjectArgs a, unsigned long long* status, int* ticket, unsig
   __shared__ __align__(16) int32_t s_cnt[kProjTile];
   __shared__ long long s_warp[kProjThreads / 32];
   __shared__ long long s_prefix;
+  __shared__ WarpWalk s_walk[kProjThreads / 32];
+  __shared__ int32_t s_wcnt[kProjThreads / 32][32];
   if (threadIdx.x == 0) s_tile = atomicAdd(ticket, 1);
   __syncthreads();
   const int64_t tile = s_tile;
   const int64_t base = tile * kProjTile;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-#pragma unroll
   for (int k = 0; k < kProjItems; ++k) {
     const int64_t idx = base + k * kProjThreads + tid;
-    s_cnt[k * kProjThreads + tid] = idx < a.total ? project_one<AA>(a, idx) : 0;
+    PairOut o;
+    Ellipse e{};
+    const bool live = idx < a.total && project_setup<AA>(a, idx, o, e);
+    if (!live) e.valid = false;
+    // the tile count of the warp's 32 pairs, row by row across the lanes: the sum of
+    // ellipse_column's (mx - mn), as ellipse_tile_count takes it
+    s_wcnt[warp][lane] = 0;
+    int rexc;
+    const int rows = warp_walk_share(s_walk[warp], lane, e, rexc);
+    for (int c0 = 0; c0 < rows; c0 += 32) {
+      int ow, u;
+      int32_t mn, mx;
+      warp_walk_row(s_walk[warp], lane, rexc, c0 + lane, rows, ow, u, mn, mx);
+      if (c0 + lane < rows) atomicAdd(&s_wcnt[warp][ow], mx - mn);
+    }
+    __syncwarp();
+    const int32_t count = live ? s_wcnt[warp][lane] : 0;
+    __syncwarp();  // the shared walk is reused by the next item
+    if (count > 0) project_store<AA>(a, idx, o, count);
+    s_cnt[k * kProjThreads + tid] = count > 0 ? count : 0;
   }
   __syncthreads();
   // each thread scans 4 consecutive pairs; a block scan of the thread sums places them

@@ -242,59 +242,29 @@ sorted_offsets_kernel(const int32_t* __restrict__ perm, const int32_t* __restric
 
 // Emission in sorted pair order, warp-cooperative: each warp takes 32 consecutive sorted pairs
 // and produces their (image | tile) bin keys and flat ids at the pairs' offsets.
-//  1. Each lane sets up its pair's ellipse walk (the count projection made) and shares it in
-//     shared memory; the warp scans the pairs' row counts.
-//  2. Rows (outer-axis lines of the walk) are taken 32 at a time, one per lane. A row's start
-//     state is the walk's rolling intersect pair at its lower line, computed directly from its
-//     definition (the line's intersect, or the initial span for the first row); its end pair
-//     is the next row's start state, taken from the next lane by shuffle when that lane holds
-//     the same pair's next row. Every float operation is the sequential walk's, so the tiles
-//     are bit-identical to it.
+//  1. Each lane sets up its pair's ellipse walk (the count projection made) and shares it
+//     (warp_walk_share).
+//  2. Rows are taken 32 at a time, one per lane (warp_walk_row: bit-identical to the
+//     sequential walk).
 //  3. The rows' tile runs are expanded 32 tiles at a time: each lane finds its row by binary
 //     lifting over the width scan, so consecutive lanes write consecutive keys.
-// A warp's cost follows the number of rows and tiles of its 32 pairs, not its largest pair.
 // The pairs' offsets must chain (each pair starts where the previous one ends, as the scan of
 // the counts gives); a mismatch with the walk sets kErrEmitCount, and no write leaves
 // [0, count).
 constexpr int kEmitWarps = 4;
 constexpr int kEmitThreads = 32 * kEmitWarps;
-constexpr int kEmitF = 13;  // shared float fields per pair
-constexpr int kEmitI = 8;   // shared int fields per pair
-
-__device__ __forceinline__ void emit_intersect(float B, float disc, float t, float coeff, float pu,
-                                               float pv, float coord, float& lo, float& hi) {
-  // ellipse_intersect, field by field
-  float h = coord - pu;
-  float sq = sqrtf(disc * h * h + t * coeff);
-  float bh = (-B) * h;
-  lo = (bh - sq) / coeff + pv;
-  hi = (bh + sq) / coeff + pv;
-}
-
-__device__ __forceinline__ int lift_find(int v, int key) {
-  // largest lane whose (non-decreasing) v is <= key
-  int pos = 0;
-#pragma unroll
-  for (int st = 16; st > 0; st >>= 1) {
-    const int c = __shfl_sync(0xffffffffu, v, pos + st);
-    if (c <= key) pos += st;
-  }
-  return pos;
-}
 
 __global__ void __launch_bounds__(kEmitThreads) emit_sorted_kernel(EmitArgs a) {
-  __shared__ float s_f[kEmitWarps][kEmitF][32];
-  __shared__ int32_t s_i[kEmitWarps][kEmitI][32];
+  __shared__ WarpWalk s_walk[kEmitWarps];
+  __shared__ int32_t s_x[kEmitWarps][3][32];  // flat id, offset, image bits of each lane's pair
   const int lane = threadIdx.x & 31, wi = threadIdx.x >> 5;
   const int64_t V = a.dtotal ? static_cast<int64_t>(*a.dtotal) : a.total;
   const int64_t first = (static_cast<int64_t>(blockIdx.x) * kEmitWarps + wi) * 32;
   if (first >= V) return;  // warp-uniform
   const int64_t i = first + lane;
   // ---- 1. per-pair setup
-  int32_t cnt = 0, off = 0, idx = -1, R = 0;
-  Ellipse e;
-  e.valid = false;
-  float i0 = 0.0f, i1 = 0.0f;
+  int32_t cnt = 0, off = 0, idx = -1;
+  Ellipse e{};
   int32_t bid = 0;
   if (i < V) {
     idx = a.perm[i];
@@ -305,95 +275,26 @@ __global__ void __launch_bounds__(kEmitThreads) emit_sorted_kernel(EmitArgs a) {
       const float4 w1 = a.walk[2 * static_cast<int64_t>(idx) + 1];
       bid = __float_as_int(w1.z);
       ellipse_init(w0.z, w0.w, w1.x, w1.y, w0.x, w0.y, a.tbx, a.tby, e);
-      if (e.valid) {
-        ellipse_init_span(e, i0, i1);
-        R = e.rmax0 - e.rmin0;
-      }
     }
   }
-  int rinc = R;  // inclusive scan of the rows
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int v = __shfl_up_sync(0xffffffffu, rinc, o);
-    if (lane >= o) rinc += v;
-  }
-  const int rexc = rinc - R;
-  const int rows = __shfl_sync(0xffffffffu, rinc, 31);
-  {
-    float* f = &s_f[wi][0][0];
-    f[0 * 32 + lane] = e.B;
-    f[1 * 32 + lane] = e.disc;
-    f[2 * 32 + lane] = e.t;
-    f[3 * 32 + lane] = e.isY ? e.A : e.C;    // coeff
-    f[4 * 32 + lane] = e.isY ? e.py : e.px;  // pu
-    f[5 * 32 + lane] = e.isY ? e.px : e.py;  // pv
-    f[6 * 32 + lane] = e.bmax0;
-    f[7 * 32 + lane] = e.amin1;
-    f[8 * 32 + lane] = e.amax1;
-    f[9 * 32 + lane] = e.bmin1;
-    f[10 * 32 + lane] = e.bmax1;
-    f[11 * 32 + lane] = i0;
-    f[12 * 32 + lane] = i1;
-    int32_t* n = &s_i[wi][0][0];
-    n[0 * 32 + lane] = e.rmin0;
-    n[1 * 32 + lane] = e.rmin1;
-    n[2 * 32 + lane] = e.rmax1;
-    n[3 * 32 + lane] = e.isY ? 1 : 0;
-    n[4 * 32 + lane] = idx;
-    n[5 * 32 + lane] = off;
-    n[6 * 32 + lane] = static_cast<int32_t>(static_cast<uint32_t>(bid) << a.tile_n_bits);
-    n[7 * 32 + lane] = rexc;
-  }
-  __syncwarp();
+  s_x[wi][0][lane] = idx;
+  s_x[wi][1][lane] = off;
+  s_x[wi][2][lane] = static_cast<int32_t>(static_cast<uint32_t>(bid) << a.tile_n_bits);
+  int rexc;
+  const int rows = warp_walk_share(s_walk[wi], lane, e, rexc);
   const int last = V - first > 32 ? 31 : static_cast<int>(V - 1 - first);
   const int64_t out0 = __shfl_sync(0xffffffffu, off, 0);
   const int64_t out_end = __shfl_sync(0xffffffffu, off + cnt, last);
   bool bad = false;
   int64_t done = 0;  // tiles written by the earlier row chunks
-  const float* F = &s_f[wi][0][0];
-  const int32_t* N = &s_i[wi][0][0];
+  const WarpWalk& W = s_walk[wi];
   // ---- 2. rows, 32 at a time
   for (int c0 = 0; c0 < rows; c0 += 32) {
     const int r = c0 + lane;
+    int ow, u;
+    int32_t mn, mx;
+    warp_walk_row(W, lane, rexc, r, rows, ow, u, mn, mx);
     const bool has = r < rows;
-    const int ow = lift_find(rexc, has ? r : rows);  // owning lane of row r
-    const float B = F[0 * 32 + ow], disc = F[1 * 32 + ow], t = F[2 * 32 + ow];
-    const float coeff = F[3 * 32 + ow], pu = F[4 * 32 + ow], pv = F[5 * 32 + ow];
-    const float bmax0 = F[6 * 32 + ow], amin1 = F[7 * 32 + ow], amax1 = F[8 * 32 + ow];
-    const float bmin1 = F[9 * 32 + ow], bmax1 = F[10 * 32 + ow];
-    const int32_t rmin0 = N[0 * 32 + ow], rmin1 = N[1 * 32 + ow], rmax1 = N[2 * 32 + ow];
-    const int u = rmin0 + (r - N[7 * 32 + ow]);
-    // start state S(u): the intersect pair at the lower line (the walk carries the last one
-    // taken at or below bmax0), or the initial span for the first row
-    float s0 = F[11 * 32 + ow], s1 = F[12 * 32 + ow];
-    if (has && u > rmin0) {
-      int m = u;
-      while (m > rmin0 && !(static_cast<float>(m - 1) * 16.0f + 16.0f <= bmax0)) --m;
-      if (m > rmin0)
-        emit_intersect(B, disc, t, coeff, pu, pv, static_cast<float>(m - 1) * 16.0f + 16.0f,
-                       s0, s1);
-    }
-    // end state: the next row's start state
-    const float n0 = __shfl_down_sync(0xffffffffu, s0, 1);
-    const float n1 = __shfl_down_sync(0xffffffffu, s1, 1);
-    const int now = __shfl_down_sync(0xffffffffu, ow, 1);
-    const bool next_same = lane < 31 && r + 1 < rows && now == ow;
-    const float min_line = static_cast<float>(u) * 16.0f;
-    const float max_line = min_line + 16.0f;
-    float j0 = s0, j1 = s1;
-    if (next_same) {
-      j0 = n0;
-      j1 = n1;
-    } else if (has && max_line <= bmax0) {
-      emit_intersect(B, disc, t, coeff, pu, pv, max_line, j0, j1);
-    }
-    int32_t mn = 0, mx = 0;
-    if (has) {
-      const float emin = (min_line <= amin1 && amin1 < max_line) ? bmin1 : fmin_w(s0, j0);
-      const float emax = (min_line <= amax1 && amax1 < max_line) ? bmax1 : fmax_w(s1, j1);
-      mn = imax(rmin1, imin(rmax1, f2i(emin / 16.0f)));
-      mx = imin(rmax1, imax(rmin1, f2i(emax / 16.0f + 1.0f)));
-    }
     const int w = has ? max(mx - mn, 0) : 0;
     int winc = w;
 #pragma unroll
@@ -404,12 +305,12 @@ __global__ void __launch_bounds__(kEmitThreads) emit_sorted_kernel(EmitArgs a) {
     const int wexc = winc - w;
     const int total = __shfl_sync(0xffffffffu, winc, 31);
     const int64_t pos = out0 + done + wexc;
-    if (has && u == rmin0 && pos != N[5 * 32 + ow]) bad = true;  // offsets must chain
-    const bool isY = N[3 * 32 + ow] != 0;
-    const uint32_t key0 = static_cast<uint32_t>(N[6 * 32 + ow]) |
+    if (has && u == W.n[0][ow] && pos != s_x[wi][1][ow]) bad = true;  // offsets must chain
+    const bool isY = W.n[3][ow] != 0;
+    const uint32_t key0 = static_cast<uint32_t>(s_x[wi][2][ow]) |
                           static_cast<uint32_t>(isY ? u * a.tbx + mn : mn * a.tbx + u);
     const int kstep = isY ? 1 : a.tbx;
-    const int32_t val = N[4 * 32 + ow];
+    const int32_t val = s_x[wi][0][ow];
     // ---- 3. expand the chunk's tiles, 32 at a time
     for (int q0 = 0; q0 < total; q0 += 32) {
       const int q = q0 + lane;
