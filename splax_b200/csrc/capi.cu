@@ -424,7 +424,8 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
     // look-back words for the larger of the two sorts
     const int64_t t_pairs = (total + sort_tile_items(pair64) - 1) / sort_tile_items(pair64);
     const int64_t t_bins = (st.isect_cap + sort_tile_items(false) - 1) / sort_tile_items(false);
-    const size_t need = sizeof(unsigned long long) * 256 * std::max(t_pairs, t_bins);
+    const size_t need =
+        sizeof(unsigned long long) * kRadixMaxDigits * std::max(t_pairs, t_bins);
     if (st.status.bytes < need) {
       SPLAX_CUDA(cudaStreamSynchronize(stream));
       cudaError_t e = buf_reserve(st.status, need);
@@ -492,7 +493,7 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
   ss.keys[1] = st.pkeys[1].p;
   ss.vals[0] = static_cast<int32_t*>(st.pvals[0].p);
   ss.vals[1] = static_cast<int32_t*>(st.pvals[1].p);
-  const int pair_passes = (pair_bits + 7) / 8;
+  const int pair_passes = radix_passes(pair_bits);
   st.timer.begin(kPairSort, total > 1 && pair_passes ? 2 + pair_passes : 0, stream);
   // only the V pairs that hit a tile are sorted; V stays on the device
   ss.filter_sentinel = true;
@@ -533,7 +534,7 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
   ss.keys[1] = st.keys[1].p;
   ss.vals[0] = static_cast<int32_t*>(st.vals[0].p);
   ss.vals[1] = static_cast<int32_t*>(st.vals[1].p);
-  const int passes = (bin_bits + 7) / 8;
+  const int passes = radix_passes(bin_bits);
   st.timer.begin(kRadixSort, count > 1 && passes ? 2 + passes : 0, stream);
   const int fin = radix_sort_pairs(ss, false, count, bin_bits, stream);
   st.timer.end(stream);

@@ -148,6 +148,10 @@ struct SortScratch {
   unsigned* err;
 };
 int sort_tile_items(bool key64);
+// Radix passes a sort of `bits` significant bits takes (8- or 9-bit digits; look-back words per
+// tile: 2^digit bits, at most kRadixMaxDigits).
+int radix_passes(int bits);
+constexpr int kRadixMaxDigits = 512;
 int radix_sort_pairs(const SortScratch& s, bool key64, int64_t count, int bits,
                      cudaStream_t stream);
 void launch_tile_bins(const uint32_t* keys, int64_t count, int32_t tile_n_bits,

@@ -370,25 +370,29 @@ constexpr int kItems32 = 12;  // 6144 keys per tile for 32-bit keys
 constexpr int kItems64 = 8;   // 4096 keys per tile for 64-bit keys
 constexpr int kHistThreads = 256;
 constexpr int kHistItems = 32;
+constexpr int kRadixHistWords = 2048;  // per histogram array: passes x digits
 
-// Upfront digit histograms of every pass (up to 8) in one read of the keys: four sets of
-// shared counters, each shared by two warps (less same-address contention than one
-// block-wide set), 16-byte loads, then one global atomic per (pass, digit) and block.
-template <typename K>
+// Upfront digit histograms of every pass in one read of the keys (RB-bit digits: up to 8 passes
+// of 8 bits or 4 of 9): four sets of shared counters, each shared by two warps (less
+// same-address contention than one block-wide set), 16-byte loads, then one global atomic per
+// (pass, digit) and block.
+template <typename K, int RB>
 __global__ void __launch_bounds__(kHistThreads)
 radix_hist_kernel(const K* __restrict__ keys, int64_t count, bool filter, int passes,
                   uint32_t* hist) {
   constexpr int kSets = 4;
+  constexpr int D = 1 << RB;
+  constexpr int kMaxPasses = kRadixHistWords / D;
   constexpr int kVec = 16 / sizeof(K);  // keys per 16-byte load
-  __shared__ uint32_t s[kSets][8][256];
+  __shared__ uint32_t s[kSets][kMaxPasses][D];
   const int warp = (threadIdx.x >> 5) & (kSets - 1);
-  for (int i = threadIdx.x; i < kSets * 8 * 256; i += kHistThreads) (&s[0][0][0])[i] = 0;
+  for (int i = threadIdx.x; i < kSets * kMaxPasses * D; i += kHistThreads) (&s[0][0][0])[i] = 0;
   __syncthreads();
   const int64_t base = static_cast<int64_t>(blockIdx.x) * kHistThreads * kHistItems;
   const int64_t end = min(count, base + static_cast<int64_t>(kHistThreads) * kHistItems);
   auto add = [&](uint64_t key) {
     if (filter && key == static_cast<uint64_t>(static_cast<K>(~K(0)))) return;  // left out
-    for (int p = 0; p < passes; ++p) atomicAdd(&s[warp][p][(key >> (8 * p)) & 255u], 1u);
+    for (int p = 0; p < passes; ++p) atomicAdd(&s[warp][p][(key >> (RB * p)) & (D - 1)], 1u);
   };
   if (end - base == static_cast<int64_t>(kHistThreads) * kHistItems) {
     const uint4* v = reinterpret_cast<const uint4*>(keys + base);
@@ -407,12 +411,12 @@ radix_hist_kernel(const K* __restrict__ keys, int64_t count, bool filter, int pa
       add(static_cast<uint64_t>(keys[i]));
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < passes * 256; i += kHistThreads) {
-    const int p = i >> 8, d = i & 255;
+  for (int i = threadIdx.x; i < passes * D; i += kHistThreads) {
+    const int p = i >> RB, d = i & (D - 1);
     uint32_t c = 0;
 #pragma unroll
     for (int w = 0; w < kSets; ++w) c += s[w][p][d];
-    if (c) atomicAdd(&hist[p * 256 + d], c);
+    if (c) atomicAdd(&hist[p * D + d], c);
   }
 }
 
@@ -433,20 +437,22 @@ __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* s
   return wpre + inc - v;
 }
 
-// exclusive scan of each pass's 256-digit histogram: offsets[p][d]; with total_out, pass 0
-// also writes the number of keys sorted
-__global__ void radix_scan_kernel(const uint32_t* hist, uint32_t* offsets, int32_t* total_out) {
-  __shared__ uint32_t s_warp[8];
+// exclusive scan of each pass's D-digit histogram (D threads): offsets[p][d]; with total_out,
+// pass 0 also writes the number of keys sorted
+template <int D>
+__global__ void __launch_bounds__(D)
+radix_scan_kernel(const uint32_t* hist, uint32_t* offsets, int32_t* total_out) {
+  __shared__ uint32_t s_warp[D / 32];
   const int p = blockIdx.x;
-  const uint32_t v = hist[p * 256 + threadIdx.x];
-  const uint32_t ex = block_exclusive_scan<256>(v, s_warp);
-  offsets[p * 256 + threadIdx.x] = ex;
-  if (total_out && p == 0 && threadIdx.x == 255) *total_out = static_cast<int32_t>(ex + v);
+  const uint32_t v = hist[p * D + threadIdx.x];
+  const uint32_t ex = block_exclusive_scan<D>(v, s_warp);
+  offsets[p * D + threadIdx.x] = ex;
+  if (total_out && p == 0 && threadIdx.x == D - 1) *total_out = static_cast<int32_t>(ex + v);
 }
 
 // FILTER (first pass of the depth sort): all-ones keys are neither ranked nor written, so the
-// output holds only the other keys, in stable order.
-template <typename K, int ITEMS, int NT, bool FILTER>
+// output holds only the other keys, in stable order. RB: digit bits (8 or 9; NT >= 2^RB).
+template <typename K, int ITEMS, int NT, bool FILTER, int RB>
 __global__ void __launch_bounds__(NT)
 onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* __restrict__ kout,
                 int32_t* __restrict__ vout, int64_t count, const int32_t* dcount, int shift,
@@ -454,9 +460,11 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
                 unsigned* err) {
   constexpr int TILE = NT * ITEMS;
   constexpr int kSortWarps = NT / 32;
-  __shared__ uint32_t s_wh[kSortWarps][256];
-  __shared__ uint32_t s_bx[256];
-  __shared__ long long s_gb[256];
+  constexpr int D = 1 << RB;
+  static_assert(NT >= D, "one thread per digit");
+  __shared__ uint32_t s_wh[kSortWarps][D];
+  __shared__ uint32_t s_bx[D];
+  __shared__ long long s_gb[D];
   __shared__ uint32_t s_warp[kSortWarps];
   __shared__ int s_tile;
   __shared__ int s_tile_keys;
@@ -465,7 +473,7 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
   int32_t* s_vals = reinterpret_cast<int32_t*>(s_raw + TILE * sizeof(K));
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int i = tid; i < kSortWarps * 256; i += NT) (&s_wh[0][0])[i] = 0;
+  for (int i = tid; i < kSortWarps * D; i += NT) (&s_wh[0][0])[i] = 0;
   if (tid == 0) s_tile = atomicAdd(tile_counter, 1);
   __syncthreads();
   const int64_t tile = s_tile;
@@ -495,12 +503,12 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
   for (int it = 0; it < ITEMS; ++it) {
     const int pos = warp_base + it * 32 + lane;
     const bool valid = pos < nvalid && (!FILTER || k[it] != static_cast<K>(~K(0)));
-    const uint32_t d = static_cast<uint32_t>(static_cast<uint64_t>(k[it]) >> shift) & 255u;
+    const uint32_t d = static_cast<uint32_t>(static_cast<uint64_t>(k[it]) >> shift) & (D - 1);
     // lanes holding the same digit: intersect one ballot per digit bit (cheaper than a
     // match instruction over up to 32 distinct digits); invalid lanes match nobody
     unsigned peers = __ballot_sync(0xffffffffu, valid);
 #pragma unroll
-    for (int bit = 0; bit < 8; ++bit) {
+    for (int bit = 0; bit < RB; ++bit) {
       const unsigned b = __ballot_sync(0xffffffffu, (d >> bit) & 1u);
       peers &= ((d >> bit) & 1u) ? b : ~b;
     }
@@ -515,7 +523,7 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
   // per digit (threads 0..255): warp exclusive offsets, the block's count, the look-back
   uint32_t sum = 0;
   long long prefix = 0;
-  if (tid < 256) {
+  if (tid < D) {
     const int dg = tid;
 #pragma unroll
     for (int w = 0; w < kSortWarps; ++w) {
@@ -523,7 +531,7 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
       s_wh[w][dg] = sum;
       sum += c;
     }
-    unsigned long long* st = status + tile * 256 + dg;
+    unsigned long long* st = status + tile * D + dg;
     if (tile == 0) {
       st_relaxed(st, kLookbackInc | sum);
     } else {
@@ -538,7 +546,7 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
         unsigned long long w[kLookAhead];
 #pragma unroll
         for (int q = 0; q < kLookAhead; ++q)
-          w[q] = j - q >= 0 ? ld_relaxed(status + (j - q) * 256 + dg) : kLookbackInc;
+          w[q] = j - q >= 0 ? ld_relaxed(status + (j - q) * D + dg) : kLookbackInc;
         int used = 0;
 #pragma unroll
         for (int q = 0; q < kLookAhead; ++q) {
@@ -561,8 +569,8 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
     }
   }
   const uint32_t excl = block_exclusive_scan<NT>(sum, s_warp);
-  if (tid == 255) s_tile_keys = static_cast<int>(excl + sum);  // keys this tile writes
-  if (tid < 256) {
+  if (tid == D - 1) s_tile_keys = static_cast<int>(excl + sum);  // keys this tile writes
+  if (tid < D) {
     s_bx[tid] = excl;
     s_gb[tid] = static_cast<long long>(goff[tid]) + prefix - static_cast<long long>(excl);
   }
@@ -571,7 +579,7 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
   for (int it = 0; it < ITEMS; ++it) {
     const int pos = warp_base + it * 32 + lane;
     if (pos < nvalid && (!FILTER || k[it] != static_cast<K>(~K(0)))) {
-      const uint32_t d = static_cast<uint32_t>(static_cast<uint64_t>(k[it]) >> shift) & 255u;
+      const uint32_t d = static_cast<uint32_t>(static_cast<uint64_t>(k[it]) >> shift) & (D - 1);
       const uint32_t lpos = s_bx[d] + s_wh[warp][d] + rank[it];
       s_keys[lpos] = k[it];
       s_vals[lpos] = val[it];
@@ -584,7 +592,7 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
     const int p = j * NT + tid;
     if (p < tile_keys) {
       const K kk = s_keys[p];
-      const uint32_t d = static_cast<uint32_t>(static_cast<uint64_t>(kk) >> shift) & 255u;
+      const uint32_t d = static_cast<uint32_t>(static_cast<uint64_t>(kk) >> shift) & (D - 1);
       const long long dst = s_gb[d] + p;
       if (dst >= 0 && dst < count) {
         kout[dst] = kk;
@@ -646,54 +654,64 @@ tile_bins_kernel(const uint32_t* __restrict__ keys, int64_t count, int32_t tile_
   }
 }
 
-template <typename K, int ITEMS, int NT, bool FILTER>
+template <typename K, int ITEMS, int NT, bool FILTER, int RB>
 void set_onesweep_smem() {
   static bool done = false;  // per instantiation: static + dynamic exceeds 48 KiB
   if (!done) {
-    cudaFuncSetAttribute(onesweep_kernel<K, ITEMS, NT, FILTER>,
+    cudaFuncSetAttribute(onesweep_kernel<K, ITEMS, NT, FILTER, RB>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(NT * ITEMS * (sizeof(K) + sizeof(int32_t))));
     done = true;
   }
 }
 
-// Stable LSD sort of `count` keys. With s.filter_sentinel the all-ones keys are dropped by the
-// histogram and the first pass, s.vcount receives how many keys remain, and the later passes
-// read that device-side count (their grids stay sized for `count`; surplus tiles leave).
-template <typename K, int ITEMS, int NT>
+// Stable LSD sort of `count` keys by their low `bits` bits in RB-bit digits. With
+// s.filter_sentinel the all-ones keys are dropped by the histogram and the first pass, s.vcount
+// receives how many keys remain, and the later passes read that device-side count (their grids
+// stay sized for `count`; surplus tiles leave).
+template <typename K, int ITEMS, int NT, int RB>
 int sort_impl(const SortScratch& s, int64_t count, int bits, cudaStream_t stream) {
-  const int passes = (bits + 7) / 8;
+  constexpr int D = 1 << RB;
+  const int passes = (bits + RB - 1) / RB;
   uint32_t* hist = s.hist;
-  uint32_t* offsets = s.hist + 8 * 256;
-  cudaMemsetAsync(hist, 0, sizeof(uint32_t) * 8 * 256, stream);
+  uint32_t* offsets = s.hist + kRadixHistWords;
+  cudaMemsetAsync(hist, 0, sizeof(uint32_t) * kRadixHistWords, stream);
   cudaMemsetAsync(s.tile_counters, 0, sizeof(int) * 8, stream);
   const int64_t hblocks = (count + kHistThreads * kHistItems - 1) / (kHistThreads * kHistItems);
-  radix_hist_kernel<K><<<static_cast<unsigned>(hblocks), kHistThreads, 0, stream>>>(
+  radix_hist_kernel<K, RB><<<static_cast<unsigned>(hblocks), kHistThreads, 0, stream>>>(
       reinterpret_cast<const K*>(s.keys[0]), count, s.filter_sentinel, passes, hist);
-  radix_scan_kernel<<<passes, 256, 0, stream>>>(hist, offsets,
-                                                 s.filter_sentinel ? s.vcount : nullptr);
+  radix_scan_kernel<D><<<passes, D, 0, stream>>>(hist, offsets,
+                                                s.filter_sentinel ? s.vcount : nullptr);
   constexpr int TILE = NT * ITEMS;
   const int64_t tiles = (count + TILE - 1) / TILE;
   const size_t smem = TILE * (sizeof(K) + sizeof(int32_t));
-  set_onesweep_smem<K, ITEMS, NT, false>();
-  set_onesweep_smem<K, ITEMS, NT, true>();
+  set_onesweep_smem<K, ITEMS, NT, false, RB>();
+  set_onesweep_smem<K, ITEMS, NT, true, RB>();
   int cur = 0;
   for (int p = 0; p < passes; ++p) {
-    cudaMemsetAsync(s.status, 0, sizeof(unsigned long long) * tiles * 256, stream);
+    cudaMemsetAsync(s.status, 0, sizeof(unsigned long long) * tiles * D, stream);
     const K* kin = reinterpret_cast<const K*>(s.keys[cur]);
     K* kout = reinterpret_cast<K*>(s.keys[cur ^ 1]);
     if (s.filter_sentinel && p == 0)
-      onesweep_kernel<K, ITEMS, NT, true><<<static_cast<unsigned>(tiles), NT, smem, stream>>>(
-          kin, s.vals[cur], kout, s.vals[cur ^ 1], count, nullptr, 8 * p, offsets + p * 256,
-          s.status, s.tile_counters + p, s.err);
+      onesweep_kernel<K, ITEMS, NT, true, RB>
+          <<<static_cast<unsigned>(tiles), NT, smem, stream>>>(
+              kin, s.vals[cur], kout, s.vals[cur ^ 1], count, nullptr, RB * p,
+              offsets + p * D, s.status, s.tile_counters + p, s.err);
     else
-      onesweep_kernel<K, ITEMS, NT, false><<<static_cast<unsigned>(tiles), NT, smem, stream>>>(
-          kin, s.vals[cur], kout, s.vals[cur ^ 1], count,
-          s.filter_sentinel ? s.vcount : nullptr, 8 * p, offsets + p * 256, s.status,
-          s.tile_counters + p, s.err);
+      onesweep_kernel<K, ITEMS, NT, false, RB>
+          <<<static_cast<unsigned>(tiles), NT, smem, stream>>>(
+              kin, s.vals[cur], kout, s.vals[cur ^ 1], count,
+              s.filter_sentinel ? s.vcount : nullptr, RB * p, offsets + p * D, s.status,
+              s.tile_counters + p, s.err);
     cur ^= 1;
   }
   return cur;
+}
+
+// 9-bit digits where they save a pass (17-18, 25-27 and 33-36 significant bits), else 8.
+int radix_digit_bits(int bits) {
+  const int p8 = (bits + 7) / 8, p9 = (bits + 8) / 9;
+  return p9 < p8 && p9 <= kRadixHistWords / 512 ? 9 : 8;
 }
 
 }  // namespace
@@ -764,8 +782,16 @@ int radix_sort_pairs(const SortScratch& s, bool key64, int64_t count, int bits,
   }
   // with the filter even a single key goes through, so that vcount is written
   if (count <= 1 && !s.filter_sentinel) return 0;
-  return key64 ? sort_impl<uint64_t, kItems64, kSortThreads>(s, count, bits, stream)
-               : sort_impl<uint32_t, kItems32, kSortThreads>(s, count, bits, stream);
+  if (radix_digit_bits(bits) == 9)
+    return key64 ? sort_impl<uint64_t, kItems64, kSortThreads, 9>(s, count, bits, stream)
+                 : sort_impl<uint32_t, kItems32, kSortThreads, 9>(s, count, bits, stream);
+  return key64 ? sort_impl<uint64_t, kItems64, kSortThreads, 8>(s, count, bits, stream)
+               : sort_impl<uint32_t, kItems32, kSortThreads, 8>(s, count, bits, stream);
+}
+
+int radix_passes(int bits) {
+  const int rb = radix_digit_bits(bits);
+  return (bits + rb - 1) / rb;
 }
 
 void launch_tile_bins(const uint32_t* keys, int64_t count, int32_t tile_n_bits,

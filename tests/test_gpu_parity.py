@@ -97,7 +97,9 @@ def _sort_cuda(sx, xys, depths, radii, conics, map_opac, cum, n, B, H, W, key_bi
 
 
 @pytest.mark.parametrize("key_bits", [0, 32, 64])
-@pytest.mark.parametrize("n,H,W,B", [(30_000, 256, 256, 1), (20_000, 200, 330, 3)])
+@pytest.mark.parametrize("n,H,W,B", [(30_000, 256, 256, 1), (20_000, 200, 330, 3),
+                                     # 17-bit bin keys and 17/26-bit pair keys: 9-bit digits
+                                     (6_000, 2160, 3840, 4)])
 def test_sort_and_bin_bit_exact(sx, oracle_lib, key_bits, n, H, W, B):
     views = viewmat() if B == 1 else np.stack([viewmat(0.1 * i) for i in range(B)])
     (m, s, q, c, op, bg, _, _), cu, orc = _proj_both(sx, oracle_lib, n, H, W, 5, views)
