@@ -266,6 +266,14 @@ int splax_l1_dssim_loss_bwd(const float *img, const float *target, int32_t B, in
                             int32_t W, int32_t views_total, float ssim_lambda,
                             const float *v_loss, float *grad, void *stream);
 
+/* splax_l1_dssim_loss and its gradient for a unit cotangent (v_loss = 1) in one pass: the
+ * training step's loss and gradient together, at about the cost of the gradient alone. loss:
+ * one device float; grad: img's shape, aliasing neither input. Scale grad by the cotangent when
+ * it is not 1. */
+int splax_l1_dssim_loss_and_grad(const float *img, const float *target, int32_t B, int32_t H,
+                                 int32_t W, int32_t views_total, float ssim_lambda, float *loss,
+                                 float *grad, void *stream);
+
 /* Fused per-parameter Adam update, in place, of num_arrays fp32 parameter arrays (device
  * pointers in host arrays: params, grads, first / second moments, element counts, learning
  * rates). No counterpart in the reference, whose training step uses optax.adam per group

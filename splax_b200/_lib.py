@@ -61,6 +61,7 @@ SIGNATURES: dict[str, list] = {
     "splax_mse_loss": [P, P, I64, F32, P, P],
     "splax_l1_dssim_loss": [P, P, I32, I32, I32, I32, F32, P, P],
     "splax_l1_dssim_loss_bwd": [P, P, I32, I32, I32, I32, F32, P, P, P],
+    "splax_l1_dssim_loss_and_grad": [P, P, I32, I32, I32, I32, F32, P, P, P],
     "splax_adam_step": [I32, P, P, P, P, P, P, I32, F32, F32, F32, P],
     "splax_nvls_allreduce_f32": [P, P, I32, I32, I64, ctypes.c_uint64, P, P],
     "splax_ply_info": [ctypes.c_char_p, P],

@@ -68,20 +68,37 @@ class _L1DssimFn(torch.autograd.Function):
         H, W = a.shape[-3], a.shape[-2]
         loss = torch.empty((), device=dev, dtype=torch.float32)
         lib = _lib.load()
+        # a training step takes the gradient next: compute it with the loss in one pass (for a
+        # unit cotangent; backward scales it)
+        fused = bool(ctx.needs_input_grad[0])
         with torch.cuda.device(dev):
-            rc = lib.splax_l1_dssim_loss(_lib.ptr(a), _lib.ptr(t), B, H, W, int(views_total),
-                                         float(ssim_lambda), _lib.ptr(loss), _lib.stream_of(a))
+            if fused:
+                g = torch.empty_like(a)
+                rc = lib.splax_l1_dssim_loss_and_grad(
+                    _lib.ptr(a), _lib.ptr(t), B, H, W, int(views_total), float(ssim_lambda),
+                    _lib.ptr(loss), _lib.ptr(g), _lib.stream_of(a))
+            else:
+                rc = lib.splax_l1_dssim_loss(_lib.ptr(a), _lib.ptr(t), B, H, W, int(views_total),
+                                             float(ssim_lambda), _lib.ptr(loss),
+                                             _lib.stream_of(a))
         _lib.check(rc)
-        ctx.save_for_backward(a, t)
+        if fused:
+            ctx.save_for_backward(g)
+        else:
+            ctx.save_for_backward(a, t)
+        ctx.fused = fused
         ctx.args = (B, H, W, int(views_total), float(ssim_lambda), img.dtype)
         return loss
 
     @staticmethod
     def backward(ctx, v_loss):
-        a, t = ctx.saved_tensors
         B, H, W, views_total, lam, dtype = ctx.args
-        g = torch.empty_like(a)
         v = v_loss.detach().to(torch.float32).reshape(()).contiguous()
+        if ctx.fused:
+            (g,) = ctx.saved_tensors
+            return g.mul_(v).to(dtype), None, None, None
+        a, t = ctx.saved_tensors
+        g = torch.empty_like(a)
         lib = _lib.load()
         with torch.cuda.device(a.device):
             rc = lib.splax_l1_dssim_loss_bwd(_lib.ptr(a), _lib.ptr(t), B, H, W, views_total, lam,

@@ -1239,8 +1239,7 @@ int splax_l1_dssim_loss(const float* img, const float* target, int32_t B, int32_
     SPLAX_CUDA(cudaGetLastError());
     st->ssim_window = true;
   }
-  const int64_t parts = l1_dssim_partials(B, H, W);
-  SPLAX_CUDA(buf_reserve(st->ssim_partials, sizeof(double2) * parts));
+  SPLAX_CUDA(buf_reserve(st->ssim_partials, sizeof(double2) * l1_dssim_partials_max(B, H, W)));
   const double V = views_total, lam = ssim_lambda;
   const double l1_scale = (1.0 - lam) / (V * H * W * 3.0);
   const double ssim_scale = lam / (V * (H - 10.0) * (W - 10.0) * 3.0);
@@ -1277,6 +1276,40 @@ int splax_l1_dssim_loss_bwd(const float* img, const float* target, int32_t B, in
   const float ssim_grad = static_cast<float>(-lam / (V * (H - 10.0) * (W - 10.0) * 3.0));
   st->timer.begin(kLoss, 1, stream);
   launch_l1_dssim_bwd(img, target, B, H, W, l1_scale, ssim_grad, v_loss, grad, stream);
+  st->timer.end(stream);
+  return finish(*st, stream);
+}
+
+int splax_l1_dssim_loss_and_grad(const float* img, const float* target, int32_t B, int32_t H,
+                                 int32_t W, int32_t views_total, float ssim_lambda, float* loss,
+                                 float* grad, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  int rc = l1_dssim_check(img, target, B, H, W, views_total, ssim_lambda,
+                          "l1_dssim_loss_and_grad");
+  if (rc) return rc;
+  if (loss == nullptr || grad == nullptr)
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "l1_dssim_loss_and_grad: loss or grad is NULL");
+  DeviceState* st;
+  rc = current_state(&st);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(st->mu);
+  rc = st->init();
+  if (rc) return rc;
+  if (!st->ssim_window) {
+    float w[11];
+    ssim_window_weights(w);
+    ssim_set_window(w);
+    SPLAX_CUDA(cudaGetLastError());
+    st->ssim_window = true;
+  }
+  SPLAX_CUDA(buf_reserve(st->ssim_partials, sizeof(double2) * l1_dssim_partials_max(B, H, W)));
+  const double V = views_total, lam = ssim_lambda;
+  const double l1_scale = (1.0 - lam) / (V * H * W * 3.0);
+  const double ssim_scale = lam / (V * (H - 10.0) * (W - 10.0) * 3.0);
+  st->timer.begin(kLoss, 2, stream);
+  launch_l1_dssim_and_grad(img, target, B, H, W, l1_scale, ssim_scale, lam * B / V,
+                           static_cast<float>(l1_scale), static_cast<float>(-ssim_scale),
+                           static_cast<double2*>(st->ssim_partials.p), loss, grad, stream);
   st->timer.end(stream);
   return finish(*st, stream);
 }

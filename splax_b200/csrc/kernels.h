@@ -223,6 +223,13 @@ void launch_l1_dssim(const float* img, const float* tgt, int32_t B, int32_t H, i
 void launch_l1_dssim_bwd(const float* img, const float* tgt, int32_t B, int32_t H, int32_t W,
                          float l1_scale, float ssim_grad_scale, const float* v_loss, float* grad,
                          cudaStream_t stream);
+// The loss and its gradient for a unit cotangent in one pass (the backward kernel, which also
+// sums the map entries and L1 it owns); partials: l1_dssim_partials_max entries.
+int64_t l1_dssim_partials_max(int32_t B, int32_t H, int32_t W);
+void launch_l1_dssim_and_grad(const float* img, const float* tgt, int32_t B, int32_t H,
+                              int32_t W, double l1_scale, double ssim_scale, double ssim_const,
+                              float l1_grad_scale, float ssim_grad_scale, double2* partials,
+                              float* loss, float* grad, cudaStream_t stream);
 
 // Fused multi-array Adam (optim.cu): up to kAdamMaxSegs parameter arrays per launch.
 constexpr int kAdamMaxSegs = 8;

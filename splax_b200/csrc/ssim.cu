@@ -194,10 +194,15 @@ __global__ void l1_dssim_finalize_kernel(const double2* partials, int64_t count,
 constexpr int kBx = kTileX + 2 * kHalo, kBy = kTileY + 2 * kHalo;  // 52 x 36 input
 constexpr int kMx = kTileX + kHalo, kMy = kTileY + kHalo;          // 42 x 26 map
 
+// FUSED (the loss and its gradient in one pass, for a unit cotangent): the CTA also sums the
+// SSIM map entries it owns ([x0, x0+32) x [y0, y0+16) of the map) and the L1 of its input
+// pixels, and writes them as its fp64 partials.
+template <bool FUSED>
 __global__ void __launch_bounds__(kSsimThreads)
 l1_dssim_bwd_kernel(const float* __restrict__ img, const float* __restrict__ tgt, int32_t H,
                     int32_t W, int32_t tiles_x, float l1_scale, float ssim_grad_scale,
-                    const float* __restrict__ v_loss, float* __restrict__ grad) {
+                    const float* __restrict__ v_loss, float* __restrict__ grad,
+                    double2* partials) {
   extern __shared__ float smem[];
   float* s_a = smem;                    // [kBy][kBx]
   float* s_b = s_a + kBy * kBx;         // [kBy][kBx]
@@ -212,8 +217,9 @@ l1_dssim_bwd_kernel(const float* __restrict__ img, const float* __restrict__ tgt
   const float* ia = img + b * H * static_cast<int64_t>(W) * 3;
   const float* ib = tgt + b * H * static_cast<int64_t>(W) * 3;
   float* go = grad + b * H * static_cast<int64_t>(W) * 3;
-  const float vl = *v_loss;
+  const float vl = FUSED ? 1.0f : *v_loss;
   const float s_ssim = ssim_grad_scale * vl, s_l1 = l1_scale * vl;
+  float ssum = 0.0f, l1 = 0.0f;  // FUSED: owned map entries and input pixels
   for (int c = 0; c < 3; ++c) {
     for (int i = threadIdx.x; i < kBy * kBx; i += kSsimThreads) {
       const int py = i / kBx, px = i % kBx;
@@ -258,7 +264,8 @@ l1_dssim_bwd_kernel(const float* __restrict__ img, const float* __restrict__ tgt
 #pragma unroll
           for (int q = 0; q < 5; ++q) e[q] = fmaf(w, s_h[(q * kBy + y + v) * kMx + x], e[q]);
         }
-        ssim_entry<true>(e[0], e[1], e[2], e[3], e[4], &gm, &gaa, &gab);
+        const float S = ssim_entry<true>(e[0], e[1], e[2], e[3], e[4], &gm, &gaa, &gab);
+        if (FUSED && y >= kHalo && x >= kHalo) ssum += S;
       }
       s_g[(0 * kMy + y) * kMx + x] = gm;
       s_g[(1 * kMy + y) * kMx + x] = gaa;
@@ -294,8 +301,32 @@ l1_dssim_bwd_kernel(const float* __restrict__ img, const float* __restrict__ tgt
       const float a = s_a[(y + kHalo) * kBx + x + kHalo], bb = s_b[(y + kHalo) * kBx + x + kHalo];
       const float d_ssim = g[0] + 2.0f * a * g[1] + bb * g[2];
       go[(static_cast<int64_t>(gy) * W + gx) * 3 + c] = s_ssim * d_ssim + s_l1 * sgn(a - bb);
+      if (FUSED) l1 += fabsf(a - bb);
     }
     __syncthreads();
+  }
+  if constexpr (FUSED) {
+    __shared__ double s_red[2][kSsimThreads / 32];
+    double ds = ssum, dl = l1;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      ds += __shfl_xor_sync(0xffffffffu, ds, off);
+      dl += __shfl_xor_sync(0xffffffffu, dl, off);
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) {
+      s_red[0][warp] = ds;
+      s_red[1][warp] = dl;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double sa = 0.0, sl = 0.0;
+      for (int w = 0; w < kSsimThreads / 32; ++w) {
+        sa += s_red[0][w];
+        sl += s_red[1][w];
+      }
+      partials[blockIdx.y * gridDim.x + blockIdx.x] = make_double2(sa, sl);
+    }
   }
 }
 
@@ -315,6 +346,16 @@ int64_t l1_dssim_partials(int32_t B, int32_t H, int32_t W) {
   return tiles * B;
 }
 
+// partials of the fused pass: one per input tile and image
+static int64_t l1_dssim_grad_partials(int32_t B, int32_t H, int32_t W) {
+  return static_cast<int64_t>((W + kTileX - 1) / kTileX) * ((H + kTileY - 1) / kTileY) * B;
+}
+
+int64_t l1_dssim_partials_max(int32_t B, int32_t H, int32_t W) {
+  const int64_t a = l1_dssim_partials(B, H, W), b = l1_dssim_grad_partials(B, H, W);
+  return a > b ? a : b;
+}
+
 void launch_l1_dssim(const float* img, const float* tgt, int32_t B, int32_t H, int32_t W,
                      double l1_scale, double ssim_scale, double ssim_const, double2* partials,
                      float* loss, cudaStream_t stream) {
@@ -331,14 +372,32 @@ void launch_l1_dssim_bwd(const float* img, const float* tgt, int32_t B, int32_t 
                          cudaStream_t stream) {
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(l1_dssim_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(l1_dssim_bwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(kBwdSmem));
     attr = true;
   }
   const int tiles_x = (W + kTileX - 1) / kTileX, tiles_y = (H + kTileY - 1) / kTileY;
   dim3 grid(tiles_x * tiles_y, B);
-  l1_dssim_bwd_kernel<<<grid, kSsimThreads, kBwdSmem, stream>>>(img, tgt, H, W, tiles_x, l1_scale,
-                                                                ssim_grad_scale, v_loss, grad);
+  l1_dssim_bwd_kernel<false><<<grid, kSsimThreads, kBwdSmem, stream>>>(
+      img, tgt, H, W, tiles_x, l1_scale, ssim_grad_scale, v_loss, grad, nullptr);
+}
+
+void launch_l1_dssim_and_grad(const float* img, const float* tgt, int32_t B, int32_t H,
+                              int32_t W, double l1_scale, double ssim_scale, double ssim_const,
+                              float l1_grad_scale, float ssim_grad_scale, double2* partials,
+                              float* loss, float* grad, cudaStream_t stream) {
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(l1_dssim_bwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(kBwdSmem));
+    attr = true;
+  }
+  const int tiles_x = (W + kTileX - 1) / kTileX, tiles_y = (H + kTileY - 1) / kTileY;
+  dim3 grid(tiles_x * tiles_y, B);
+  l1_dssim_bwd_kernel<true><<<grid, kSsimThreads, kBwdSmem, stream>>>(
+      img, tgt, H, W, tiles_x, l1_grad_scale, ssim_grad_scale, nullptr, grad, partials);
+  l1_dssim_finalize_kernel<<<1, 256, 0, stream>>>(partials, l1_dssim_grad_partials(B, H, W),
+                                                  l1_scale, ssim_scale, ssim_const, loss);
 }
 
 }  // namespace splax

@@ -56,6 +56,35 @@ def test_l1_dssim_matches_oracle(B, H, W):
 
 
 @pytest.mark.gpu
+def test_l1_dssim_fused_pass_equals_separate_passes():
+    """The one-pass loss-and-gradient (taken when the image requires grad) agrees with the
+    separate loss and gradient entry points."""
+    import ctypes
+
+    import splax_b200 as sx
+    from splax_b200 import _lib
+    rng = np.random.default_rng(5)
+    a = rng.uniform(size=(2, 61, 83, 3)).astype(np.float32)
+    b = np.clip(a + rng.normal(0, 0.1, size=a.shape), 0, 1).astype(np.float32)
+    img = torch.tensor(a, device="cuda", requires_grad=True)
+    tgt = torch.tensor(b, device="cuda")
+    loss_f = sx.l1_dssim_loss(img, tgt)
+    (2.5 * loss_f).backward()
+    with torch.no_grad():
+        loss_s = sx.l1_dssim_loss(img, tgt)
+    assert abs(loss_f.item() - loss_s.item()) <= 1e-6 * abs(loss_s.item())
+    x = img.detach().contiguous()
+    g = torch.empty_like(x)
+    v = torch.tensor(2.5, device="cuda")
+    lib = _lib.load()
+    _lib.check(lib.splax_l1_dssim_loss_bwd(_lib.ptr(x), _lib.ptr(tgt), 2, 61, 83, 2,
+                                           ctypes.c_float(0.2), _lib.ptr(v), _lib.ptr(g),
+                                           _lib.stream_of(x)))
+    rel = (img.grad - g).norm() / g.norm()
+    assert rel.item() <= 1e-6, rel.item()
+
+
+@pytest.mark.gpu
 def test_l1_dssim_shares_add_up_and_single_view():
     import splax_b200 as sx
     rng = np.random.default_rng(9)
