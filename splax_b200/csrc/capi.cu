@@ -17,6 +17,16 @@
 #include "common.cuh"
 #include "kernels.h"
 
+#include <nvtx3/nvToolsExt.h>
+
+// One NVTX range per C entry point (a no-op unless a profiler is attached), so a timeline shows
+// the reference's FFI targets around their kernels.
+struct NvtxScope {
+  explicit NvtxScope(const char* name) { nvtxRangePushA(name); }
+  ~NvtxScope() { nvtxRangePop(); }
+};
+#define SPLAX_NVTX(name) NvtxScope splax_nvtx_scope_(name)
+
 namespace splax {
 namespace {
 
@@ -851,6 +861,7 @@ int splax_project(const float* means3d, int64_t means3d_rows, const float* scale
                   float fx, float fy, float cx, float cy, float glob_scale, float clip_thresh,
                   int64_t total, float* xys, float* depths, int32_t* radii, float* conics,
                   int32_t* num_tiles_hit, int32_t* cum_tiles_hit, void* stream) {
+  SPLAX_NVTX("splax_project");
   return project_impl(means3d, means3d_rows, scales, scales_rows, quats_xyzw, quats_rows,
                       viewmat, viewmat_rows, opacities, opacities_rows, gaussian_transforms,
                       transforms_rows, transform_ids, num_gaussians, num_transforms,
@@ -870,6 +881,7 @@ int splax_project_ex(const float* means3d, int64_t means3d_rows, const float* sc
                      float* depths, int32_t* radii, float* conics, int32_t* num_tiles_hit,
                      int32_t* cum_tiles_hit, int32_t quats_wxyz, float aa_eps, float aa_eps2,
                      float* rho, void* stream) {
+  SPLAX_NVTX("splax_project_ex");
   return project_impl(means3d, means3d_rows, scales, scales_rows, quats, quats_rows, viewmat,
                       viewmat_rows, opacities, opacities_rows, gaussian_transforms,
                       transforms_rows, transform_ids, num_gaussians, num_transforms,
@@ -974,6 +986,7 @@ int splax_project_bwd(const float* means3d, int64_t means3d_rows, const float* s
                       int32_t has_transforms, float fx, float fy, float glob_scale,
                       int64_t out_rows, float* v_mean3d, float* v_scale, float* v_quat,
                       float* v_viewmat, float* v_transforms, void* stream) {
+  SPLAX_NVTX("splax_project_bwd");
   return project_bwd_impl(means3d, means3d_rows, scales, scales_rows, quats_xyzw, quats_rows,
                           viewmat, viewmat_rows, radii, radii_rows, conics, conics_rows, v_xy,
                           v_xy_rows, v_depth, v_depth_rows, v_conic, v_conic_rows, nullptr, 0,
@@ -996,6 +1009,7 @@ int splax_project_bwd_ex(const float* means3d, int64_t means3d_rows, const float
                          float glob_scale, int64_t out_rows, int32_t quats_wxyz,
                          int32_t fold_batch, float* v_mean3d, float* v_scale, float* v_quat,
                          float* v_viewmat, float* v_transforms, void* stream) {
+  SPLAX_NVTX("splax_project_bwd_ex");
   return project_bwd_impl(means3d, means3d_rows, scales, scales_rows, quats, quats_rows,
                           viewmat, viewmat_rows, radii, radii_rows, conics, conics_rows, v_xy,
                           v_xy_rows, v_depth, v_depth_rows, v_conic, v_conic_rows, v_rho,
@@ -1012,6 +1026,7 @@ int splax_rasterize(const float* colors, int64_t colors_rows, const float* opaci
                     const int32_t* cum_tiles_hit, int64_t geom_rows, int32_t num_gaussians,
                     int32_t img_h, int32_t img_w, int64_t out_rows, int32_t key_bits,
                     float* final_Ts, int32_t* final_idx, float* out_img, void* stream) {
+  SPLAX_NVTX("splax_rasterize");
   return rasterize_common(colors, colors_rows, opacities, opacities_rows, map_opacities,
                           map_opacities_rows, background, background_rows, xys, depths, radii,
                           conics, cum_tiles_hit, geom_rows, num_gaussians, img_h, img_w, out_rows,
@@ -1027,6 +1042,7 @@ int splax_rasterize_depth(const float* colors, int64_t colors_rows, const float*
                           int64_t geom_rows, int32_t num_gaussians, int32_t img_h, int32_t img_w,
                           int64_t out_rows, int32_t key_bits, float* final_Ts, int32_t* final_idx,
                           float* out_img, float* out_depth, void* stream) {
+  SPLAX_NVTX("splax_rasterize_depth");
   if (!out_depth) return fail(SPLAX_ERR_INVALID_ARGUMENT, "rasterize_depth: out_depth is NULL");
   return rasterize_common(colors, colors_rows, opacities, opacities_rows, map_opacities,
                           map_opacities_rows, background, background_rows, xys, depths, radii,
@@ -1045,6 +1061,7 @@ int splax_rasterize_bwd(const float* colors, int64_t colors_rows, const float* o
                         int32_t img_h, int32_t img_w, int64_t grad_rows, int32_t key_bits,
                         float* v_colors, float* v_opacity, float* v_xy, float* v_conic,
                         void* stream) {
+  SPLAX_NVTX("splax_rasterize_bwd");
   return rasterize_bwd_common(colors, colors_rows, opacities, opacities_rows, map_opacities,
                               map_opacities_rows, background, background_rows, xys, depths,
                               radii, conics, cum_tiles_hit, geom_rows, final_Ts, final_idx,
@@ -1066,6 +1083,7 @@ int splax_rasterize_bwd_depth(const float* colors, int64_t colors_rows, const fl
                               int64_t grad_rows, int32_t key_bits, float* v_colors,
                               float* v_opacity, float* v_xy, float* v_conic, float* v_depths,
                               void* stream) {
+  SPLAX_NVTX("splax_rasterize_bwd_depth");
   if (!v_out_depth || !v_depths)
     return fail(SPLAX_ERR_INVALID_ARGUMENT, "rasterize_bwd_depth: depth buffers are NULL");
   return rasterize_bwd_common(colors, colors_rows, opacities, opacities_rows, map_opacities,
@@ -1089,6 +1107,7 @@ int splax_rasterize_bwd_ex(const float* colors, int64_t colors_rows, const float
                            int32_t fold_colors, int32_t fold_opacity, float* v_colors,
                            float* v_opacity, float* v_xy, float* v_conic, float* v_depths,
                            void* stream) {
+  SPLAX_NVTX("splax_rasterize_bwd_ex");
   if ((v_out_depth == nullptr) != (v_depths == nullptr))
     return fail(SPLAX_ERR_INVALID_ARGUMENT,
                 "rasterize_bwd_ex: v_out_depth and v_depths must be given together");
@@ -1108,6 +1127,7 @@ int splax_sort_and_bin(const float* xys, const float* depths, const int32_t* rad
                        int32_t key_bits, int32_t* gaussian_ids, int64_t gaussian_ids_cap,
                        int64_t* sorted_keys, int32_t* tile_bins, int64_t* num_intersects,
                        int32_t* used_key_bits, void* stream_) {
+  SPLAX_NVTX("splax_sort_and_bin");
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   if (num_gaussians <= 0 || num_images <= 0 || img_h <= 0 || img_w <= 0)
     return fail(SPLAX_ERR_INVALID_ARGUMENT, "sort_and_bin: invalid sizes");
@@ -1156,6 +1176,7 @@ int splax_sort_and_bin(const float* xys, const float* depths, const int32_t* rad
 
 int splax_mse_loss(const float* img, const float* target, int64_t count, float denom,
                    float* loss, void* stream_) {
+  SPLAX_NVTX("splax_mse_loss");
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   if (count < 0 || !(denom > 0.0f) || loss == nullptr ||
       (count > 0 && (img == nullptr || target == nullptr)))
@@ -1182,6 +1203,7 @@ int splax_mse_loss(const float* img, const float* target, int64_t count, float d
 
 int splax_mse_loss_bwd(const float* img, const float* target, int64_t count, float denom,
                        const float* v_loss, float* grad, void* stream_) {
+  SPLAX_NVTX("splax_mse_loss_bwd");
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   if (count < 0 || !(denom > 0.0f) || v_loss == nullptr ||
       (count > 0 && (img == nullptr || target == nullptr || grad == nullptr)))
@@ -1222,6 +1244,7 @@ static int l1_dssim_check(const float* img, const float* target, int32_t B, int3
 
 int splax_l1_dssim_loss(const float* img, const float* target, int32_t B, int32_t H, int32_t W,
                         int32_t views_total, float ssim_lambda, float* loss, void* stream_) {
+  SPLAX_NVTX("splax_l1_dssim_loss");
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   int rc = l1_dssim_check(img, target, B, H, W, views_total, ssim_lambda, "l1_dssim_loss");
   if (rc) return rc;
@@ -1253,6 +1276,7 @@ int splax_l1_dssim_loss(const float* img, const float* target, int32_t B, int32_
 int splax_l1_dssim_loss_bwd(const float* img, const float* target, int32_t B, int32_t H,
                             int32_t W, int32_t views_total, float ssim_lambda,
                             const float* v_loss, float* grad, void* stream_) {
+  SPLAX_NVTX("splax_l1_dssim_loss_bwd");
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   int rc = l1_dssim_check(img, target, B, H, W, views_total, ssim_lambda, "l1_dssim_loss_bwd");
   if (rc) return rc;
@@ -1283,6 +1307,7 @@ int splax_l1_dssim_loss_bwd(const float* img, const float* target, int32_t B, in
 int splax_l1_dssim_loss_and_grad(const float* img, const float* target, int32_t B, int32_t H,
                                  int32_t W, int32_t views_total, float ssim_lambda, float* loss,
                                  float* grad, void* stream_) {
+  SPLAX_NVTX("splax_l1_dssim_loss_and_grad");
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   int rc = l1_dssim_check(img, target, B, H, W, views_total, ssim_lambda,
                           "l1_dssim_loss_and_grad");
@@ -1318,6 +1343,7 @@ int splax_adam_step(int32_t num_arrays, float* const* params, const float* const
                     float* const* exp_avg, float* const* exp_avg_sq, const int64_t* sizes,
                     const float* lrs, int32_t step, float b1, float b2, float eps,
                     void* stream_) {
+  SPLAX_NVTX("splax_adam_step");
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   if (num_arrays < 0 || step < 1 || (num_arrays > 0 && (params == nullptr || grads == nullptr ||
                                                         exp_avg == nullptr ||
@@ -1354,6 +1380,7 @@ int splax_adam_step(int32_t num_arrays, float* const* params, const float* const
 int splax_nvls_allreduce_f32(float* multicast, void* const* flag_ptrs, int32_t rank,
                              int32_t world, int64_t n, uint64_t epoch, uint32_t* err,
                              void* stream_) {
+  SPLAX_NVTX("splax_nvls_allreduce_f32");
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   if (multicast == nullptr || flag_ptrs == nullptr || err == nullptr || world < 1 ||
       world > 8 || rank < 0 || rank >= world || n < 0 || epoch == 0 ||
@@ -1396,6 +1423,7 @@ int splax_ply_info(const char* path, int64_t* num_vertices) {
 
 int splax_ply_load(const char* path, int64_t num_vertices, float* means, float* scales,
                    float* quats, float* colors, float* opacities, void* stream_) {
+  SPLAX_NVTX("splax_ply_load");
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   if (path == nullptr || num_vertices < 0 ||
       (num_vertices > 0 && (!means || !scales || !quats || !colors || !opacities)))
