@@ -20,6 +20,10 @@
 namespace splax {
 namespace {
 
+// the record loop unrolled by two: one record's reduction overlaps the next one's pixel math
+// (3.60 -> 3.46 ms; by three 3.51, by four 3.79)
+constexpr int kBwdUnroll = 2;
+
 constexpr float kLn2 = 0.693147180559945f;
 
 // Two vertically adjacent pixels of one thread, advanced in lock-step with packed fp32x2 math.
@@ -217,6 +221,7 @@ raster_bwd_kernel(RasterBwdArgs a) {
     const int32_t batch_size = min(kBlockSize, batch_end - range_start + 1);
     // entries above every pixel of the tile are skipped as a whole
     const int32_t t_begin = max(0, batch_end - wmax);
+#pragma unroll kBwdUnroll
     for (int32_t t = t_begin; t < batch_size; ++t) {
       const int32_t idx = batch_end - t;
       const float4 r0 = s_r0[t];

@@ -4,13 +4,13 @@
 // One 64-thread CTA per (image, 16x16 tile); each warp owns a 16x8 block of the tile and each
 // thread four vertically adjacent pixels, so every shared-memory record read and the x-terms of
 // the Gaussian exponent serve four evaluations; the exponents are computed as two pairs with
-// packed fp32x2 instructions, the blend step per pixel (branches skip finished pixels). The tile's sorted list is walked in batches of
-// 256: the CTA
-// gathers the packed 48-byte records (three 16-byte loads each, written by the emission pass)
-// into shared memory, then blends the batch front to back from shared memory with broadcast
-// reads. Records carry the conic pre-scaled by -log2(e)/2, so the exponent is a quadratic form
-// evaluated with FMAs and one ex2. A block vote (__syncthreads_count) ends the walk once every
-// pixel has saturated.
+// packed fp32x2 instructions, the blend step per pixel with one branch for "skip" (a finished
+// pixel, or the reference's sigma / alpha tests) and one for termination. The tile's sorted list
+// is walked in batches of 256: the CTA gathers the packed 48-byte records (three 16-byte loads
+// each, written by the emission pass) into shared memory, then blends the batch front to back
+// from shared memory with broadcast reads, two records per loop trip. Records carry the conic
+// pre-scaled by -log2(e)/2, so the exponent is a quadratic form evaluated with FMAs and one ex2.
+// A block vote (__syncthreads_count) ends the walk once every pixel has saturated.
 //
 // Pixel semantics are the reference's: a gaussian is skipped when sigma < 0 (exponent > 0) or
 // alpha < 1/255, and the walk stops before the gaussian that would take T to <= 1e-4.
@@ -19,6 +19,9 @@
 
 namespace splax {
 namespace {
+// the record loop unrolled by two: the next record's exponents overlap this one's blend
+// (1.84 -> 1.76 ms; by four: 1.79)
+constexpr int kFwdUnroll = 2;
 
 
 struct PixelState {
@@ -33,10 +36,10 @@ __device__ __forceinline__ void blend_one(PixelState& s, float p, float opac, fl
                                           float b, float depth, int32_t idx,
                                           unsigned long long& evals,
                                           unsigned long long& contribs) {
-  if (s.done) return;
-  if constexpr (COUNT) ++evals;
+  // the skip tests of a done pixel and of the reference's sigma / alpha tests share one branch
+  if constexpr (COUNT) evals += s.done ? 0 : 1;
   const float alpha = fminf(kAlphaMax, opac * ex2_approx(p));
-  if (p > 0.0f || alpha < kAlphaThreshold) return;
+  if (s.done || p > 0.0f || alpha < kAlphaThreshold) return;
   const float next_T = s.T * (1.0f - alpha);
   if (next_T <= kTransmittanceMin) {
     s.done = true;
@@ -110,6 +113,7 @@ raster_fwd_kernel(RasterFwdArgs a) {
     __syncthreads();
     const int32_t batch_size = min(kBlockSize, range_end - batch_start);
     if (!all_done) {
+#pragma unroll kFwdUnroll
       for (int32_t t = 0; t < batch_size; ++t) {
         const float4 r0 = s_r0[t];  // x, y, qa, qb  (q = -log2(e)/2 * (a, 2b, c))
         const float4 r1 = s_r1[t];  // qc, opacity, r, g
