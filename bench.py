@@ -398,8 +398,9 @@ def main() -> None:
     denom = float(B * H * W * 3)
     reducer = None if opts.get("forward_only") else make_reducer(args, params, dev, world)
 
-    def step(vm, tgt, ps=params):
-        """One step; returns the rendered images (forward only) or the loss."""
+    def step(vm, tgt, ps=params, tgt_ready=None):
+        """One step; returns the rendered images (forward only) or the loss. tgt_ready: an
+        event the loss waits for (the targets' copy may overlap the forward render)."""
         if opts.get("forward_only"):
             with torch.no_grad():
                 imgs, _ = sx.render(*ps, viewmat=vm, **kw)
@@ -409,6 +410,8 @@ def main() -> None:
         if vm.requires_grad:
             vm.grad = None
         imgs, _ = sx.render(*ps, viewmat=vm, **kw)
+        if tgt_ready is not None:
+            torch.cuda.current_stream(dev).wait_event(tgt_ready)
         loss = sx.mse_loss(imgs, tgt, denom=denom)
         loss.backward()
         if world > 1:  # the gradients of the shared gaussians (and the loss) summed over ranks
@@ -483,8 +486,8 @@ def main() -> None:
     # reads its result back: the loss, or for a forward-only step the rendered images. The
     # gaussians are the model: like a training loop, the step keeps them resident on the device.
     # A copy stream fills one of two device slots with step k+1's batch while step k computes
-    # (a prefetching data loader) and drains the images of forward-only steps; every copy is
-    # inside the timed region.
+    # (a prefetching data loader; a step's loss waits for its targets, its render only for its
+    # cameras) and drains the images of forward-only steps; every copy is inside the timed region.
     e2e = None
     if not args.no_e2e:
         fwd_only = bool(opts.get("forward_only"))
@@ -499,7 +502,8 @@ def main() -> None:
         d2h = per * H * W * 3 * 4 if fwd_only else 4
         compute = torch.cuda.current_stream(dev)
         copier = torch.cuda.Stream(dev)
-        copied = [torch.cuda.Event() for _ in range(2)]
+        copied = [torch.cuda.Event() for _ in range(2)]      # cameras on the device
+        copied_tgt = [torch.cuda.Event() for _ in range(2)]  # targets on the device
         released = [torch.cuda.Event() for _ in range(2)]
 
         def load(k):
@@ -507,14 +511,17 @@ def main() -> None:
             with torch.cuda.stream(copier), torch.no_grad():
                 copier.wait_event(released[s])
                 slots[s][0].copy_(v_host, non_blocking=True)
+                copied[s].record(copier)
                 if not fwd_only:
                     slots[s][1].copy_(t_host, non_blocking=True)
-                copied[s].record(copier)
+                copied_tgt[s].record(copier)
 
         def run(k):
+            # the render waits for the cameras only; the loss waits for the targets, whose copy
+            # overlaps the forward of the same step
             s = k % 2
             compute.wait_event(copied[s])
-            out = step(slots[s][0], slots[s][1])
+            out = step(slots[s][0], slots[s][1], tgt_ready=copied_tgt[s])
             if fwd_only:
                 rendered = torch.cuda.Event()
                 rendered.record(compute)
