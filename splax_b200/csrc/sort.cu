@@ -41,12 +41,17 @@ depth_minmax_kernel(const float* __restrict__ depths, const int32_t* __restrict_
   const int64_t base = static_cast<int64_t>(blockIdx.x) * kMmThreads * kMmItems;
   int64_t img_cur = -1;
   int32_t lo = 0x7fffffff, hi = static_cast<int32_t>(0x80000000u);
+  // image of each index without a 64-bit division per item: one division, then boundaries
+  int64_t im = (base + threadIdx.x) / n, im_end = (im + 1) * n;
 #pragma unroll 4
   for (int k = 0; k < kMmItems; ++k) {
     const int64_t idx = base + k * kMmThreads + threadIdx.x;
     if (idx >= total) break;
+    while (idx >= im_end) {
+      ++im;
+      im_end += n;
+    }
     if (radii[idx] <= 0) continue;
-    const int64_t im = idx / n;
     const int32_t d = float_to_ordered(depths[idx]);
     if (im != img_cur) {
       if (img_cur >= 0) {
@@ -180,7 +185,7 @@ __global__ void __launch_bounds__(kPrepThreads) pair_prep_kernel(PairKeyArgs a, 
 // Exclusive scan of the tile counts in sorted pair order, one pass with a decoupled look-back
 // (bounded spin).
 constexpr int kScanThreads = 256;
-constexpr int kScanItems = 8;
+constexpr int kScanItems = 8;  // the 16-byte loads and stores below assume 8
 
 __global__ void __launch_bounds__(kScanThreads)
 sorted_offsets_kernel(const int32_t* __restrict__ perm, const int32_t* __restrict__ counts,
@@ -197,11 +202,20 @@ sorted_offsets_kernel(const int32_t* __restrict__ perm, const int32_t* __restric
   const int64_t base = tile * kScanThreads * kScanItems + static_cast<int64_t>(threadIdx.x) * kScanItems;
   long long c[kScanItems];
   long long tsum = 0;
+  const bool full = base + kScanItems <= total;  // whole run: two 16-byte loads of perm
+  int32_t pm[kScanItems];
+  if (full) {
+    const int4 p0 = *reinterpret_cast<const int4*>(perm + base);
+    const int4 p1 = *reinterpret_cast<const int4*>(perm + base + 4);
+    pm[0] = p0.x; pm[1] = p0.y; pm[2] = p0.z; pm[3] = p0.w;
+    pm[4] = p1.x; pm[5] = p1.y; pm[6] = p1.z; pm[7] = p1.w;
+  } else {
+#pragma unroll
+    for (int k = 0; k < kScanItems; ++k) pm[k] = base + k < total ? perm[base + k] : -1;
+  }
 #pragma unroll
   for (int k = 0; k < kScanItems; ++k) {
-    const int64_t i = base + k;
-    long long v = 0;
-    if (i < total) v = counts[perm[i]];
+    const long long v = pm[k] >= 0 ? counts[pm[k]] : 0;
     c[k] = v;
     tsum += v;
   }
@@ -232,11 +246,19 @@ sorted_offsets_kernel(const int32_t* __restrict__ perm, const int32_t* __restric
   }
   __syncthreads();
   long long run = s_prefix + wpre + inc - tsum;
+  int32_t o[kScanItems];
 #pragma unroll
   for (int k = 0; k < kScanItems; ++k) {
-    const int64_t i = base + k;
-    if (i < total) offsets[i] = static_cast<int32_t>(run);
+    o[k] = static_cast<int32_t>(run);
     run += c[k];
+  }
+  if (full) {
+    *reinterpret_cast<int4*>(offsets + base) = make_int4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<int4*>(offsets + base + 4) = make_int4(o[4], o[5], o[6], o[7]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < kScanItems; ++k)
+      if (base + k < total) offsets[base + k] = o[k];
   }
 }
 
