@@ -485,24 +485,25 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
   constexpr int D = 1 << RB;
   static_assert(NT >= D, "one thread per digit");
   __shared__ uint32_t s_wh[kSortWarps][D];
-  // 8-bit digits find a digit's lanes through a shared word per digit (atomicOr of the lane bits:
-  // a quarter of the instructions of the per-bit ballots; sort 1.07 -> 0.97 ms per step); 9-bit
-  // digits keep the ballots, as a second 32 KB table would cost a CTA per SM
-  constexpr bool kOrMatch = RB == 8;
-  __shared__ uint32_t s_match[kOrMatch ? kSortWarps : 1][kOrMatch ? D : 1];
+  // a digit's lanes are found through a shared word per (warp, digit): atomicOr of the lane bits,
+  // a quarter of the instructions of one ballot per digit bit (sort 1.07 -> 0.97 ms per step).
+  // The words live in the dynamic buffer, which the ranking does not otherwise use (the staged
+  // keys and values are written after it).
+  static_assert(kSortWarps * D * sizeof(uint32_t) <= TILE * (sizeof(K) + sizeof(int32_t)),
+                "the digit words fit in the staging buffer");
   __shared__ uint32_t s_bx[D];
   __shared__ long long s_gb[D];
   __shared__ uint32_t s_warp[kSortWarps];
   __shared__ int s_tile;
   __shared__ int s_tile_keys;
   extern __shared__ __align__(16) unsigned char s_raw[];
+  uint32_t* s_match = reinterpret_cast<uint32_t*>(s_raw);  // [kSortWarps][D], ranking only
   K* s_keys = reinterpret_cast<K*>(s_raw);
   int32_t* s_vals = reinterpret_cast<int32_t*>(s_raw + TILE * sizeof(K));
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int i = tid; i < kSortWarps * D; i += NT) (&s_wh[0][0])[i] = 0;
-  if constexpr (kOrMatch)
-    for (int i = tid; i < kSortWarps * D; i += NT) (&s_match[0][0])[i] = 0;
+  for (int i = tid; i < kSortWarps * D; i += NT) s_match[i] = 0;
   if (tid == 0) s_tile = atomicAdd(tile_counter, 1);
   __syncthreads();
   const int64_t tile = s_tile;
@@ -535,25 +536,15 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
     const uint32_t d = static_cast<uint32_t>(static_cast<uint64_t>(k[it]) >> shift) & (D - 1);
     // lanes holding the same digit: intersect one ballot per digit bit (cheaper than a
     // match instruction over up to 32 distinct digits); invalid lanes match nobody
-    unsigned peers;
-    if constexpr (kOrMatch) {
-      // lanes holding the same digit: each ORs its bit into the digit's word, reads the word
-      // back, and the group's lowest lane clears it for the next item
-      if (valid) atomicOr(&s_match[warp][d], 1u << lane);
-      __syncwarp();
-      peers = valid ? s_match[warp][d] : (1u << lane);
-      __syncwarp();
-      if (valid && (peers & lt_mask) == 0) s_match[warp][d] = 0;
-      __syncwarp();
-    } else {
-      peers = __ballot_sync(0xffffffffu, valid);
-#pragma unroll
-      for (int bit = 0; bit < RB; ++bit) {
-        const unsigned b = __ballot_sync(0xffffffffu, (d >> bit) & 1u);
-        peers &= ((d >> bit) & 1u) ? b : ~b;
-      }
-      if (!valid) peers = 1u << lane;
-    }
+    // lanes holding the same digit: each ORs its bit into the digit's word, reads the word
+    // back, and the group's lowest lane clears it for the next item
+    uint32_t* word = s_match + warp * D + d;
+    if (valid) atomicOr(word, 1u << lane);
+    __syncwarp();
+    const unsigned peers = valid ? *word : (1u << lane);
+    __syncwarp();
+    if (valid && (peers & lt_mask) == 0) *word = 0;
+    __syncwarp();
     const int leader = __ffs(peers) - 1;
     uint32_t prev = 0;
     if (valid && lane == leader) prev = atomicAdd(&s_wh[warp][d], __popc(peers));
