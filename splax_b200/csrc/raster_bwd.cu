@@ -54,11 +54,13 @@ __device__ __forceinline__ bool vjp_pair(BwdPair& s, int32_t idx, float2 p, floa
                                          BwdAcc& acc, unsigned long long& contribs) {
   const float2 vis = make_float2(ex2_approx(p.x), ex2_approx(p.y));
   const float2 ov = mul2(opac, vis);
-  const float a0 = fminf(kAlphaMax, ov.x), a1 = fminf(kAlphaMax, ov.y);
-  const bool v0 = idx <= s.bf0 && !(p.x > 0.0f) && !(a0 < kAlphaThreshold);
-  const bool v1 = idx <= s.bf1 && !(p.y > 0.0f) && !(a1 < kAlphaThreshold);
+  // alpha = min(0.999, ov) < 1/255 exactly when ov < 1/255
+  const bool v0 = idx <= s.bf0 && !(p.x > 0.0f) && !(ov.x < kAlphaThreshold);
+  const bool v1 = idx <= s.bf1 && !(p.y > 0.0f) && !(ov.y < kAlphaThreshold);
   if constexpr (COUNT) contribs += static_cast<unsigned>(v0) + static_cast<unsigned>(v1);
-  const float2 am = make_float2(v0 ? a0 : 0.0f, v1 ? a1 : 0.0f);
+  // ov of the pixels that take part (0 elsewhere): alpha and the unclamped mask follow from it
+  const float2 ovv = make_float2(v0 ? ov.x : 0.0f, v1 ? ov.y : 0.0f);
+  const float2 am = make_float2(fminf(kAlphaMax, ovv.x), fminf(kAlphaMax, ovv.y));
   const float2 om = one_minus2(am);
   const float2 ra = make_float2(__fdividef(1.0f, om.x), __fdividef(1.0f, om.y));
   // a pixel that does not take part has am = 0, om = 1 and ra = rcp.approx(1) = 1 exactly
@@ -79,8 +81,8 @@ __device__ __forceinline__ bool vjp_pair(BwdPair& s, int32_t idx, float2 p, floa
   const float2 va = fma2(s.T, cv, make_float2(-rb.x, -rb.y));
   s.behind = fma2(cv, fac, s.behind);
   // where the 0.999 clamp is active alpha is constant: no sigma or opacity cotangent
-  const float2 ovm = make_float2(v0 && ov.x <= kAlphaMax ? ov.x : 0.0f,
-                                 v1 && ov.y <= kAlphaMax ? ov.y : 0.0f);
+  const float2 ovm = make_float2(ovv.x <= kAlphaMax ? ovv.x : 0.0f,
+                                 ovv.y <= kAlphaMax ? ovv.y : 0.0f);
   const float2 w = mul2(ovm, va);
   acc.w = add2(acc.w, w);
   const float2 wy = mul2(w, dy);

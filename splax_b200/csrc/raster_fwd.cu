@@ -38,8 +38,10 @@ __device__ __forceinline__ void blend_one(PixelState& s, float p, float opac, fl
                                           unsigned long long& contribs) {
   // the skip tests of a done pixel and of the reference's sigma / alpha tests share one branch
   if constexpr (COUNT) evals += s.done ? 0 : 1;
-  const float alpha = fminf(kAlphaMax, opac * ex2_approx(p));
-  if (s.done || p > 0.0f || alpha < kAlphaThreshold) return;
+  const float ov = opac * ex2_approx(p);
+  // min(0.999, ov) < 1/255 exactly when ov < 1/255
+  if (s.done || p > 0.0f || ov < kAlphaThreshold) return;
+  const float alpha = fminf(kAlphaMax, ov);
   const float next_T = s.T * (1.0f - alpha);
   if (next_T <= kTransmittanceMin) {
     s.done = true;
