@@ -90,17 +90,56 @@ def load_peaks() -> tuple[dict, str]:
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling while the timed region runs."""
+    """SM clock and clock-event (throttle) reasons sampled while the timed region runs: NVML
+    read every 2 ms from a thread (read-only queries), else nvidia-smi every 200 ms."""
 
     FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, uuid: str | None):
         self.uuid = uuid
         self.proc = None
+        self.thread = None
+        self.samples: list[tuple[float, int]] = []
+        self.max_mhz = None
+
+    def _start_nvml(self) -> bool:
+        import threading
+
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = (pynvml.nvmlDeviceGetHandleByUUID(self.uuid) if self.uuid
+                 else pynvml.nvmlDeviceGetHandleByIndex(0))
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons",
+                              getattr(pynvml, "nvmlDeviceGetCurrentClocksThrottleReasons", None))
+            self.bits = (getattr(pynvml, "nvmlClocksEventReasonHwSlowdown", 0x8),
+                         getattr(pynvml, "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+                         getattr(pynvml, "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+                         getattr(pynvml, "nvmlClocksEventReasonSwPowerCap", 0x4))
+        except Exception:
+            return False
+        self.stop_flag = threading.Event()
+
+        def loop():
+            while not self.stop_flag.is_set():
+                try:
+                    self.samples.append((float(pynvml.nvmlDeviceGetClockInfo(
+                        h, pynvml.NVML_CLOCK_SM)), int(reasons(h)) if reasons else 0))
+                except Exception:
+                    pass
+                time.sleep(0.002)
+
+        self.thread = threading.Thread(target=loop, daemon=True)
+        self.thread.start()
+        return True
 
     def start(self) -> None:
+        if self._start_nvml():
+            return
         try:
             cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                    "-lms", "200"]
@@ -112,6 +151,16 @@ class ClockSampler:
             self.proc = None
 
     def stop(self) -> dict | None:
+        if self.thread is not None:
+            self.stop_flag.set()
+            self.thread.join(timeout=5)
+            if not self.samples:
+                return None
+            sm = [c for c, _ in self.samples]
+            reasons = sorted({n for _, r in self.samples for n, b in zip(self.NAMES, self.bits)
+                              if r & b})
+            return {"sm_mhz": statistics.median(sm), "sm_max_mhz": self.max_mhz,
+                    "reasons": reasons, "samples": len(sm), "source": "nvml, 2 ms"}
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -125,11 +174,11 @@ class ClockSampler:
             return None
         sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
         mx = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[k] for r in rows for k in range(4) if r[6 + k].strip() == "Active"})
+        reasons = sorted({self.NAMES[k] for r in rows for k in range(4)
+                          if r[6 + k].strip() == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(rows)}
+                "samples": len(rows), "source": "nvidia-smi, 200 ms"}
 
 
 def cpu_baseline(scene: dict, threads: int, forward_only: bool = False) -> dict:
@@ -299,7 +348,8 @@ def train_bench(args) -> None:
     _lib.profile_reset()
     if sampler:
         sampler.start()
-        time.sleep(0.3)
+        if sampler.thread is None:
+            time.sleep(0.3)  # nvidia-smi's first sample
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -434,7 +484,8 @@ def main() -> None:
     _lib.profile_reset()
     if sampler:
         sampler.start()
-        time.sleep(0.3)
+        if sampler.thread is None:
+            time.sleep(0.3)  # nvidia-smi's first sample
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
