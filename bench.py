@@ -34,7 +34,7 @@ sys.path.insert(0, str(ROOT))
 METRIC = "fwd+bwd frames/s (1M gaussians, 1080p, 8 cams) at 1/2/4/8 B200; % roofline"
 CONFIG = 2
 WORKLOAD = "config 2: 1M gaussians, 8 ring cams, 1080x1920, MSE fwd+bwd, grads of 5 param arrays"
-# the other fwd+bwd configurations of BASELINE (not the headline): metric, workload, options
+# the other fwd+bwd configurations of the benchmark (not the headline): metric, workload, options
 FWD_BWD = {
     0: ("config 0 forward frames/s (10k gaussians, 256x256, 1 cam)",
         "config 0: 10k gaussians, 1 cam, 256x256, white background, forward render only",
