@@ -65,6 +65,27 @@ def test_project_bit_exact(sx, oracle_lib, n, H, W, seed):
         assert np.array_equal(a, orc[k]), (name, int((a != orc[k]).sum()))
 
 
+def test_large_gaussians_count_and_emission_bit_exact(sx, oracle_lib):
+    """Gaussians spanning up to ~45 tile rows: the warp-cooperative walks (row chunks of 32 per
+    warp, several chunks per warp) reproduce the sequential walk's counts and tiles."""
+    n, H, W = 3000, 720, 1280
+    scene, cu, orc = _proj_both(sx, oracle_lib, n, H, W, 11, spread=1.0, smin=0.05, smax=0.6,
+                                omin=0.0, omax=1.0)
+    for k in range(6):
+        a = N(cu[k]).reshape(orc[k].shape)
+        assert np.array_equal(a, orc[k]), k
+    nth = N(cu[4]).reshape(-1)
+    assert nth.max() > 200  # large footprints are present
+    xys, d, r, cn, _, cum = cu
+    op = scene[4]
+    g_c, k_c, b_c, count, _ = _sort_cuda(sx, xys, d, r, cn, T(op), cum, n, 1, H, W, 0)
+    rc, g_o, k_o, b_o, _ = oracle_lib.sort_and_bin(*orc[:4], op, orc[5], n=n, B=1,
+                                                   img_shape=(H, W))
+    assert rc == 0 and count == len(g_o)
+    assert np.array_equal(g_c, g_o)
+    assert np.array_equal(b_c, b_o)
+
+
 def test_project_batched_bit_exact(sx, oracle_lib):
     views = np.stack([viewmat(0.0), viewmat(0.3), viewmat(-0.2, 0.1, 4.0)])
     (_, _, _, _, _, _, _, B), cu, orc = _proj_both(sx, oracle_lib, 8000, 128, 160, 4, views)
