@@ -91,7 +91,8 @@ def load_peaks() -> tuple[dict, str]:
 
 class ClockSampler:
     """SM clock and clock-event (throttle) reasons sampled while the timed region runs: NVML
-    read every 2 ms from a thread (read-only queries), else nvidia-smi every 200 ms."""
+    read every 20 ms from a thread (read-only queries; faster polling slowed the launch-bound
+    small configurations), else nvidia-smi every 200 ms."""
 
     FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -131,7 +132,7 @@ class ClockSampler:
                         h, pynvml.NVML_CLOCK_SM)), int(reasons(h)) if reasons else 0))
                 except Exception:
                     pass
-                time.sleep(0.002)
+                time.sleep(0.02)
 
         self.thread = threading.Thread(target=loop, daemon=True)
         self.thread.start()
@@ -160,7 +161,7 @@ class ClockSampler:
             reasons = sorted({n for _, r in self.samples for n, b in zip(self.NAMES, self.bits)
                               if r & b})
             return {"sm_mhz": statistics.median(sm), "sm_max_mhz": self.max_mhz,
-                    "reasons": reasons, "samples": len(sm), "source": "nvml, 2 ms"}
+                    "reasons": reasons, "samples": len(sm), "source": "nvml, 20 ms"}
         if self.proc is None:
             return None
         self.proc.terminate()
