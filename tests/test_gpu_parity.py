@@ -273,6 +273,35 @@ def test_key_width_fallback_and_overflow(sx):
     assert sx.scratch_info()["sig"] is None
 
 
+def test_all_culled_and_tiny_batches(sx, oracle_lib):
+    """No visible gaussian: the image is the background, the gradients are zero and no device
+    error is raised. Then 5 gaussians seen by 5 cameras at an odd size match the oracle."""
+    from splax_b200 import _lib
+
+    n, H, W = 64, 37, 53
+    m, s, q, c, op, bg = random_scene(n, 21)
+    m = m.copy()
+    m[:, 2] = -20.0  # behind every camera below
+    params = [T(x).requires_grad_() for x in (m, s, q, c, op)]
+    img, _ = sx.render(*params, viewmat=T(viewmat()), background=T(bg), **cam(H, W))
+    assert torch.equal(img, T(bg).expand(H, W, 3))
+    img.sum().backward()
+    for p in params:
+        assert p.grad is None or not bool(p.grad.any())
+    _lib.check(_lib.load().splax_check_device_errors(_lib.stream_of(img)))
+
+    n, B = 5, 5
+    views = np.stack([viewmat(0.1 * i, 0.05 * i, 3.0 + 0.2 * i) for i in range(B)])
+    (m, s, q, c, op, bg, views, B), cu, orc = _raster_inputs(sx, oracle_lib, n, H, W, 22, views)
+    xys, d, r, cn, nth, cum = cu
+    assert np.array_equal(N(nth).reshape(-1), orc[4])
+    img = sx.rasterize(T(c), T(op), T(bg), xys, d, r, cn, cum, img_shape=(H, W))
+    fT, fi, img_o, _, flags = oracle_lib.rasterize(c, op, op, bg, *orc[:4], orc[5], n=n, B=B,
+                                                   img_shape=(H, W))
+    _compare_images(N(img).reshape(B * H, W, 3), img_o.reshape(B * H, W, 3),
+                    flags.reshape(B * H, W))
+
+
 def test_scratch_reuse_across_sizes(sx):
     """A warm, differently sized scratch gives the same image as a cleared one
     (tests/test_warp_rasterize.py:211-228)."""
