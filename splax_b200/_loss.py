@@ -96,7 +96,7 @@ class _L1DssimFn(torch.autograd.Function):
         v = v_loss.detach().to(torch.float32).reshape(()).contiguous()
         if ctx.fused:
             (g,) = ctx.saved_tensors
-            return g.mul_(v).to(dtype), None, None, None
+            return (g * v).to(dtype), None, None, None  # out of place: backward may run twice
         a, t = ctx.saved_tensors
         g = torch.empty_like(a)
         lib = _lib.load()
