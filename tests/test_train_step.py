@@ -82,6 +82,13 @@ def test_l1_dssim_fused_pass_equals_separate_passes():
                                            _lib.stream_of(x)))
     rel = (img.grad - g).norm() / g.norm()
     assert rel.item() <= 1e-6, rel.item()
+    # a retained graph runs the backward twice: the gradient accumulates, unchanged per call
+    img.grad = None
+    loss2 = sx.l1_dssim_loss(img, tgt)
+    (2.5 * loss2).backward(retain_graph=True)
+    first = img.grad.clone()
+    (2.5 * loss2).backward()
+    assert torch.allclose(img.grad, 2.0 * first, rtol=1e-6, atol=0.0)
 
 
 @pytest.mark.gpu
