@@ -125,17 +125,23 @@ __device__ __forceinline__ void ellipse_init(float A, float B, float C, float t,
   s.valid = true;
 }
 
-// Cross-axis extent of the ellipse at one line of the outer axis (splax/_intersect.py:110-133)
-__device__ __forceinline__ void ellipse_intersect(const Ellipse& s, float coord, float& lo,
-                                                  float& hi) {
-  float pu = s.isY ? s.py : s.px;
-  float pv = s.isY ? s.px : s.py;
-  float coeff = s.isY ? s.A : s.C;
+// Cross-axis extent of the ellipse at one line of the outer axis (splax/_intersect.py:110-133):
+// the interval [lo, hi] on the line `coord`, from the ellipse fields (pu / pv: the centre along
+// the outer / cross axis, coeff: the outer axis' quadratic coefficient). The one definition the
+// sequential and the warp-cooperative walks share.
+__device__ __forceinline__ void walk_intersect(float B, float disc, float t, float coeff, float pu,
+                                               float pv, float coord, float& lo, float& hi) {
   float h = coord - pu;
-  float sq = sqrtf(s.disc * h * h + s.t * coeff);
-  float bh = (-s.B) * h;
+  float sq = sqrtf(disc * h * h + t * coeff);
+  float bh = (-B) * h;
   lo = (bh - sq) / coeff + pv;
   hi = (bh + sq) / coeff + pv;
+}
+
+__device__ __forceinline__ void ellipse_intersect(const Ellipse& s, float coord, float& lo,
+                                                  float& hi) {
+  walk_intersect(s.B, s.disc, s.t, s.isY ? s.A : s.C, s.isY ? s.py : s.px, s.isY ? s.px : s.py,
+                 coord, lo, hi);
 }
 
 // Leading line of the walk (splax/_intersect.py:136-143)
@@ -188,16 +194,6 @@ __device__ __forceinline__ int32_t ellipse_tile_count(const Ellipse& s) {
 // state is the next row's start state, taken from the next lane by shuffle when that lane holds
 // the same pair's next row. Every float operation is the sequential walk's (ellipse_column), so
 // [mn, mx) is bit-identical to it.
-
-// ellipse_intersect on the shared fields
-__device__ __forceinline__ void walk_intersect(float B, float disc, float t, float coeff, float pu,
-                                               float pv, float coord, float& lo, float& hi) {
-  float h = coord - pu;
-  float sq = sqrtf(disc * h * h + t * coeff);
-  float bh = (-B) * h;
-  lo = (bh - sq) / coeff + pv;
-  hi = (bh + sq) / coeff + pv;
-}
 
 // Largest lane whose (non-decreasing across lanes) v is <= key.
 __device__ __forceinline__ int lift_find(int v, int key) {
