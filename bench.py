@@ -316,12 +316,24 @@ def train_bench(args) -> None:
             "opac_logit": logit(scene["opacities"])}
     params = [torch.tensor(host[k].astype(np.float32), device=dev).requires_grad_()
               for k in TRAIN_LRS]
-    opt = sx.Adam(params, [lr * float(np.sqrt(B)) for lr in TRAIN_LRS.values()])
+    lrs = [lr * float(np.sqrt(B)) for lr in TRAIN_LRS.values()]
     views = torch.tensor(scene["viewmats"][cams], device=dev)
     target = torch.tensor(targets_np, device=dev)
     bg = torch.tensor(scene["background"], device=dev)
     kw = dict(background=bg, img_shape=(H, W), f=(f, f))
-    reducer = make_reducer(args, params, dev, world)
+    # with --collective nvls the exchange and the update fuse into one NVLS kernel (sharded
+    # moments); otherwise an all-reduce, then Adam on every rank
+    fused = None
+    if world > 1 and args.collective == "nvls":
+        from splax_b200._collective import NvlsAdam
+        try:
+            fused = NvlsAdam(params, lrs, dev)
+            params = fused.params
+        except RuntimeError:
+            if args.collective == "nvls":
+                raise
+    opt = None if fused is not None else sx.Adam(params, lrs)
+    reducer = None if fused is not None else make_reducer(args, params, dev, world)
 
     def step(vm, tgt):
         for p in params:
@@ -329,6 +341,10 @@ def train_bench(args) -> None:
         imgs, _ = sx.render_log(*params, viewmat=vm, **kw)
         loss = sx.l1_dssim_loss(imgs, tgt, ssim_lambda=SSIM_LAMBDA, views_total=B)
         loss.backward()
+        if fused is not None:
+            fused.step([p.grad for p in params])
+            dist.all_reduce(loss.detach())
+            return loss
         if world > 1:  # the shared gradients (and the loss) summed over the ranks
             loss = reduce_grads(reducer, params, loss, dev)
         opt.step([p.grad for p in params])
@@ -387,7 +403,8 @@ def train_bench(args) -> None:
                                    "per-group Adam", "gaussians": n, "cams_per_gpu": per,
                        "parallelism": f"camera-sharded dp{world}",
                        "collective": None if world == 1 else
-                       ("nvls (library kernel)" if reducer is not None else "nccl")},
+                       ("nvls exchange fused with Adam (library kernel)" if fused is not None
+                        else "nvls (library kernel)" if reducer is not None else "nccl")},
             "loss": loss_v,
             "kernels": {k: {**v, "share": v["ms"] / max(sum(total_ms.values()), 1e-9)}
                         for k, v in kern.items()},
@@ -398,6 +415,8 @@ def train_bench(args) -> None:
     if world > 1:
         if reducer is not None:
             reducer.close()
+        if fused is not None:
+            fused.close()
         dist.barrier()
         dist.destroy_process_group()
 

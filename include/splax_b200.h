@@ -298,6 +298,25 @@ int splax_nvls_allreduce_f32(float *multicast, void *const *flag_ptrs, int32_t r
                              int32_t world, int64_t n, uint64_t epoch, uint32_t *err,
                              void *stream);
 
+/* The training step's gradient exchange fused with its Adam update, for the same symmetric
+ * setup as splax_nvls_allreduce_f32: grad_mc and param_mc are the multicast addresses of two
+ * symmetric buffers of n floats (the gradients, and the parameters whose local copy is
+ * param_local), split into num_groups (1..8) consecutive parameter groups of group_sizes[k]
+ * elements and learning rate lrs[k] (host arrays). Each rank sums its shard of the gradients
+ * through the switch, applies Adam (splax_adam_step's update, step >= 1 after this update) with
+ * its shard of the moments, exp_avg / exp_avg_sq of splax_nvls_adam_shard_len floats (zero
+ * before the first step), and writes the updated parameters into every rank's copy; entry and
+ * exit barriers use epoch and epoch + 1 on flag_ptrs (one flag array, as above). No counterpart
+ * in the reference: it replaces the psum followed by optax.adam of a sharded training step. */
+int splax_nvls_adam_step(const float *grad_mc, float *param_mc, const float *param_local,
+                         float *exp_avg, float *exp_avg_sq, int64_t n, int32_t num_groups,
+                         const int64_t *group_sizes, const float *lrs, int32_t step, float b1,
+                         float b2, float eps, void *const *flag_ptrs, int32_t rank,
+                         int32_t world, uint64_t epoch, uint32_t *err, void *stream);
+
+/* Length (floats) of this rank's shard of the moments for splax_nvls_adam_step. */
+int splax_nvls_adam_shard_len(int64_t n, int32_t rank, int32_t world, int64_t *len);
+
 /* load_ply, splax/io.py:78-98, first half: parse a 3DGS .ply header and report its vertex
  * count (host only, no GPU work). Binary little-endian files whose first element is `vertex`
  * with scalar properties, the fields x y z scale_0..2 rot_0..3 f_dc_0..2 opacity in float32. */

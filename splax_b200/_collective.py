@@ -8,6 +8,11 @@ set up through torch.distributed's symmetric memory), and ``splax_nvls_allreduce
 the buffer in place: each rank reduces its shard with multimem.ld_reduce and multicasts the sums
 with multimem.st, between two cross-rank barriers. Every rank ends with identical sums.
 
+``NvlsAdam`` fuses that exchange with the training step's Adam update
+(``splax_nvls_adam_step``): each rank sums its shard of the gradients through the switch,
+updates that shard of the parameters with its shard of the moments and multicasts the new
+parameters into every rank's copy.
+
 One process per GPU; the group's ranks must share an NVSwitch fabric with multicast support.
 """
 
@@ -98,3 +103,82 @@ class GradAllReduce:
 
         torch.cuda.synchronize(self.buf.device)
         dist.barrier(self.group)
+
+
+class NvlsAdam:
+    """Adam for camera-sharded training with the gradient exchange fused into the update.
+
+    The parameters live in a symmetric buffer (``self.params`` are new leaf tensors viewing it:
+    train with those). ``step(grads)`` copies the gradients into a second symmetric buffer and
+    runs ``splax_nvls_adam_step``: each rank sums its 1/G shard of the gradients through the
+    switch, updates that shard with its 1/G of the moments (optax.adam's update, as ``Adam``),
+    and multicasts the new parameters into every rank's copy. The optimiser state is sharded over
+    the ranks; every rank ends the step with identical parameters.
+    """
+
+    def __init__(self, params: Sequence[torch.Tensor], lrs: Sequence[float] | float,
+                 device: torch.device, group=None, b1: float = 0.9, b2: float = 0.999,
+                 eps: float = 1e-8):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+
+        params = list(params)
+        if isinstance(lrs, (int, float)):
+            lrs = [float(lrs)] * len(params)
+        if not 1 <= len(params) <= 8 or len(lrs) != len(params):
+            raise ValueError("1 to 8 parameter tensors, one learning rate each")
+        self.grads = GradAllReduce([p.shape for p in params], device, group)
+        self.rank, self.world, self.group = self.grads.rank, self.grads.world, group
+        n = self.grads.n
+        self.n = n
+        self.pbuf = symm_mem.empty(-(-n // _ALIGN) * _ALIGN, dtype=torch.float32, device=device)
+        with torch.no_grad():
+            torch.cat([p.detach().reshape(-1).to(torch.float32) for p in params],
+                      out=self.pbuf[:n])
+        torch.cuda.synchronize(device)
+        name = group.group_name if group is not None else dist.group.WORLD.group_name
+        self.phdl = symm_mem.rendezvous(self.pbuf, name)
+        if not self.phdl.multicast_ptr:
+            raise RuntimeError("NVLS Adam: this fabric offers no multicast address")
+        off = self.pbuf.data_ptr() - self.phdl.buffer_ptrs[self.rank]
+        if off < 0 or off + 4 * self.pbuf.numel() > self.phdl.buffer_size:
+            raise RuntimeError("NVLS Adam: buffer outside its symmetric allocation")
+        self.pmc = self.phdl.multicast_ptr + off
+        self.params = []
+        o = 0
+        for p in params:
+            k = p.numel()
+            self.params.append(self.pbuf[o:o + k].view(p.shape).requires_grad_())
+            o += k
+        lib = _lib.load()
+        ln = ctypes.c_int64(0)
+        _lib.check(lib.splax_nvls_adam_shard_len(n, self.rank, self.world, ctypes.byref(ln)))
+        self.exp_avg = torch.zeros(max(ln.value, 4), dtype=torch.float32, device=device)
+        self.exp_avg_sq = torch.zeros_like(self.exp_avg)
+        self.sizes = (ctypes.c_int64 * len(params))(*[p.numel() for p in params])
+        self.lrs = (ctypes.c_float * len(params))(*[float(x) for x in lrs])
+        self.b1, self.b2, self.eps = float(b1), float(b2), float(eps)
+        self.count = 0
+        dist.barrier(group)
+
+    @torch.no_grad()
+    def step(self, grads: Sequence[torch.Tensor] | None = None) -> None:
+        if grads is None:
+            grads = [p.grad for p in self.params]
+        torch.cat([g.reshape(-1) for g in grads], out=self.grads.payload)
+        self.count += 1
+        g = self.grads
+        stream = torch.cuda.current_stream(self.pbuf.device).cuda_stream
+        _lib.check(_lib.load().splax_nvls_adam_step(
+            ctypes.c_void_p(g.mc), ctypes.c_void_p(self.pmc), ctypes.c_void_p(self.pbuf.data_ptr()),
+            ctypes.c_void_p(self.exp_avg.data_ptr()), ctypes.c_void_p(self.exp_avg_sq.data_ptr()),
+            self.n, len(self.params), self.sizes, self.lrs, self.count, self.b1, self.b2,
+            self.eps, g.flag_ptrs, self.rank, self.world, ctypes.c_uint64(g.epoch),
+            ctypes.c_void_p(g.err.data_ptr()), ctypes.c_void_p(stream)))
+        g.epoch += 2
+
+    def check(self) -> None:
+        self.grads.check()
+
+    def close(self) -> None:
+        self.grads.close()

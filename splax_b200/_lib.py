@@ -64,6 +64,9 @@ SIGNATURES: dict[str, list] = {
     "splax_l1_dssim_loss_and_grad": [P, P, I32, I32, I32, I32, F32, P, P, P],
     "splax_adam_step": [I32, P, P, P, P, P, P, I32, F32, F32, F32, P],
     "splax_nvls_allreduce_f32": [P, P, I32, I32, I64, ctypes.c_uint64, P, P],
+    "splax_nvls_adam_step": [P, P, P, P, P, I64, I32, P, P, I32, F32, F32, F32, P, I32, I32,
+                             ctypes.c_uint64, P, P],
+    "splax_nvls_adam_shard_len": [I64, I32, I32, P],
     "splax_ply_info": [ctypes.c_char_p, P],
     "splax_ply_load": [ctypes.c_char_p, I64, P, P, P, P, P, P],
     "splax_mse_loss_bwd": [P, P, I64, F32, P, P, P],

@@ -1406,6 +1406,63 @@ int splax_nvls_allreduce_f32(float* multicast, void* const* flag_ptrs, int32_t r
   return finish(*st, stream);
 }
 
+int splax_nvls_adam_shard_len(int64_t n, int32_t rank, int32_t world, int64_t* len) {
+  if (len == nullptr || n < 0 || world < 1 || world > 8 || rank < 0 || rank >= world)
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "nvls_adam_shard_len: invalid n, rank or world");
+  *len = nvls_adam_shard_len(n, rank, world);
+  return SPLAX_OK;
+}
+
+int splax_nvls_adam_step(const float* grad_mc, float* param_mc, const float* param_local,
+                         float* exp_avg, float* exp_avg_sq, int64_t n, int32_t num_groups,
+                         const int64_t* group_sizes, const float* lrs, int32_t step, float b1,
+                         float b2, float eps, void* const* flag_ptrs, int32_t rank,
+                         int32_t world, uint64_t epoch, uint32_t* err, void* stream_) {
+  SPLAX_NVTX("splax_nvls_adam_step");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (grad_mc == nullptr || param_mc == nullptr || param_local == nullptr || exp_avg == nullptr ||
+      exp_avg_sq == nullptr || group_sizes == nullptr || lrs == nullptr ||
+      flag_ptrs == nullptr || err == nullptr || n < 0 || num_groups < 1 ||
+      num_groups > kAdamMaxSegs || step < 1 || world < 1 || world > 8 || rank < 0 ||
+      rank >= world || epoch == 0)
+    return fail(SPLAX_ERR_INVALID_ARGUMENT,
+                "nvls_adam_step: NULL pointer, groups outside 1..8, step < 1, rank / world out "
+                "of range or epoch 0");
+  NvlsAdamGroups gr{};
+  int64_t end = 0;
+  for (int32_t k = 0; k < num_groups; ++k) {
+    if (group_sizes[k] < 0)
+      return fail(SPLAX_ERR_INVALID_ARGUMENT, "nvls_adam_step: negative group size");
+    end += group_sizes[k];
+    gr.end[k] = end;
+    gr.lr[k] = lrs[k];
+  }
+  gr.count = num_groups;
+  if (end != n)
+    return fail(SPLAX_ERR_INVALID_ARGUMENT, "nvls_adam_step: group sizes do not add up to n");
+  DeviceState* st;
+  int rc = current_state(&st);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(st->mu);
+  rc = st->init();
+  if (rc) return rc;
+  // bias corrections as optax forms them in fp32 (as splax_adam_step)
+  const float bc1 = 1.0f - std::pow(b1, static_cast<float>(step));
+  const float bc2 = 1.0f - std::pow(b2, static_cast<float>(step));
+  auto* const* flags = reinterpret_cast<unsigned long long* const*>(flag_ptrs);
+  st->timer.begin(kAllReduce, 3, stream);
+  if (launch_nvls_barrier(flags, rank, world, epoch, err, stream) ||
+      launch_nvls_adam(grad_mc, param_mc, param_local, exp_avg, exp_avg_sq, n, rank, world, gr,
+                       b1, b2, bc1, bc2, eps, stream) ||
+      launch_nvls_barrier(flags, rank, world, epoch + 1, err, stream)) {
+    st->timer.end(stream);
+    return fail(SPLAX_ERR_INVALID_ARGUMENT,
+                "nvls_adam_step: invalid flag array or a buffer not 16-byte aligned");
+  }
+  st->timer.end(stream);
+  return finish(*st, stream);
+}
+
 int splax_ply_info(const char* path, int64_t* num_vertices) {
   if (path == nullptr || num_vertices == nullptr)
     return fail(SPLAX_ERR_INVALID_ARGUMENT, "ply_info: NULL argument");

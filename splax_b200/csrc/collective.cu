@@ -21,6 +21,7 @@
 // returns.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 
 #include "common.cuh"
@@ -120,6 +121,64 @@ nvls_reduce_kernel(float* mc, int64_t n, int rank, int world) {
   asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
 
+// The training step's exchange and optimiser in one pass: for each 16-byte vector of this rank's
+// shard, the switch sums the gradients of every rank (multimem.ld_reduce), the rank applies Adam
+// with its shard of the moments (the optimiser state is sharded over the ranks), and multicasts
+// the updated parameters into every rank's copy (multimem.st). Reduce-scatter, update and
+// parameter all-gather in one kernel, moving the bytes of one all-reduce. Element e's learning
+// rate is the rate of the parameter group whose [start, end) holds e.
+__device__ __forceinline__ float group_lr(const NvlsAdamGroups& gr, int64_t e) {
+  float lr = gr.lr[0];
+#pragma unroll
+  for (int k = 1; k < kAdamMaxSegs; ++k)
+    if (k < gr.count && e >= gr.end[k - 1]) lr = gr.lr[k];
+  return lr;
+}
+
+__global__ void __launch_bounds__(kReduceThreads)
+nvls_adam_kernel(const float* grad_mc, float* param_mc, const float* __restrict__ param_local,
+                 float* __restrict__ m_shard, float* __restrict__ v_shard, int64_t n, int rank,
+                 int world, NvlsAdamGroups gr, float b1, float b2, float bc1, float bc2,
+                 float eps) {
+  const int64_t nv = n >> 2;
+  const int64_t per = (nv + world - 1) / world;
+  const int64_t v0 = min(nv, static_cast<int64_t>(rank) * per);
+  const int64_t v1 = min(nv, v0 + per);
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kReduceThreads;
+  for (int64_t v = v0 + static_cast<int64_t>(blockIdx.x) * kReduceThreads + threadIdx.x; v < v1;
+       v += stride) {
+    const float4 g = mm_ld_reduce(grad_mc + 4 * v);
+    float4 p = *reinterpret_cast<const float4*>(param_local + 4 * v);
+    float4 m = reinterpret_cast<float4*>(m_shard)[v - v0];
+    float4 w = reinterpret_cast<float4*>(v_shard)[v - v0];
+    const int64_t e = 4 * v;
+    adam_one(p.x, g.x, m.x, w.x, group_lr(gr, e), b1, b2, bc1, bc2, eps);
+    adam_one(p.y, g.y, m.y, w.y, group_lr(gr, e + 1), b1, b2, bc1, bc2, eps);
+    adam_one(p.z, g.z, m.z, w.z, group_lr(gr, e + 2), b1, b2, bc1, bc2, eps);
+    adam_one(p.w, g.w, m.w, w.w, group_lr(gr, e + 3), b1, b2, bc1, bc2, eps);
+    reinterpret_cast<float4*>(m_shard)[v - v0] = m;
+    reinterpret_cast<float4*>(v_shard)[v - v0] = w;
+    mm_st(param_mc + 4 * v, p);
+  }
+  // the n % 4 trailing elements: the last rank, first block; their moments follow its shard's
+  if (rank == world - 1 && blockIdx.x == 0) {
+    const int64_t i = 4 * nv + threadIdx.x;
+    if (i < n) {
+      float g;
+      asm volatile("multimem.ld_reduce.relaxed.sys.global.add.f32 %0, [%1];"
+                   : "=f"(g)
+                   : "l"(grad_mc + i)
+                   : "memory");
+      float p = param_local[i];
+      const int64_t j = 4 * (v1 - v0) + (i - 4 * nv);
+      adam_one(p, g, m_shard[j], v_shard[j], group_lr(gr, i), b1, b2, bc1, bc2, eps);
+      asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(param_mc + i), "f"(p)
+                   : "memory");
+    }
+  }
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
 }  // namespace
 
 int launch_nvls_barrier(unsigned long long* const* flags, int rank, int world,
@@ -131,6 +190,36 @@ int launch_nvls_barrier(unsigned long long* const* flags, int rank, int world,
     pf.p[q] = flags[q];
   }
   nvls_barrier_kernel<<<1, 32, 0, stream>>>(pf, rank, world, epoch, err);
+  return 0;
+}
+
+int64_t nvls_adam_shard_len(int64_t n, int rank, int world) {
+  const int64_t nv = n >> 2;
+  const int64_t per = (nv + world - 1) / world;
+  const int64_t v0 = std::min(nv, static_cast<int64_t>(rank) * per);
+  const int64_t v1 = std::min(nv, v0 + per);
+  return 4 * (v1 - v0) + (rank == world - 1 ? n - 4 * nv : 0);
+}
+
+int launch_nvls_adam(const float* grad_mc, float* param_mc, const float* param_local,
+                     float* m_shard, float* v_shard, int64_t n, int rank, int world,
+                     const NvlsAdamGroups& gr, float b1, float b2, float bc1, float bc2, float eps,
+                     cudaStream_t stream) {
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || n < 0) return -1;
+  if (n == 0) return 0;
+  if ((reinterpret_cast<uintptr_t>(grad_mc) | reinterpret_cast<uintptr_t>(param_mc) |
+       reinterpret_cast<uintptr_t>(param_local) | reinterpret_cast<uintptr_t>(m_shard) |
+       reinterpret_cast<uintptr_t>(v_shard)) % 16 != 0)
+    return -1;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t per = ((n >> 2) + world - 1) / world;
+  int64_t blocks = (per + kReduceThreads - 1) / kReduceThreads;
+  blocks = blocks < 1 ? 1 : (blocks > 4 * sms ? 4 * sms : blocks);
+  nvls_adam_kernel<<<static_cast<unsigned>(blocks), kReduceThreads, 0, stream>>>(
+      grad_mc, param_mc, param_local, m_shard, v_shard, n, rank, world, gr, b1, b2, bc1, bc2,
+      eps);
   return 0;
 }
 

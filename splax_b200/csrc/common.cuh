@@ -297,6 +297,17 @@ __device__ __forceinline__ void warp_walk_row(const WarpWalk& w, int lane, int r
   }
 }
 
+// One Adam update in optax's scale_by_adam form (fp32): m = (1 - b1) g + b1 m,
+// v = (1 - b2) g^2 + b2 v, p += -lr (m / bc1) / (sqrt(v / bc2) + eps), bc = 1 - b^step. Shared
+// by the single-GPU update and the fused NVLS exchange-and-update, so both round alike.
+__device__ __forceinline__ void adam_one(float& p, float g, float& m, float& v, float lr,
+                                         float b1, float b2, float bc1, float bc2, float eps) {
+  m = (1.0f - b1) * g + b1 * m;
+  v = (1.0f - b2) * (g * g) + b2 * v;
+  const float mh = m / bc1, vh = v / bc2;
+  p = p + (-lr) * (mh / (sqrtf(vh) + eps));
+}
+
 // Hardware base-2 exponential (MUFU): the blend kernels' exponent is pre-scaled by log2(e).
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;

@@ -9,20 +9,13 @@
 
 #include <cstdint>
 
+#include "common.cuh"
 #include "kernels.h"
 
 namespace splax {
 namespace {
 
 constexpr int kAdamThreads = 256;
-
-__device__ __forceinline__ void adam_one(float& p, float g, float& m, float& v, float lr,
-                                         float b1, float b2, float bc1, float bc2, float eps) {
-  m = (1.0f - b1) * g + b1 * m;
-  v = (1.0f - b2) * (g * g) + b2 * v;
-  const float mh = m / bc1, vh = v / bc2;
-  p = p + (-lr) * (mh / (sqrtf(vh) + eps));
-}
 
 __global__ void __launch_bounds__(kAdamThreads) adam_kernel(AdamSegs s, float b1, float b2,
                                                             float bc1, float bc2, float eps) {

@@ -190,3 +190,33 @@ def test_nvls_allreduce_argument_checks(lib):
         rc = f(a["mc"], flags, a["rank"], a["world"], a["n"], ctypes.c_uint64(a["epoch"]), err,
                None)
         assert rc == _lib.SPLAX_ERR_INVALID_ARGUMENT, bad
+
+
+def test_nvls_adam_argument_checks(lib):
+    """The fused exchange-and-Adam step refuses bad groups, steps, ranks and epochs before any
+    launch; the shard lengths of the ranks cover the buffer once."""
+    import ctypes
+
+    from splax_b200 import _lib
+
+    flags = (ctypes.c_void_p * 2)(16, 32)
+    sizes = (ctypes.c_int64 * 2)(6, 5)
+    lrs = (ctypes.c_float * 2)(1e-3, 1e-2)
+    P = ctypes.c_void_p
+    ok = dict(n=11, groups=2, step=1, rank=0, world=2, epoch=1)
+    for bad in (dict(n=12), dict(groups=0), dict(groups=9), dict(step=0), dict(rank=2),
+                dict(world=9), dict(epoch=0)):
+        a = {**ok, **bad}
+        rc = lib.splax_nvls_adam_step(P(1 << 20), P(1 << 21), P(1 << 22), P(1 << 23), P(1 << 24),
+                                      a["n"], a["groups"], sizes, lrs, a["step"], 0.9, 0.999,
+                                      1e-8, flags, a["rank"], a["world"],
+                                      ctypes.c_uint64(a["epoch"]), P(64), None)
+        assert rc == _lib.SPLAX_ERR_INVALID_ARGUMENT, bad
+    for n in (0, 3, 11, 1001, 9009):
+        for world in (1, 2, 3, 8):
+            total = 0
+            for rank in range(world):
+                ln = ctypes.c_int64(-1)
+                assert lib.splax_nvls_adam_shard_len(n, rank, world, ctypes.byref(ln)) == 0
+                total += ln.value
+            assert total == n, (n, world)
