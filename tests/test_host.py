@@ -220,3 +220,24 @@ def test_nvls_adam_argument_checks(lib):
                 assert lib.splax_nvls_adam_shard_len(n, rank, world, ctypes.byref(ln)) == 0
                 total += ln.value
             assert total == n, (n, world)
+
+
+def test_bench_reference_arm_contract():
+    """`bench.py --impl reference` (the CPU arm the driver runs) prints one JSON line with the
+    contract's keys, here on a small scene."""
+    import json
+    import subprocess
+    import sys
+
+    res = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference",
+                          "--steps", "1", "--warmup", "0", "--n", "2000"],
+                         capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert res.returncode == 0, res.stderr[-2000:]
+    line = json.loads(res.stdout.strip().splitlines()[-1])
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+                "higher_is_better", "scaling", "vs_baseline", "dtype", "data", "config",
+                "cpu_baseline", "e2e", "impl"):
+        assert key in line, key
+    assert line["impl"] == "reference" and line["value"] > 0
+    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
+    assert line["e2e"]["h2d_bytes_per_step"] == 0
