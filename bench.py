@@ -288,7 +288,8 @@ def reduce_grads(reducer, params, loss, dev):
 
 def train_bench(args) -> None:
     """Config 3: one batched training step = render_log fwd+bwd of B views, fused L1 + D-SSIM
-    loss, NCCL all-reduce of the gradients (camera shards), fused per-group Adam."""
+    loss and gradient, on camera shards the gradient exchange (NCCL or the library's NVLS
+    all-reduce, or with --collective nvls the exchange fused with Adam), per-group Adam."""
     import torch
     import torch.distributed as dist
 
