@@ -31,7 +31,7 @@ namespace splax {
 namespace {
 
 constexpr int kMaxRanks = 8;
-constexpr long long kBarrierSpinLimit = 1ll << 24;  // with a 64 ns back-off: ~1-2 s
+constexpr long long kBarrierSpinLimit = 1ll << 24;  // polls with a 64 ns back-off: seconds
 constexpr int kReduceThreads = 512;
 constexpr int kReduceUnroll = 1;  // 4 and 8 loads in flight per thread measured no faster
 
