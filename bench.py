@@ -11,7 +11,8 @@ summed with one NCCL all-reduce per step.
 
 ``--impl reference`` times the CPU restatement of the path (the C oracle, with every host
 thread) because the reference's own runtime (warp-lang + jax) cannot be installed here; rank 0
-alone runs it. Each of its steps is one camera of the workload (a bounded sample).
+alone runs it. Each of its steps renders one camera of the workload forward and backward, the
+steps rotating through all the cameras (a bounded sample of the same 8-camera mix).
 """
 
 from __future__ import annotations
@@ -52,7 +53,7 @@ L2_BYTES = 126 << 20
 # algorithmic work per unit: FLOPs per blend evaluation / contribution (FMA = 2), restated from
 # the reference blend loop (splax/_rasterize/_kernels.py:185-197) and vjp (:1235-1253)
 # DRAM bytes (read + write) per launch of the full config-2 workload from single-pass ncu
-# captures (dram__bytes_read.sum + dram__bytes_write.sum), summarised in profiles/*.md
+# captures (dram__bytes_read.sum + dram__bytes_write.sum)
 TRAFFIC_BYTES_PER_LAUNCH = {"raster_bwd": 575.29e6, "raster_fwd": 491.80e6,
                             "emit_keys": 811.68e6}
 FWD_FLOPS_PER_EVAL = 22
@@ -68,9 +69,9 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--impl", default="splax_b200", choices=["splax_b200", "reference"])
     ap.add_argument("--n", type=int, default=None, help="override the gaussian count (debug)")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--collective", default="auto", choices=["nccl", "nvls", "auto"],
-                    help="gradient all-reduce for N>1: NCCL, the library's NVLS kernel, or auto "
-                         "(NVLS from 4 ranks when the fabric offers multicast, else NCCL)")
+    ap.add_argument("--collective", default="nccl", choices=["nccl", "nvls", "auto"],
+                    help="gradient all-reduce for N>1: NCCL (default; 'auto' is the same), or "
+                         "the library's NVLS kernel, opt-in")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--forward-only", action="store_true",
                     help="time the forward render alone (configs 1, 2, 4)")
@@ -182,17 +183,17 @@ class ClockSampler:
                 "samples": len(rows), "source": "nvidia-smi, 200 ms"}
 
 
-def cpu_baseline(scene: dict, threads: int, forward_only: bool = False) -> dict:
-    """One camera of the workload, forward + backward (or forward only), through the C
-    oracle."""
+def cpu_baseline(scene: dict, threads: int, forward_only: bool = False, cam_index: int = 0,
+                 target: np.ndarray | None = None) -> dict:
+    """One camera of the workload (camera ``cam_index``, against ``target``, its (H, W, 3)
+    image), forward + backward (or forward only), through the C oracle."""
     import oracle
 
     oracle.build()
     n, H, W, f = scene["means"].shape[0], scene["H"], scene["W"], scene["f"]
     cam = dict(img_shape=(H, W), f=(f, f), c=(W / 2, H / 2))
     xyzw = np.roll(scene["quats"], -1, -1)
-    vm = scene["viewmats"][0]
-    target = scene["target"][0].reshape(H * W, 3)
+    vm = scene["viewmats"][cam_index]
     t0 = time.perf_counter()
     xys, d, r, cn, nth, cum = oracle.project(scene["means"], scene["scales"], xyzw, vm,
                                              scene["opacities"], n=n, nthreads=threads, **cam)
@@ -201,7 +202,7 @@ def cpu_baseline(scene: dict, threads: int, forward_only: bool = False) -> dict:
                                          cn, cum, n=n, B=1, img_shape=(H, W), nthreads=threads)
     if forward_only:
         return {"seconds": time.perf_counter() - t0, "counters": oracle.counters()}
-    v_img = 2.0 * (img.reshape(H * W, 3) - target) / (scene["B"] * H * W * 3)
+    v_img = 2.0 * (img.reshape(H * W, 3) - target.reshape(H * W, 3)) / (scene["B"] * H * W * 3)
     vc, vo, vxy, vcon, _ = oracle.rasterize_bwd(scene["colors"], op, op, scene["background"], xys,
                                                 d, r, cn, cum, fT, fi, v_img, n=n, B_out=1,
                                                 B_geom=1, img_shape=(H, W), nthreads=threads)
@@ -211,29 +212,65 @@ def cpu_baseline(scene: dict, threads: int, forward_only: bool = False) -> dict:
     return {"seconds": dt, "counters": oracle.counters()}
 
 
+def arm_config(workload: str, n: int, per: int, world: int, input_bytes: int, flush: bool,
+               collective: str | None) -> dict:
+    """The ``config`` object of a bench line; both arms print the same one for a workload."""
+    return {"workload": workload, "cams_per_gpu": per, "gaussians": n,
+            "l2": (f"inputs {input_bytes / 1e6:.0f} MB per rank, below 2x the 126 MB L2: L2 "
+                   "flushed (256 MB write) between timed steps" if flush else
+                   f"inputs {input_bytes / 1e6:.0f} MB per rank (targets + parameters) plus the "
+                   "per-step sort scratch exceed the 126 MB L2"),
+            "parallelism": f"camera-sharded dp{world}", "collective": collective}
+
+
 def reference_arm(args) -> None:
+    """The reference arm: the CPU restatement of the path on the host cores, on the same
+    workload and config object as this repo's arm. Step k renders camera k mod B (forward and
+    backward for the fwd+bwd configurations), so the steps cover the workload's camera mix."""
     from splax_b200 import utils
 
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    scene = utils.synthetic_scene(CONFIG, n=args.n)
-    scene["target"] = utils.target_images(scene, [0])
+    world = max(args.gpus, 1)
+    config = args.config if args.config in (0, 1, 2) else CONFIG
+    metric, workload, opts = FWD_BWD[config]
+    fwd_only = bool(opts.get("forward_only")) or args.forward_only
+    if args.forward_only and not opts.get("forward_only"):
+        metric = metric.replace("fwd+bwd", "forward")
+        workload += " (forward render only)"
+    scene = utils.synthetic_scene(config, n=args.n)
+    B, H, W = scene["B"], scene["H"], scene["W"]
+    n = scene["means"].shape[0]
+    per = B // world if B % world == 0 else B
+    targets = None if fwd_only else utils.target_images(scene)
     threads = os.cpu_count() or 1
-    for _ in range(min(args.warmup, 1)):
-        cpu_baseline(scene, threads)
-    times = [cpu_baseline(scene, threads)["seconds"] for _ in range(args.steps)]
+
+    def one(k):
+        c = k % B
+        return cpu_baseline(scene, threads, forward_only=fwd_only, cam_index=c,
+                            target=None if targets is None else targets[c])["seconds"]
+
+    for k in range(min(args.warmup, 1)):
+        one(k)
+    times = [one(k) for k in range(args.steps)]
     total = sum(times)
     value = args.steps / total  # one frame per step
-    sample = (f"1 of {scene['B']} cameras per step (N={scene['means'].shape[0]}, "
-              f"{scene['H']}x{scene['W']}, fwd+bwd)")
+    sample = (f"one camera per step, cameras 0..{B - 1} in turn (N={n}, {H}x{W}, "
+              f"{'forward' if fwd_only else 'fwd+bwd'}), C oracle with {threads} threads")
+    input_bytes = 4 * (14 * n + per * H * W * 3)
+    collective = None if world == 1 else ("nvls (library kernel)" if args.collective == "nvls"
+                                          else "nccl")
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "frames/s",
+        "impl": "reference", "metric": metric, "value": value, "unit": "frames/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, config 2 distributions)",
-        "config": {"workload": WORKLOAD,
-                   "implementation": "C oracle (CPU restatement; warp-lang/jax unavailable)"},
+        "vs_baseline": None, "dtype": "f32",
+        "data": f"synthetic (seeded, config {config} distributions)",
+        "config": arm_config(workload, n, per, world, input_bytes, input_bytes < 2 * L2_BYTES,
+                             collective),
+        "implementation": "C oracle: the CPU restatement of the path (warp-lang/jax, the "
+                          "reference's runtime, cannot be installed here)",
         "cpu_baseline": {"value": value, "unit": "frames/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": "frames/s", "h2d_bytes_per_step": 0,
@@ -250,19 +287,35 @@ SSIM_LAMBDA = 0.2
 
 
 def make_reducer(args, params, dev, world):
-    """The library's NVLS gradient all-reduce over the parameters' gradients plus the loss, or
-    None for NCCL. auto: NVLS from 4 ranks on a fabric with multicast (at 2 ranks NCCL's ring
-    moves the same bytes and measured faster here)."""
-    if world == 1 or args.collective == "nccl" or (args.collective == "auto" and world < 4):
+    """The library's NVLS gradient all-reduce over the parameters' gradients plus the loss when
+    --collective nvls asks for it, else None (NCCL). NVLS stays opt-in: it measured 2% faster
+    than NCCL at 4 ranks, and its symmetric buffers are bound to an NVLink multicast object for
+    the life of the run."""
+    if world == 1 or args.collective != "nvls":
         return None
     from splax_b200._collective import GradAllReduce
 
+    return GradAllReduce([p.shape for p in params] + [(1,)], dev)
+
+
+def teardown(world: int, closers: list) -> None:
+    """End a multi-rank run on every path, the error path included: wait for this rank's queued
+    work, release the collective objects (each waits for every rank before its symmetric memory
+    may go), then leave the process group. A rank that raised thus keeps its memory bound until
+    the others have left their kernels, or until the group's timeout ends the barrier."""
+    if world <= 1:
+        return
+    import torch
+    import torch.distributed as dist
+
     try:
-        return GradAllReduce([p.shape for p in params] + [(1,)], dev)
-    except RuntimeError:
-        if args.collective == "nvls":
-            raise
-        return None
+        torch.cuda.synchronize()
+        for c in closers:
+            c.close()
+        if not closers:
+            dist.barrier()
+    finally:
+        dist.destroy_process_group()
 
 
 def reduce_grads(reducer, params, loss, dev):
@@ -303,123 +356,119 @@ def train_bench(args) -> None:
     dev = torch.device("cuda", local)
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
-    scene = utils.synthetic_scene(3, n=args.n)
-    B, H, W, f = scene["B"], scene["H"], scene["W"], scene["f"]
-    n = scene["means"].shape[0]
-    if B % world:
-        raise SystemExit(f"{B} cameras do not split over {world} ranks")
-    per = B // world
-    cams = slice(rank * per, (rank + 1) * per)
-    targets_np = utils.target_images(scene, range(rank * per, (rank + 1) * per))
-    logit = lambda x: np.log(x) - np.log1p(-x)  # noqa: E731
-    host = {"means": scene["means"], "log_scales": np.log(scene["scales"]),
-            "quats": scene["quats"], "colors_logit": logit(np.clip(scene["colors"], 1e-4, 1 - 1e-4)),
-            "opac_logit": logit(scene["opacities"])}
-    params = [torch.tensor(host[k].astype(np.float32), device=dev).requires_grad_()
-              for k in TRAIN_LRS]
-    lrs = [lr * float(np.sqrt(B)) for lr in TRAIN_LRS.values()]
-    views = torch.tensor(scene["viewmats"][cams], device=dev)
-    target = torch.tensor(targets_np, device=dev)
-    bg = torch.tensor(scene["background"], device=dev)
-    kw = dict(background=bg, img_shape=(H, W), f=(f, f))
-    # with --collective nvls the exchange and the update fuse into one NVLS kernel (sharded
-    # moments); otherwise an all-reduce, then Adam on every rank
-    fused = None
-    if world > 1 and args.collective == "nvls":
-        from splax_b200._collective import NvlsAdam
-        try:
-            fused = NvlsAdam(params, lrs, dev)
-            params = fused.params
-        except RuntimeError:
-            if args.collective == "nvls":
-                raise
-    opt = None if fused is not None else sx.Adam(params, lrs)
-    reducer = None if fused is not None else make_reducer(args, params, dev, world)
-
-    def step(vm, tgt):
-        for p in params:
-            p.grad = None
-        imgs, _ = sx.render_log(*params, viewmat=vm, **kw)
-        loss = sx.l1_dssim_loss(imgs, tgt, ssim_lambda=SSIM_LAMBDA, views_total=B)
-        loss.backward()
-        if fused is not None:
-            fused.step([p.grad for p in params])
-            dist.all_reduce(loss.detach())
-            return loss
-        if world > 1:  # the shared gradients (and the loss) summed over the ranks
-            loss = reduce_grads(reducer, params, loss, dev)
-        opt.step([p.grad for p in params])
-        return loss
-
-    for _ in range(args.warmup):
-        step(views, target)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    uuid = None
+    closers: list = []
     try:
-        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
-    except Exception:
-        pass
-    sampler = ClockSampler(uuid) if rank == 0 else None
-    _lib.profile_enable(timing=True, count_work=False)
-    _lib.profile_reset()
-    if sampler:
-        sampler.start()
-        if sampler.thread is None:
-            time.sleep(0.3)  # nvidia-smi's first sample
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for _ in range(args.steps):
-        loss = step(views, target)
-    t1.record()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    clocks = sampler.stop() if sampler else None
-    prof = _lib.profile_report()
-    _lib.profile_enable(timing=False, count_work=False)
-    ms_t = torch.tensor([t0.elapsed_time(t1)], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-    ms = float(ms_t.item())
-    loss_v = float(loss.item())
-    if not np.isfinite(loss_v):
-        raise SystemExit("non-finite training loss")
-    if rank == 0:
-        kern = prof["kernels"]
-        total_ms = {k: v["ms"] for k, v in kern.items()}
-        line = {
-            "metric": "config 3 batched training step frames/s (3M gaussians, 840x1297, 32 cams)",
-            "value": B * args.steps / (ms / 1e3), "unit": "frames/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-            "steps_per_s": args.steps / (ms / 1e3), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded, config 3 distributions)",
-            "config": {"workload": "config 3: render_log fwd+bwd, L1 + 0.2 D-SSIM, all-reduce, "
-                                   "per-group Adam", "gaussians": n, "cams_per_gpu": per,
-                       "parallelism": f"camera-sharded dp{world}",
-                       "collective": None if world == 1 else
-                       ("nvls exchange fused with Adam (library kernel)" if fused is not None
-                        else "nvls (library kernel)" if reducer is not None else "nccl")},
-            "loss": loss_v,
-            "kernels": {k: {**v, "share": v["ms"] / max(sum(total_ms.values()), 1e-9)}
-                        for k, v in kern.items()},
-            "clocks": clocks,
-            "gpu_launches": int(sum(k["kernels"] for k in kern.values())),
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
+        scene = utils.synthetic_scene(3, n=args.n)
+        B, H, W, f = scene["B"], scene["H"], scene["W"], scene["f"]
+        n = scene["means"].shape[0]
+        if B % world:
+            raise SystemExit(f"{B} cameras do not split over {world} ranks")
+        per = B // world
+        cams = slice(rank * per, (rank + 1) * per)
+        targets_np = utils.target_images(scene, range(rank * per, (rank + 1) * per))
+        logit = lambda x: np.log(x) - np.log1p(-x)  # noqa: E731
+        host = {"means": scene["means"], "log_scales": np.log(scene["scales"]),
+                "quats": scene["quats"], "colors_logit": logit(np.clip(scene["colors"], 1e-4, 1 - 1e-4)),
+                "opac_logit": logit(scene["opacities"])}
+        params = [torch.tensor(host[k].astype(np.float32), device=dev).requires_grad_()
+                  for k in TRAIN_LRS]
+        lrs = [lr * float(np.sqrt(B)) for lr in TRAIN_LRS.values()]
+        views = torch.tensor(scene["viewmats"][cams], device=dev)
+        target = torch.tensor(targets_np, device=dev)
+        bg = torch.tensor(scene["background"], device=dev)
+        kw = dict(background=bg, img_shape=(H, W), f=(f, f))
+        # with --collective nvls the exchange and the update fuse into one NVLS kernel (sharded
+        # moments); otherwise an all-reduce, then Adam on every rank
+        fused = None
+        if world > 1 and args.collective == "nvls":
+            from splax_b200._collective import NvlsAdam
+            fused = NvlsAdam(params, lrs, dev)
+            closers.append(fused)
+            params = fused.params
+        opt = None if fused is not None else sx.Adam(params, lrs)
+        reducer = None if fused is not None else make_reducer(args, params, dev, world)
         if reducer is not None:
-            reducer.close()
-        if fused is not None:
-            fused.close()
-        dist.barrier()
-        dist.destroy_process_group()
+            closers.append(reducer)
+
+        def step(vm, tgt):
+            for p in params:
+                p.grad = None
+            imgs, _ = sx.render_log(*params, viewmat=vm, **kw)
+            loss = sx.l1_dssim_loss(imgs, tgt, ssim_lambda=SSIM_LAMBDA, views_total=B)
+            loss.backward()
+            if fused is not None:
+                fused.step([p.grad for p in params])
+                dist.all_reduce(loss.detach())
+                return loss
+            if world > 1:  # the shared gradients (and the loss) summed over the ranks
+                loss = reduce_grads(reducer, params, loss, dev)
+            opt.step([p.grad for p in params])
+            return loss
+
+        for _ in range(args.warmup):
+            step(views, target)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        uuid = None
+        try:
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+        except Exception:
+            pass
+        sampler = ClockSampler(uuid) if rank == 0 else None
+        _lib.profile_enable(timing=True, count_work=False)
+        _lib.profile_reset()
+        if sampler:
+            sampler.start()
+            if sampler.thread is None:
+                time.sleep(0.3)  # nvidia-smi's first sample
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.steps):
+            loss = step(views, target)
+        t1.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        clocks = sampler.stop() if sampler else None
+        prof = _lib.profile_report()
+        _lib.profile_enable(timing=False, count_work=False)
+        ms_t = torch.tensor([t0.elapsed_time(t1)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+        ms = float(ms_t.item())
+        loss_v = float(loss.item())
+        if not np.isfinite(loss_v):
+            raise SystemExit("non-finite training loss")
+        if rank == 0:
+            kern = prof["kernels"]
+            total_ms = {k: v["ms"] for k, v in kern.items()}
+            line = {
+                "metric": "config 3 batched training step frames/s (3M gaussians, 840x1297, 32 cams)",
+                "value": B * args.steps / (ms / 1e3), "unit": "frames/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+                "steps_per_s": args.steps / (ms / 1e3), "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded, config 3 distributions)",
+                "config": {"workload": "config 3: render_log fwd+bwd, L1 + 0.2 D-SSIM, all-reduce, "
+                                       "per-group Adam", "gaussians": n, "cams_per_gpu": per,
+                           "parallelism": f"camera-sharded dp{world}",
+                           "collective": None if world == 1 else
+                           ("nvls exchange fused with Adam (library kernel)" if fused is not None
+                            else "nvls (library kernel)" if reducer is not None else "nccl")},
+                "loss": loss_v,
+                "kernels": {k: {**v, "share": v["ms"] / max(sum(total_ms.values()), 1e-9)}
+                            for k, v in kern.items()},
+                "clocks": clocks,
+                "gpu_launches": int(sum(k["kernels"] for k in kern.values())),
+            }
+            print(json.dumps(line), flush=True)
+    finally:
+        teardown(world, closers)
 
 
 def main() -> None:
@@ -444,313 +493,306 @@ def main() -> None:
     dev = torch.device("cuda", local)
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
-
-    metric, workload, opts = FWD_BWD[args.config]
-    if args.forward_only and not opts.get("forward_only"):
-        opts = dict(opts, forward_only=True, viewmat_grad=False)
-        metric = metric.replace("fwd+bwd", "forward")
-        workload += " (forward render only)"
-    scene = utils.synthetic_scene(args.config, n=args.n)
-    B, H, W, f = scene["B"], scene["H"], scene["W"], scene["f"]
-    n = scene["means"].shape[0]
-    if B % world:
-        raise SystemExit(f"{B} cameras do not split over {world} ranks")
-    per = B // world
-    cams = slice(rank * per, (rank + 1) * per)
-    targets_np = utils.target_images(scene, range(rank * per, (rank + 1) * per))
-    host = {k: scene[k] for k in ("means", "scales", "quats", "colors", "opacities")}
-    params = [torch.tensor(host[k], device=dev).requires_grad_() for k in host]
-    views = torch.tensor(scene["viewmats"][cams], device=dev)
-    if opts["viewmat_grad"]:
-        views.requires_grad_()
-    target = torch.tensor(targets_np, device=dev)
-    bg = torch.tensor(scene["background"], device=dev)
-    kw = dict(background=bg, img_shape=(H, W), f=(f, f), antialiased=opts["antialiased"])
-    denom = float(B * H * W * 3)
-    reducer = None if opts.get("forward_only") else make_reducer(args, params, dev, world)
-
-    def step(vm, tgt, ps=params, tgt_ready=None):
-        """One step; returns the rendered images (forward only) or the loss. tgt_ready: an
-        event the loss waits for (the targets' copy may overlap the forward render)."""
-        if opts.get("forward_only"):
-            with torch.no_grad():
-                imgs, _ = sx.render(*ps, viewmat=vm, **kw)
-            return imgs
-        for p in ps:
-            p.grad = None
-        if vm.requires_grad:
-            vm.grad = None
-        imgs, _ = sx.render(*ps, viewmat=vm, **kw)
-        if tgt_ready is not None:
-            torch.cuda.current_stream(dev).wait_event(tgt_ready)
-        loss = sx.mse_loss(imgs, tgt, denom=denom)
-        loss.backward()
-        if world > 1:  # the gradients of the shared gaussians (and the loss) summed over ranks
-            loss = reduce_grads(reducer, ps, loss, dev)
-        return loss
-
-    for _ in range(args.warmup):
-        step(views, target)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-
-    uuid = None
+    closers: list = []
     try:
-        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
-    except Exception:
-        pass
-    sampler = ClockSampler(uuid) if rank == 0 else None
-    _lib.profile_enable(timing=True, count_work=False)
-    _lib.profile_reset()
-    if sampler:
-        sampler.start()
-        if sampler.thread is None:
-            time.sleep(0.3)  # nvidia-smi's first sample
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    # Inputs smaller than L2 (config 1): time each step alone and flush L2 between steps by
-    # writing a 256 MB buffer outside the timed events; otherwise one event pair around all.
-    input_bytes = 4 * (sum(p.numel() for p in params) + target.numel())
-    flush = input_bytes < 2 * L2_BYTES
-    if flush:
-        scratch = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in range(args.steps)]
-        for a, b in evs:
-            scratch.fill_(1)
-            a.record()
+
+        metric, workload, opts = FWD_BWD[args.config]
+        if args.forward_only and not opts.get("forward_only"):
+            opts = dict(opts, forward_only=True, viewmat_grad=False)
+            metric = metric.replace("fwd+bwd", "forward")
+            workload += " (forward render only)"
+        scene = utils.synthetic_scene(args.config, n=args.n)
+        B, H, W, f = scene["B"], scene["H"], scene["W"], scene["f"]
+        n = scene["means"].shape[0]
+        if B % world:
+            raise SystemExit(f"{B} cameras do not split over {world} ranks")
+        per = B // world
+        cams = slice(rank * per, (rank + 1) * per)
+        targets_np = utils.target_images(scene, range(rank * per, (rank + 1) * per))
+        host = {k: scene[k] for k in ("means", "scales", "quats", "colors", "opacities")}
+        params = [torch.tensor(host[k], device=dev).requires_grad_() for k in host]
+        views = torch.tensor(scene["viewmats"][cams], device=dev)
+        if opts["viewmat_grad"]:
+            views.requires_grad_()
+        target = torch.tensor(targets_np, device=dev)
+        bg = torch.tensor(scene["background"], device=dev)
+        kw = dict(background=bg, img_shape=(H, W), f=(f, f), antialiased=opts["antialiased"])
+        denom = float(B * H * W * 3)
+        reducer = None if opts.get("forward_only") else make_reducer(args, params, dev, world)
+        if reducer is not None:
+            closers.append(reducer)
+
+        def step(vm, tgt, ps=params, tgt_ready=None):
+            """One step; returns the rendered images (forward only) or the loss. tgt_ready: an
+            event the loss waits for (the targets' copy may overlap the forward render)."""
+            if opts.get("forward_only"):
+                with torch.no_grad():
+                    imgs, _ = sx.render(*ps, viewmat=vm, **kw)
+                return imgs
+            for p in ps:
+                p.grad = None
+            if vm.requires_grad:
+                vm.grad = None
+            imgs, _ = sx.render(*ps, viewmat=vm, **kw)
+            if tgt_ready is not None:
+                torch.cuda.current_stream(dev).wait_event(tgt_ready)
+            loss = sx.mse_loss(imgs, tgt, denom=denom)
+            loss.backward()
+            if world > 1:  # the gradients of the shared gaussians (and the loss) summed over ranks
+                loss = reduce_grads(reducer, ps, loss, dev)
+            return loss
+
+        for _ in range(args.warmup):
             step(views, target)
-            b.record()
-        torch.cuda.synchronize()
-        ms = sum(a.elapsed_time(b) for a, b in evs)
-    else:
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
-        t0.record()
-        for _ in range(args.steps):
-            step(views, target)
-        t1.record()
-        torch.cuda.synchronize()
-        ms = t0.elapsed_time(t1)
-    if world > 1:
-        dist.barrier()
-    clocks = sampler.stop() if sampler else None
-    prof = _lib.profile_report()
-    _lib.profile_enable(timing=False, count_work=False)
-    ms_t = torch.tensor([ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-    ms = float(ms_t.item())
-    value = B * args.steps / (ms / 1e3)
-
-    # one instrumented step outside the timed region: exact work units per step
-    _lib.profile_enable(timing=False, count_work=True)
-    _lib.profile_reset()
-    step(views, target)
-    torch.cuda.synchronize()
-    work = _lib.profile_report()["units"]
-    _lib.profile_enable(timing=False, count_work=False)
-
-    # end to end through the public API from pinned host buffers. Every step copies its batch
-    # from pinned host memory -- its cameras and, with a backward, its target images -- and
-    # reads its result back: the loss, or for a forward-only step the rendered images. The
-    # gaussians are the model: like a training loop, the step keeps them resident on the device.
-    # A copy stream fills one of two device slots with step k+1's batch while step k computes
-    # (a prefetching data loader; a step's loss waits for its targets, its render only for its
-    # cameras) and drains the images of forward-only steps; every copy is inside the timed region.
-    e2e = None
-    if not args.no_e2e:
-        fwd_only = bool(opts.get("forward_only"))
-        v_host = torch.from_numpy(np.ascontiguousarray(scene["viewmats"][cams])).pin_memory()
-        t_host = torch.from_numpy(np.ascontiguousarray(targets_np)).pin_memory()
-        loss_host = torch.empty((args.steps + 1,), dtype=torch.float32).pin_memory()
-        img_host = ([torch.empty((per, H, W, 3), dtype=torch.float32).pin_memory()
-                     for _ in range(2)] if fwd_only else None)
-        slots = [(torch.empty_like(views).requires_grad_(views.requires_grad),
-                  torch.empty_like(target)) for _ in range(2)]
-        h2d = v_host.numel() * 4 + (0 if fwd_only else t_host.numel() * 4)
-        d2h = per * H * W * 3 * 4 if fwd_only else 4
-        compute = torch.cuda.current_stream(dev)
-        copier = torch.cuda.Stream(dev)
-        copied = [torch.cuda.Event() for _ in range(2)]      # cameras on the device
-        copied_tgt = [torch.cuda.Event() for _ in range(2)]  # targets on the device
-        released = [torch.cuda.Event() for _ in range(2)]
-
-        def load(k):
-            s = k % 2
-            with torch.cuda.stream(copier), torch.no_grad():
-                copier.wait_event(released[s])
-                slots[s][0].copy_(v_host, non_blocking=True)
-                copied[s].record(copier)
-                if not fwd_only:
-                    slots[s][1].copy_(t_host, non_blocking=True)
-                copied_tgt[s].record(copier)
-
-        def run(k):
-            # the render waits for the cameras only; the loss waits for the targets, whose copy
-            # overlaps the forward of the same step
-            s = k % 2
-            compute.wait_event(copied[s])
-            out = step(slots[s][0], slots[s][1], tgt_ready=copied_tgt[s])
-            if fwd_only:
-                rendered = torch.cuda.Event()
-                rendered.record(compute)
-                with torch.cuda.stream(copier):
-                    copier.wait_event(rendered)
-                    img_host[s].copy_(out, non_blocking=True)
-                    out.record_stream(copier)
-            else:
-                loss_host[k].copy_(out.detach(), non_blocking=True)
-            released[s].record(compute)
-
-        for s in range(2):
-            released[s].record(compute)
-        load(0)
-        run(0)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(compute)
-        copier.wait_event(e0)
-        load(1)
-        for k in range(1, args.steps + 1):
-            if k + 1 <= args.steps:
-                load(k + 1)
-            run(k)
-        compute.wait_stream(copier)  # the last images are on the host
-        e1.record(compute)
+
+        uuid = None
+        try:
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+        except Exception:
+            pass
+        sampler = ClockSampler(uuid) if rank == 0 else None
+        _lib.profile_enable(timing=True, count_work=False)
+        _lib.profile_reset()
+        if sampler:
+            sampler.start()
+            if sampler.thread is None:
+                time.sleep(0.3)  # nvidia-smi's first sample
         torch.cuda.synchronize()
-        ems = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
         if world > 1:
-            dist.all_reduce(ems, op=dist.ReduceOp.MAX)
-        if fwd_only:
-            if not bool(torch.isfinite(img_host[args.steps % 2]).all()):
-                raise SystemExit("non-finite image in the end-to-end steps")
-        elif not bool(torch.isfinite(loss_host[1:]).all()):
-            raise SystemExit("non-finite loss in the end-to-end steps")
-        e2e = {"value": B * args.steps / (float(ems.item()) / 1e3), "unit": "frames/s",
-               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-               "inputs": "per-step cameras" + ("" if fwd_only else " and target images") +
-                         " from pinned host memory; gaussians resident (the model)",
-               "result": "rendered images to pinned host memory" if fwd_only else "loss",
-               "pipelining": "copy stream, two input slots"}
+            dist.barrier()
+        # Inputs smaller than L2 (config 1): time each step alone and flush L2 between steps by
+        # writing a 256 MB buffer outside the timed events; otherwise one event pair around all.
+        input_bytes = 4 * (sum(p.numel() for p in params) + target.numel())
+        flush = input_bytes < 2 * L2_BYTES
+        if flush:
+            scratch = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(args.steps)]
+            for a, b in evs:
+                scratch.fill_(1)
+                a.record()
+                step(views, target)
+                b.record()
+            torch.cuda.synchronize()
+            ms = sum(a.elapsed_time(b) for a, b in evs)
+        else:
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            t0.record()
+            for _ in range(args.steps):
+                step(views, target)
+            t1.record()
+            torch.cuda.synchronize()
+            ms = t0.elapsed_time(t1)
+        if world > 1:
+            dist.barrier()
+        clocks = sampler.stop() if sampler else None
+        prof = _lib.profile_report()
+        _lib.profile_enable(timing=False, count_work=False)
+        ms_t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+        ms = float(ms_t.item())
+        value = B * args.steps / (ms / 1e3)
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config in (0, 1, 2):
-        sc = dict(scene)
-        sc["target"] = targets_np[:1]
-        threads = os.cpu_count() or 1
-        fo = bool(opts.get("forward_only"))
-        res = cpu_baseline(sc, threads, forward_only=fo)
-        cpu = {"value": 1.0 / res["seconds"], "unit": "frames/s", "cores": threads,
-               "kind": "port",
-               "sample": f"camera 0 of {B} (one frame), N={n}, {H}x{W}, "
-                         f"{'forward' if fo else 'fwd+bwd'}, C oracle"}
+        # one instrumented step outside the timed region: exact work units per step
+        _lib.profile_enable(timing=False, count_work=True)
+        _lib.profile_reset()
+        step(views, target)
+        torch.cuda.synchronize()
+        work = _lib.profile_report()["units"]
+        _lib.profile_enable(timing=False, count_work=False)
 
-    if rank == 0:
-        peaks, peak_src = load_peaks()
-        props = torch.cuda.get_device_properties(dev)
-        sm_mhz = (clocks or {}).get("sm_mhz") or 1965.0
-        fp32_peak = props.multi_processor_count * 128 * 2 * sm_mhz * 1e6 / 1e12  # TFLOP/s
-        kern = prof["kernels"]
-        steps = args.steps
-        rows = {}
+        # end to end through the public API from pinned host buffers. Every step copies its batch
+        # from pinned host memory -- its cameras and, with a backward, its target images -- and
+        # reads its result back: the loss, or for a forward-only step the rendered images. The
+        # gaussians are the model: like a training loop, the step keeps them resident on the device.
+        # A copy stream fills one of two device slots with step k+1's batch while step k computes
+        # (a prefetching data loader; a step's loss waits for its targets, its render only for its
+        # cameras) and drains the images of forward-only steps; every copy is inside the timed region.
+        e2e = None
+        if not args.no_e2e:
+            fwd_only = bool(opts.get("forward_only"))
+            v_host = torch.from_numpy(np.ascontiguousarray(scene["viewmats"][cams])).pin_memory()
+            t_host = torch.from_numpy(np.ascontiguousarray(targets_np)).pin_memory()
+            loss_host = torch.empty((args.steps + 1,), dtype=torch.float32).pin_memory()
+            img_host = ([torch.empty((per, H, W, 3), dtype=torch.float32).pin_memory()
+                         for _ in range(2)] if fwd_only else None)
+            slots = [(torch.empty_like(views).requires_grad_(views.requires_grad),
+                      torch.empty_like(target)) for _ in range(2)]
+            h2d = v_host.numel() * 4 + (0 if fwd_only else t_host.numel() * 4)
+            d2h = per * H * W * 3 * 4 if fwd_only else 4
+            compute = torch.cuda.current_stream(dev)
+            copier = torch.cuda.Stream(dev)
+            copied = [torch.cuda.Event() for _ in range(2)]      # cameras on the device
+            copied_tgt = [torch.cuda.Event() for _ in range(2)]  # targets on the device
+            released = [torch.cuda.Event() for _ in range(2)]
 
-        def avg_ms(name):
-            k = kern[name]
-            return k["ms"] / k["launches"] if k["launches"] else None
+            def load(k):
+                s = k % 2
+                with torch.cuda.stream(copier), torch.no_grad():
+                    copier.wait_event(released[s])
+                    slots[s][0].copy_(v_host, non_blocking=True)
+                    copied[s].record(copier)
+                    if not fwd_only:
+                        slots[s][1].copy_(t_host, non_blocking=True)
+                    copied_tgt[s].record(copier)
 
-        units = prof["units"]
-        per_launch = lambda key, name: units[key] / max(kern[name]["launches"], 1)  # noqa: E731
-        I = work["intersections"]
-        # HBM-bound stages: algorithmic bytes per launch
-        kb = work["key_bytes"] / max(I, 1)
-        passes = work["sort_pass_keys"] / max(I, 1)
-        pairs = per_launch("pairs_fwd", "project_fwd")
-        V = work["pairs_sorted"]  # pairs that hit a tile (exact, from the instrumented step)
-        kbp = work["pair_key_bytes"] / max(V, 1)
-        pp = work["pair_pass_keys"] / max(V, 1)
-        bytes_est = {
-            "project_fwd": 44 * n + 36 * pairs,
-            "emit_keys": per_launch("intersections", "emit_keys") * (kb + 4) + 36 * pairs,
-            "radix_sort": per_launch("intersections", "radix_sort") * kb
-            + 2 * passes * per_launch("intersections", "radix_sort") * (kb + 4),
-            "tile_bins": per_launch("key_bytes", "tile_bins") + 8 * per_launch("bins", "tile_bins"),
-            # depth-order sort: the histogram and first pass read all P pair keys and keep the
-            # V that hit a tile; the other passes move V keys and values
-            "pair_sort": pairs * kbp + pairs * (kbp + 4) + V * (kbp + 4)
-            + 2 * max(pp - 1, 0) * V * (kbp + 4),
-            # prep pass: reads depth, radius, cum pair, xy, conic, both opacities, colour
-            # (56 B); writes key, value, walk record, blend record (88 B)
-            "pair_keys": 144 * pairs,
-            # the scan of the V sorted pairs' counts: perm, gathered count, offset
-            "pair_scan": 12 * V,
-            # per pair: radius, conic, v_xy, v_conic (36 B); per gaussian: means, scales,
-            # quats read and their cotangents written once, summed over the cameras (80 B)
-            "project_bwd": 36 * per_launch("pairs_bwd", "project_bwd") + 80 * n,
-            "depth_minmax": 8 * pairs,
-        }
-        for name, b in bytes_est.items():
-            t = avg_ms(name)
-            if t:
-                gbs = b / (t / 1e3) / 1e9
-                rows[name] = {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"],
-                              "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"], "ms": t}
-        fwd_flops = FWD_FLOPS_PER_EVAL * work["fwd_evals"]
-        bwd_flops = BWD_FLOPS_PER_EVAL * work["bwd_evals"] + BWD_FLOPS_PER_CONTRIB * work["bwd_contribs"]
-        for name, fl in (("raster_fwd", fwd_flops), ("raster_bwd", bwd_flops)):
-            t = avg_ms(name)
-            if t:
-                tf = fl / (t / 1e3) / 1e12
-                rows[name] = {"bound": "fp32", "achieved": tf, "peak": fp32_peak,
-                              "unit": "TFLOP/s", "frac": tf / fp32_peak, "ms": t}
-        total_ms = {k: v["ms"] for k, v in kern.items()}
-        dom = max(total_ms, key=total_ms.get)
-        for name, t in TRAFFIC_BYTES_PER_LAUNCH.items():
-            if name in rows and args.config == 2 and args.n is None and world == 1:
-                rows[name]["traffic"] = t
-        roof = dict(rows.get(dom, {}))
-        roof.pop("ms", None)
-        roof.update({"kernel": dom, "traffic": roof.get("traffic"),
-                     "peak_source": peak_src if roof.get("bound") == "hbm"
-                     else f"derived: {props.multi_processor_count} SMs x 128 FP32 lanes x 2 x "
-                          f"{sm_mhz:.0f} MHz sampled SM clock"})
-        launches = sum(k["kernels"] for k in kern.values())
-        line = {
-            "metric": metric, "value": value, "unit": "frames/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-            "data": f"synthetic (seeded, config {args.config} distributions)",
-            "config": {"workload": workload,
-                       "cams_per_gpu": per, "gaussians": n,
-                       "l2": (f"inputs {input_bytes / 1e6:.0f} MB per rank, below 2x the "
-                              "126 MB L2: L2 flushed (256 MB write) between timed steps"
-                              if flush else
-                              f"inputs {input_bytes / 1e6:.0f} MB per rank (targets + "
-                              "parameters) plus the per-step sort scratch exceed the 126 MB L2"),
-                       "parallelism": f"camera-sharded dp{world}",
-                       "collective": None if world == 1 else
-                       ("nvls (library kernel)" if reducer is not None else "nccl")},
-            "roofline": roof,
-            "kernels": {k: {**v, "share": v["ms"] / max(sum(total_ms.values()), 1e-9)}
-                        for k, v in kern.items()},
-            "kernel_rooflines": rows,
-            "work_per_step": work,
-            "clocks": clocks,
-            "e2e": e2e,
-            "cpu_baseline": cpu,
-            "gpu_launches": int(launches),
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        if reducer is not None:
-            reducer.close()
-        dist.barrier()
-        dist.destroy_process_group()
+            def run(k):
+                # the render waits for the cameras only; the loss waits for the targets, whose copy
+                # overlaps the forward of the same step
+                s = k % 2
+                compute.wait_event(copied[s])
+                out = step(slots[s][0], slots[s][1], tgt_ready=copied_tgt[s])
+                if fwd_only:
+                    rendered = torch.cuda.Event()
+                    rendered.record(compute)
+                    with torch.cuda.stream(copier):
+                        copier.wait_event(rendered)
+                        img_host[s].copy_(out, non_blocking=True)
+                        out.record_stream(copier)
+                else:
+                    loss_host[k].copy_(out.detach(), non_blocking=True)
+                released[s].record(compute)
+
+            for s in range(2):
+                released[s].record(compute)
+            load(0)
+            run(0)
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(compute)
+            copier.wait_event(e0)
+            load(1)
+            for k in range(1, args.steps + 1):
+                if k + 1 <= args.steps:
+                    load(k + 1)
+                run(k)
+            compute.wait_stream(copier)  # the last images are on the host
+            e1.record(compute)
+            torch.cuda.synchronize()
+            ems = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+            if world > 1:
+                dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+            if fwd_only:
+                if not bool(torch.isfinite(img_host[args.steps % 2]).all()):
+                    raise SystemExit("non-finite image in the end-to-end steps")
+            elif not bool(torch.isfinite(loss_host[1:]).all()):
+                raise SystemExit("non-finite loss in the end-to-end steps")
+            e2e = {"value": B * args.steps / (float(ems.item()) / 1e3), "unit": "frames/s",
+                   "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                   "inputs": "per-step cameras" + ("" if fwd_only else " and target images") +
+                             " from pinned host memory; gaussians resident (the model)",
+                   "result": "rendered images to pinned host memory" if fwd_only else "loss",
+                   "pipelining": "copy stream, two input slots"}
+
+        cpu = None
+        if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config in (0, 1, 2):
+            threads = os.cpu_count() or 1
+            fo = bool(opts.get("forward_only"))
+            res = cpu_baseline(scene, threads, forward_only=fo, cam_index=0,
+                               target=None if fo else targets_np[0])
+            cpu = {"value": 1.0 / res["seconds"], "unit": "frames/s", "cores": threads,
+                   "kind": "port",
+                   "sample": f"camera 0 of {B} (one frame), N={n}, {H}x{W}, "
+                             f"{'forward' if fo else 'fwd+bwd'}, C oracle"}
+
+        if rank == 0:
+            peaks, peak_src = load_peaks()
+            props = torch.cuda.get_device_properties(dev)
+            sm_mhz = (clocks or {}).get("sm_mhz") or 1965.0
+            fp32_peak = props.multi_processor_count * 128 * 2 * sm_mhz * 1e6 / 1e12  # TFLOP/s
+            kern = prof["kernels"]
+            steps = args.steps
+            rows = {}
+
+            def avg_ms(name):
+                k = kern[name]
+                return k["ms"] / k["launches"] if k["launches"] else None
+
+            units = prof["units"]
+            per_launch = lambda key, name: units[key] / max(kern[name]["launches"], 1)  # noqa: E731
+            I = work["intersections"]
+            # HBM-bound stages: algorithmic bytes per launch
+            kb = work["key_bytes"] / max(I, 1)
+            passes = work["sort_pass_keys"] / max(I, 1)
+            pairs = per_launch("pairs_fwd", "project_fwd")
+            V = work["pairs_sorted"]  # pairs that hit a tile (exact, from the instrumented step)
+            kbp = work["pair_key_bytes"] / max(V, 1)
+            pp = work["pair_pass_keys"] / max(V, 1)
+            bytes_est = {
+                "project_fwd": 44 * n + 36 * pairs,
+                "emit_keys": per_launch("intersections", "emit_keys") * (kb + 4) + 36 * pairs,
+                "radix_sort": per_launch("intersections", "radix_sort") * kb
+                + 2 * passes * per_launch("intersections", "radix_sort") * (kb + 4),
+                "tile_bins": per_launch("key_bytes", "tile_bins") + 8 * per_launch("bins", "tile_bins"),
+                # depth-order sort: the histogram and first pass read all P pair keys and keep the
+                # V that hit a tile; the other passes move V keys and values
+                "pair_sort": pairs * kbp + pairs * (kbp + 4) + V * (kbp + 4)
+                + 2 * max(pp - 1, 0) * V * (kbp + 4),
+                # prep pass: reads depth, radius, cum pair, xy, conic, both opacities, colour
+                # (56 B); writes key, value, walk record, blend record (88 B)
+                "pair_keys": 144 * pairs,
+                # the scan of the V sorted pairs' counts: perm, gathered count, offset
+                "pair_scan": 12 * V,
+                # per pair: radius, conic, v_xy, v_conic (36 B); per gaussian: means, scales,
+                # quats read and their cotangents written once, summed over the cameras (80 B)
+                "project_bwd": 36 * per_launch("pairs_bwd", "project_bwd") + 80 * n,
+                "depth_minmax": 8 * pairs,
+            }
+            for name, b in bytes_est.items():
+                t = avg_ms(name)
+                if t:
+                    gbs = b / (t / 1e3) / 1e9
+                    rows[name] = {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"],
+                                  "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"], "ms": t}
+            fwd_flops = FWD_FLOPS_PER_EVAL * work["fwd_evals"]
+            bwd_flops = BWD_FLOPS_PER_EVAL * work["bwd_evals"] + BWD_FLOPS_PER_CONTRIB * work["bwd_contribs"]
+            for name, fl in (("raster_fwd", fwd_flops), ("raster_bwd", bwd_flops)):
+                t = avg_ms(name)
+                if t:
+                    tf = fl / (t / 1e3) / 1e12
+                    rows[name] = {"bound": "fp32", "achieved": tf, "peak": fp32_peak,
+                                  "unit": "TFLOP/s", "frac": tf / fp32_peak, "ms": t}
+            total_ms = {k: v["ms"] for k, v in kern.items()}
+            dom = max(total_ms, key=total_ms.get)
+            for name, t in TRAFFIC_BYTES_PER_LAUNCH.items():
+                if name in rows and args.config == 2 and args.n is None and world == 1:
+                    rows[name]["traffic"] = t
+            roof = dict(rows.get(dom, {}))
+            roof.pop("ms", None)
+            roof.update({"kernel": dom, "traffic": roof.get("traffic"),
+                         "peak_source": peak_src if roof.get("bound") == "hbm"
+                         else f"derived: {props.multi_processor_count} SMs x 128 FP32 lanes x 2 x "
+                              f"{sm_mhz:.0f} MHz sampled SM clock"})
+            launches = sum(k["kernels"] for k in kern.values())
+            line = {
+                "metric": metric, "value": value, "unit": "frames/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+                "data": f"synthetic (seeded, config {args.config} distributions)",
+                "config": arm_config(workload, n, per, world, input_bytes, flush,
+                                     None if world == 1 else
+                                     ("nvls (library kernel)" if reducer is not None else "nccl")),
+                "roofline": roof,
+                "kernels": {k: {**v, "share": v["ms"] / max(sum(total_ms.values()), 1e-9)}
+                            for k, v in kern.items()},
+                "kernel_rooflines": rows,
+                "work_per_step": work,
+                "clocks": clocks,
+                "e2e": e2e,
+                "cpu_baseline": cpu,
+                "gpu_launches": int(launches),
+            }
+            print(json.dumps(line), flush=True)
+    finally:
+        teardown(world, closers)
 
 
 if __name__ == "__main__":

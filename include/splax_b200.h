@@ -64,11 +64,15 @@ int splax_project(const float *means3d, int64_t means3d_rows, const float *scale
 
 /* Projection forward that allocates nothing. No counterpart in the reference: same arguments
  * and outputs as splax_project, for callers that cannot let a library call cudaMalloc (an XLA
- * custom call under a preallocating JAX allocator, a stream being captured into a CUDA graph,
- * a fixed device-memory budget). Its scan scratch is a 512 KiB file-scope __device__ array,
- * so total = B*n is limited to 16,777,216 pairs (larger calls fail with
+ * custom call in a JAX process whose allocator has reserved most of the GPU up front, or an
+ * embedder with a fixed device-memory budget). Its scan scratch is a file-scope __device__
+ * array of 128 KiB + 16 bytes, held by every GPU that loads the library until the process
+ * exits, so total = B*n is limited to 16,777,216 pairs (larger calls fail with
  * SPLAX_ERR_INVALID_ARGUMENT). The first call on a device resolves the array's address; make
- * it before any stream capture. Calls share the array: calls overlapping on the GPU race. */
+ * it before any stream capture. Calls share the array: calls overlapping on the GPU race.
+ * Device-side errors (an intersection count past the int32 range, a scan wait that gave up)
+ * land in the array's own error word, which is read back only when SPLAX_SYNC_CHECK=1 (the call
+ * then synchronises the stream); otherwise they go unreported on this path. */
 int splax_project_noalloc(const float *means3d, int64_t means3d_rows, const float *scales,
                           int64_t scales_rows, const float *quats_xyzw, int64_t quats_rows,
                           const float *viewmat, int64_t viewmat_rows, const float *opacities,
@@ -291,7 +295,10 @@ int splax_adam_step(int32_t num_arrays, float *const *params, const float *const
  * before the first call). One call runs an entry barrier with `epoch`, the reduction of this
  * rank's shard (multimem.ld_reduce + multimem.st) and an exit barrier with epoch + 1, so epochs
  * advance by 2 per call, identically on every rank. A barrier that waits past its bound sets
- * bit 5 in *err (device word) and returns. No counterpart in the reference, which has no
+ * bit 5 in *err (device word) and returns; from then on, while *err is nonzero, every launch of
+ * this call and of later calls returns without touching peer or multicast memory, so the
+ * caller must read *err and stop the run (the exchange is not restartable in place). No
+ * counterpart in the reference, which has no
  * multi-device path: it replaces the psum of the gaussian gradients over a camera mesh that
  * a shard_map data-parallel training step would issue. */
 int splax_nvls_allreduce_f32(float *multicast, void *const *flag_ptrs, int32_t rank,

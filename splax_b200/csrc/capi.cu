@@ -1397,7 +1397,7 @@ int splax_nvls_allreduce_f32(float* multicast, void* const* flag_ptrs, int32_t r
   auto* const* flags = reinterpret_cast<unsigned long long* const*>(flag_ptrs);
   st->timer.begin(kAllReduce, 3, stream);
   if (launch_nvls_barrier(flags, rank, world, epoch, err, stream) ||
-      launch_nvls_allreduce(multicast, n, rank, world, stream) ||
+      launch_nvls_allreduce(multicast, n, rank, world, err, stream) ||
       launch_nvls_barrier(flags, rank, world, epoch + 1, err, stream)) {
     st->timer.end(stream);
     return fail(SPLAX_ERR_INVALID_ARGUMENT, "nvls_allreduce: invalid flag array");
@@ -1453,7 +1453,7 @@ int splax_nvls_adam_step(const float* grad_mc, float* param_mc, const float* par
   st->timer.begin(kAllReduce, 3, stream);
   if (launch_nvls_barrier(flags, rank, world, epoch, err, stream) ||
       launch_nvls_adam(grad_mc, param_mc, param_local, exp_avg, exp_avg_sq, n, rank, world, gr,
-                       b1, b2, bc1, bc2, eps, stream) ||
+                       b1, b2, bc1, bc2, eps, err, stream) ||
       launch_nvls_barrier(flags, rank, world, epoch + 1, err, stream)) {
     st->timer.end(stream);
     return fail(SPLAX_ERR_INVALID_ARGUMENT,

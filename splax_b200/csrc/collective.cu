@@ -18,7 +18,10 @@
 // each rank's copy of the buffer: rank r stores the epoch into slot r of every peer's array
 // (plain peer stores, release at system scope) and waits until its own array holds the epoch
 // in every slot (acquire loads). Waits are bounded; on expiry the kernel sets an error bit and
-// returns.
+// returns. Once a wait has given up, the error word stays set and every later launch of the
+// exchange on this rank (barriers, reductions) returns before touching peer or multicast memory:
+// a rank that failed to meet its peers stops issuing NVLink traffic toward them, so memory of a
+// rank that has left is never read or written through the switch afterwards.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -47,13 +50,18 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
   asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+// The rank's own error word (local memory); nonzero once a barrier of this or an earlier call
+// gave up.
+__device__ __forceinline__ bool exchange_failed(const unsigned* err) {
+  return *reinterpret_cast<const volatile unsigned*>(err) != 0u;
+}
 
 // Lane q < world signals peer q and then waits for peer q's signal.
 __global__ void __launch_bounds__(32)
 nvls_barrier_kernel(PeerFlags peers, int rank, int world, unsigned long long epoch,
                     unsigned* err) {
   const int q = threadIdx.x;
-  if (q >= world) return;
+  if (q >= world || exchange_failed(err)) return;
   asm volatile("fence.acq_rel.sys;" ::: "memory");
   st_release_sys(peers.p[q] + rank, epoch);
   const unsigned long long* mine = peers.p[rank] + q;
@@ -83,7 +91,8 @@ __device__ __forceinline__ void mm_st(float* a, float4 v) {
 
 // Each thread keeps kReduceUnroll loads in flight (consecutive threads, consecutive vectors).
 __global__ void __launch_bounds__(kReduceThreads)
-nvls_reduce_kernel(float* mc, int64_t n, int rank, int world) {
+nvls_reduce_kernel(float* mc, int64_t n, int rank, int world, const unsigned* err) {
+  if (exchange_failed(err)) return;  // the entry barrier did not meet every rank
   const int64_t nv = n >> 2;
   const int64_t per = (nv + world - 1) / world;
   const int64_t v0 = min(nv, static_cast<int64_t>(rank) * per);
@@ -139,7 +148,8 @@ __global__ void __launch_bounds__(kReduceThreads)
 nvls_adam_kernel(const float* grad_mc, float* param_mc, const float* __restrict__ param_local,
                  float* __restrict__ m_shard, float* __restrict__ v_shard, int64_t n, int rank,
                  int world, NvlsAdamGroups gr, float b1, float b2, float bc1, float bc2,
-                 float eps) {
+                 float eps, const unsigned* err) {
+  if (exchange_failed(err)) return;  // the entry barrier did not meet every rank
   const int64_t nv = n >> 2;
   const int64_t per = (nv + world - 1) / world;
   const int64_t v0 = min(nv, static_cast<int64_t>(rank) * per);
@@ -204,7 +214,7 @@ int64_t nvls_adam_shard_len(int64_t n, int rank, int world) {
 int launch_nvls_adam(const float* grad_mc, float* param_mc, const float* param_local,
                      float* m_shard, float* v_shard, int64_t n, int rank, int world,
                      const NvlsAdamGroups& gr, float b1, float b2, float bc1, float bc2, float eps,
-                     cudaStream_t stream) {
+                     const unsigned* err, cudaStream_t stream) {
   if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || n < 0) return -1;
   if (n == 0) return 0;
   if ((reinterpret_cast<uintptr_t>(grad_mc) | reinterpret_cast<uintptr_t>(param_mc) |
@@ -219,11 +229,11 @@ int launch_nvls_adam(const float* grad_mc, float* param_mc, const float* param_l
   blocks = blocks < 1 ? 1 : (blocks > 4 * sms ? 4 * sms : blocks);
   nvls_adam_kernel<<<static_cast<unsigned>(blocks), kReduceThreads, 0, stream>>>(
       grad_mc, param_mc, param_local, m_shard, v_shard, n, rank, world, gr, b1, b2, bc1, bc2,
-      eps);
+      eps, err);
   return 0;
 }
 
-int launch_nvls_allreduce(float* multicast, int64_t n, int rank, int world,
+int launch_nvls_allreduce(float* multicast, int64_t n, int rank, int world, const unsigned* err,
                           cudaStream_t stream) {
   if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || n < 0) return -1;
   if (n == 0 || world == 1) return 0;
@@ -235,8 +245,8 @@ int launch_nvls_allreduce(float* multicast, int64_t n, int rank, int world,
   const int64_t chunk = static_cast<int64_t>(kReduceThreads) * kReduceUnroll;
   int64_t blocks = (per + chunk - 1) / chunk;
   blocks = blocks < 1 ? 1 : (blocks > 4 * sms ? 4 * sms : blocks);
-  nvls_reduce_kernel<<<static_cast<unsigned>(blocks), kReduceThreads, 0, stream>>>(multicast, n,
-                                                                                   rank, world);
+  nvls_reduce_kernel<<<static_cast<unsigned>(blocks), kReduceThreads, 0, stream>>>(
+      multicast, n, rank, world, err);
   return 0;
 }
 

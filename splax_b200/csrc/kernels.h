@@ -258,8 +258,10 @@ struct PlyLayout {
 // rank's u64[world] flag array (all zero before the first epoch; epochs increase per call).
 int launch_nvls_barrier(unsigned long long* const* flags, int rank, int world,
                         unsigned long long epoch, unsigned* err, cudaStream_t stream);
-// In-place sum over the ranks of n floats at the multicast address (16-byte aligned).
-int launch_nvls_allreduce(float* multicast, int64_t n, int rank, int world, cudaStream_t stream);
+// In-place sum over the ranks of n floats at the multicast address (16-byte aligned); does
+// nothing once *err (this rank's error word) is nonzero.
+int launch_nvls_allreduce(float* multicast, int64_t n, int rank, int world, const unsigned* err,
+                          cudaStream_t stream);
 // Fused exchange and Adam update of a flat parameter buffer split in up to kAdamMaxSegs groups
 // (group k holds the elements below end[k], learning rate lr[k]).
 struct NvlsAdamGroups {
@@ -272,7 +274,7 @@ int64_t nvls_adam_shard_len(int64_t n, int rank, int world);
 int launch_nvls_adam(const float* grad_mc, float* param_mc, const float* param_local,
                      float* m_shard, float* v_shard, int64_t n, int rank, int world,
                      const NvlsAdamGroups& gr, float b1, float b2, float bc1, float bc2, float eps,
-                     cudaStream_t stream);
+                     const unsigned* err, cudaStream_t stream);
 
 int ply_parse_header(FILE* f, PlyLayout* L, int64_t* count, int64_t* body_offset,
                      std::string* why);

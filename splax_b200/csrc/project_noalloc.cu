@@ -4,23 +4,25 @@
 // splax_project keeps its scan's look-back words in scratch the library allocates with
 // cudaMalloc on first use. Some callers cannot let a library do that: an XLA custom call in a
 // JAX process whose allocator has preallocated most of the GPU (cudaMalloc then fails or
-// fragments what is left), code recording a CUDA graph on a stream where allocation is not
-// permitted, or an embedder whose memory budget is fixed up front. This entry point runs the
+// fragments what is left), or an embedder whose memory budget is fixed up front. This entry
+// point runs the
 // same kernel with its scratch in a file-scope __device__ array instead, so it never calls
 // cudaMalloc, cudaFree or any allocating routine. The caller still passes every input and
 // output buffer.
 //
 // Limits and rules:
 //  - at most kNoAllocMaxPairs = 16,777,216 (camera, gaussian) pairs per call (B * n); larger
-//    calls are rejected with SPLAX_ERR_INVALID_ARGUMENT. The array is 512 KiB + 16 bytes and
-//    every GPU that loads the library holds it until the process exits;
+//    calls are rejected with SPLAX_ERR_INVALID_ARGUMENT. The array is 128 KiB + 16 bytes
+//    (16,386 eight-byte words) and every GPU that loads the library holds it until the process
+//    exits;
 //  - the first call on each device resolves the array's device address (cudaGetSymbolAddress,
 //    with that device current); make that first call before any stream capture;
 //  - every call shares the one array and rewrites it (the scan words are cleared at the start
 //    of each call), so calls that overlap on the GPU -- two streams at once -- race and must be
 //    serialised by the caller;
-//  - the device error word (int32 overflow of the intersection count) is only read back when
-//    SPLAX_SYNC_CHECK=1, as for the other entry points between count readbacks.
+//  - the call's device error word (int32 overflow of the intersection count, a look-back wait
+//    that gave up) is the array's word 1, which no other entry point reads: it is read back,
+//    and reported, only when SPLAX_SYNC_CHECK=1. Without it those errors go unreported here.
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -40,6 +42,8 @@ constexpr int64_t kNoAllocTiles = kNoAllocMaxPairs / kProjScanTile;
 constexpr int64_t kNoAllocWords = kNoAllocTiles + 2;
 
 static __device__ __align__(256) unsigned long long g_noalloc_scratch[kNoAllocWords];
+static_assert(sizeof(g_noalloc_scratch) == 128 * 1024 + 16,
+              "the documented size of the no-alloc scratch is 128 KiB + 16 bytes");
 
 constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mu;

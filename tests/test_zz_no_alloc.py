@@ -1,13 +1,15 @@
 """splax_project_noalloc: the projection for callers that cannot allocate device memory.
 
 Some callers of this library must not let it call cudaMalloc -- an XLA custom call inside a
-JAX process whose allocator has already reserved most of the GPU, a stream being captured into a
-CUDA graph, an embedder with a fixed device-memory budget. For them the projection has a second
-entry point whose scan scratch is a fixed 512 KiB array compiled into the library (at most
-16,777,216 camera-gaussian pairs per call). This test calls it through the C ABI twice in a row
-and requires the same outputs, bit for bit, as splax_project -- the tolerance of every other
-projection test -- so a stale array left by the first call would show up in the second. It
-also checks that an oversized call is refused with a clear message.
+JAX process whose allocator has already reserved most of the GPU, or an embedder with a fixed
+device-memory budget. For them the projection has a second entry point whose scan scratch is a
+fixed 128 KiB + 16 byte array compiled into the library (at most 16,777,216 camera-gaussian
+pairs per call). This test calls it through the C ABI twice in a row, before the library's
+allocating projection has run in this test, so its first call does the per-device set-up, and
+requires the same outputs, bit for bit, as splax_project -- the tolerance of every other
+projection test -- so a stale array left by the first call would show up in the second. The
+device's free memory must not change across the second call. It also checks that an oversized
+call is refused with a clear message.
 
 The file is named to be collected last, so a run that stops at the first failure has already
 run every other test; it passes alone in a fresh process as well as after the others.
@@ -60,12 +62,14 @@ def test_project_noalloc_matches_project():
     ins = (t(m), t(s), t(np.roll(q, -1, -1)), t(views.reshape(-1, 4)), t(op),
            torch.zeros((1, 4, 4), device="cuda"), torch.full((1,), -1, device="cuda",
                                                               dtype=torch.int32))
+    # two calls in a row over differently stale buffers; the first one sets the device up
+    got = [_call(lib, "splax_project_noalloc", ins, n, H, W, B * n, fill)
+           for fill in (3.0, -5.0)]
     ref = _call(lib, "splax_project", ins, n, H, W, B * n, 0.0)
     assert ref[5][-1] > 0  # the scene hits tiles
-    for k, fill in enumerate((3.0, -5.0)):  # two calls in a row over differently stale buffers
-        got = _call(lib, "splax_project_noalloc", ins, n, H, W, B * n, fill)
-        for name, a, b in zip(["xys", "depths", "radii", "conics", "num_tiles_hit", "cum"], got,
-                              ref):
+    for k in range(2):
+        for name, a, b in zip(["xys", "depths", "radii", "conics", "num_tiles_hit", "cum"],
+                              got[k], ref):
             assert np.array_equal(a, b), f"call {k}: {name} differs"
     # a single-camera call after the batched ones must not see the batched call's scan words
     got1 = _call(lib, "splax_project_noalloc", (ins[0], ins[1], ins[2], t(viewmat()), ins[4],
@@ -74,6 +78,40 @@ def test_project_noalloc_matches_project():
                                         ins[6]), n, H, W, n, 0.0)
     for a, b in zip(got1, ref1):
         assert np.array_equal(a, b)
+
+
+def test_project_noalloc_leaves_free_memory_unchanged():
+    """Once set up, a call changes nothing in the device's free memory."""
+    if not torch.cuda.is_available():
+        pytest.fail("CUDA device required for -m gpu tests")
+    from splax_b200 import _lib
+
+    lib = _lib.load()
+    n, H, W = 20_000, 200, 300
+    m, s, q, c, op, bg = random_scene(n, 23, spread=1.0, smin=0.005, smax=0.05)
+    t = lambda a: torch.tensor(np.ascontiguousarray(a), device="cuda")  # noqa: E731
+    ins = (t(m), t(s), t(np.roll(q, -1, -1)), t(viewmat()), t(op),
+           torch.zeros((1, 4, 4), device="cuda"), torch.full((1,), -1, device="cuda",
+                                                              dtype=torch.int32))
+    outs = [torch.empty((n, 2), device="cuda"), torch.empty((n,), device="cuda"),
+            torch.empty((n,), device="cuda", dtype=torch.int32), torch.empty((n, 3), device="cuda"),
+            torch.empty((n,), device="cuda", dtype=torch.int32),
+            torch.empty((n,), device="cuda", dtype=torch.int32)]
+    p = _lib.ptr
+    cm = cam(H, W)
+
+    def call():
+        _lib.check(lib.splax_project_noalloc(
+            p(ins[0]), n, p(ins[1]), n, p(ins[2]), n, p(ins[3]), 4, p(ins[4]), n, p(ins[5]), 1,
+            p(ins[6]), n, 1, 0, H, W, cm["f"][0], cm["f"][1], float(cm["c"][0]),
+            float(cm["c"][1]), 1.0, 0.01, n, *[p(o) for o in outs], _lib.stream_of(ins[0])))
+        torch.cuda.synchronize()
+
+    call()  # set-up (module load, symbol address) happens here at the latest
+    free0, _ = torch.cuda.mem_get_info()
+    call()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
 
 
 def test_project_noalloc_rejects_oversized_calls():
