@@ -204,23 +204,36 @@ def test_rasterize_bwd_parity(sx, oracle_lib):
         assert rel_l2(N(a).reshape(b.shape), b) <= GRAD_TOL, name
 
 
+def _masked_cotangent(ch, m, s, q, c, op, bg, vm, H, W, seed):
+    """A seeded image cotangent, zero on the pixels whose threshold decisions (alpha vs 1/255,
+    T vs 1e-4, sigma's sign) the oracle flags as within rounding distance of the boundary: there
+    the two implementations may legitimately take different branches, as in the image test."""
+    _, _, st = ch.render(m, s, q, c, op, bg, vm, **cam(H, W))
+    flags = st["flags"].reshape(H, W)
+    assert (flags == 0).mean() > 0.99
+    w = np.random.default_rng(seed).uniform(size=(H, W, 3)).astype(np.float32) / (H * W)
+    w[flags != 0] = 0.0
+    return w
+
+
 def test_render_grads_vs_oracle(sx, oracle_lib):
-    """End to end: torch autograd through render vs the oracle's vjp chain."""
+    """End to end: torch autograd through render vs the oracle's vjp chain, the image cotangent
+    masked on flagged pixels."""
     import _oracle_chain as ch
 
     n, H, W = 3000, 128, 128
     m, s, q, c, op, bg = random_scene(n, 11)
     vm = viewmat()
-    w = np.random.default_rng(3).uniform(size=(H, W, 3)).astype(np.float32) / (H * W)
+    w = _masked_cotangent(ch, m, s, q, c, op, bg, vm, H, W, 3)
     params = [T(x).requires_grad_() for x in (m, s, q, c, op)]
     vm_t = T(vm).requires_grad_()
     img, _ = sx.render(*params, viewmat=vm_t, background=T(bg), **cam(H, W))
     (img * T(w)).sum().backward()
     ref = ch.grads(m, s, q, c, op, bg, vm, w, **cam(H, W))
     names = ["means", "scales", "quats", "colors", "opacities"]
-    for name, pt, g in zip(names, params, ref[:5]):
-        assert rel_l2(N(pt.grad), g) <= 5 * GRAD_TOL, name
-    assert rel_l2(N(vm_t.grad), ref[5]) <= 5 * GRAD_TOL
+    errs = {name: rel_l2(N(pt.grad), g) for name, pt, g in zip(names, params, ref[:5])}
+    errs["viewmat"] = rel_l2(N(vm_t.grad), ref[5])
+    assert max(errs.values()) <= GRAD_TOL, errs
 
 
 def test_batched_render_equals_stack_64bit(sx, monkeypatch):
@@ -255,7 +268,8 @@ def test_batched_grads_match_sequential(sx):
     img, _ = sx.render(bt, T(s), T(q), T(c), T(op), **kw)
     img.sum().backward()
     seq = np.stack([grad_of(bm[i]) for i in range(B)])
-    assert np.allclose(N(bt.grad), seq, rtol=2e-3, atol=1e-4)
+    for i in range(B):  # each image's means gradient (only the atomics' order differs)
+        assert rel_l2(N(bt.grad)[i], seq[i]) <= GRAD_TOL, i
 
 
 def test_key_width_fallback_and_overflow(sx):
