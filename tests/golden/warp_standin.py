@@ -1,0 +1,577 @@
+"""A minimal CPU stand-in for the ``warp`` module, enough to execute the reference's own kernel
+source -- TEST INFRASTRUCTURE ONLY (fixture generation; nothing in the product imports it).
+
+warp-lang 1.15.0 (the reference's pin, pixi.lock:8308-8309) is not installed here and cannot
+be. Its kernels, though, are plain Python source. This module provides the subset of Warp's
+Python API that splax/_intersect.py, splax/_rasterize/_sort/_kernels.py,
+splax/_rasterize/_sort/_sort.py and the forward of splax/_project/_kernels.py use, with the
+semantics those kernels need, so that the unmodified reference functions run thread by thread
+on the CPU:
+
+- scalars are numpy scalars: ``float32`` rounds every operation to IEEE single precision (no
+  fused multiply-add), ``int32`` / ``int64`` wrap like C integers;
+- ``wp.int32(x)`` of a float truncates toward zero and saturates (NaN -> 0), the device's
+  cvt.rzi semantics;
+- ``/`` between integers is C's truncating division (Warp's ``int / int``); the loader
+  rewrites every ``/`` of the loaded source into that dispatch (see ``load_reference``);
+- vectors and 3x3 matrices are small float32 / int32 arrays; a matrix product sums over k in
+  ascending order, ``(a0 b0 + a1 b1) + a2 b2``;
+- ``wp.quat_to_matrix`` is the standard rotation matrix of a unit quaternion stored xyzw,
+  ``wp.sqrt`` the correctly rounded square root, ``wp.ceil`` IEEE ceil;
+- ``wp.log`` is pluggable (``set_log``): the default is the atanh-series logarithm restated
+  below (the one the CUDA path and the C oracle evaluate), the alternative numpy's float32 log
+  (the C library's logf) -- Warp's own fast-math ``log`` is native code absent from the
+  reference tree;
+- ``wp.utils.radix_sort_pairs`` is a stable ascending sort of signed keys and
+  ``wp.utils.array_scan`` an int32 inclusive scan (the semantics the reference's tests pin:
+  tests/test_warp_batch.py:124-126, 129-244);
+- ``wp.launch`` runs the kernel body once per thread index, in order, converting the launch's
+  arguments to the kernel's annotated parameter types as Warp does.
+
+These are statements about builtins whose implementation lives in warp-lang's native library;
+the fixtures made with this module therefore pin the reference's kernel code -- its control
+flow, integer logic, key layouts, operation order and quirks -- under these builtin
+semantics, not Warp's compiled fast-math arithmetic.
+"""
+
+from __future__ import annotations
+
+import ast
+import builtins
+import sys
+import types
+import warnings
+from pathlib import Path
+
+import numpy as np
+
+warnings.filterwarnings("ignore", category=RuntimeWarning)
+
+
+# ------------------------------------------------------------------ scalar types
+class float32:
+    def __new__(cls, x=0.0):
+        return np.float32(x)
+
+
+def _f2i(x, dtype):
+    info = np.iinfo(dtype)
+    xf = float(x)
+    if xf != xf:
+        return dtype(0)
+    if xf >= float(info.max) + 1.0:
+        return dtype(info.max)
+    if xf < float(info.min):
+        return dtype(info.min)
+    return dtype(int(xf))  # int() truncates toward zero
+
+
+class int32:
+    def __new__(cls, x=0):
+        if isinstance(x, (float, np.floating)):
+            return _f2i(x, np.int32)
+        return np.uint32(int(x) & 0xFFFFFFFF).astype(np.int32)  # wraps like C
+
+
+class int64:
+    def __new__(cls, x=0):
+        if isinstance(x, (float, np.floating)):
+            return _f2i(x, np.int64)
+        return np.uint64(int(x) & 0xFFFFFFFFFFFFFFFF).astype(np.int64)
+
+
+class uint32:
+    def __new__(cls, x=0):
+        if isinstance(x, (float, np.floating)):
+            return _f2i(x, np.uint32)
+        return np.uint32(int(x) & 0xFFFFFFFF)
+
+
+class bool_:
+    def __new__(cls, x=False):
+        return builtins.bool(x)
+
+
+# ------------------------------------------------------------------ vectors / matrices
+class _Vec:
+    _n = 0
+    _dt = np.float32
+
+    def __init__(self, *args, _view=None):
+        if _view is not None:
+            self.a = _view
+            return
+        if len(args) == 0:
+            self.a = np.zeros(self._n, self._dt)
+        elif len(args) == 1 and isinstance(args[0], _Vec):
+            self.a = args[0].a.astype(self._dt).copy()
+        elif len(args) == 1:
+            self.a = np.full(self._n, args[0], self._dt)
+        else:
+            assert len(args) == self._n, (type(self).__name__, args)
+            self.a = np.array([self._dt(v) if not isinstance(v, np.generic) else v.astype(self._dt)
+                               for v in args], self._dt)
+
+    def __getitem__(self, i):
+        return self.a[int(i)]
+
+    def __setitem__(self, i, v):
+        self.a[int(i)] = v
+
+    def _new(self, arr):
+        v = type(self).__new__(type(self))
+        v.a = arr.astype(self._dt)
+        return v
+
+    def __add__(self, o):
+        return self._new(self.a + (o.a if isinstance(o, _Vec) else o))
+
+    def __sub__(self, o):
+        return self._new(self.a - (o.a if isinstance(o, _Vec) else o))
+
+    def __mul__(self, o):
+        assert not isinstance(o, _Vec)
+        return self._new(self.a * self._dt(o))
+
+    __rmul__ = __mul__
+
+    def __truediv__(self, o):
+        return self._new(self.a / self._dt(o))
+
+    def __neg__(self):
+        return self._new(-self.a)
+
+    def __repr__(self):
+        return f"{type(self).__name__}({list(self.a)})"
+
+
+def _vec_type(name, n, dt):
+    return type(name, (_Vec,), {"_n": n, "_dt": dt})
+
+
+vec2 = _vec_type("vec2", 2, np.float32)
+vec3 = _vec_type("vec3", 3, np.float32)
+vec4 = _vec_type("vec4", 4, np.float32)
+vec2i = _vec_type("vec2i", 2, np.int32)
+
+
+class quat(_Vec):
+    """xyzw storage, as wp.quat."""
+    _n = 4
+    _dt = np.float32
+
+
+def _dot3(r, v):
+    return (r[0] * v[0] + r[1] * v[1]) + r[2] * v[2]
+
+
+class mat33:
+    def __init__(self, *args, _arr=None):
+        if _arr is not None:
+            self.m = _arr.astype(np.float32)
+        elif len(args) == 0:
+            self.m = np.zeros((3, 3), np.float32)
+        else:
+            assert len(args) == 9
+            self.m = np.array([np.float32(v) for v in args], np.float32).reshape(3, 3)
+
+    def __getitem__(self, ij):
+        if isinstance(ij, tuple):
+            return self.m[int(ij[0]), int(ij[1])]
+        return vec3(_view=self.m[int(ij)].copy())
+
+    def __mul__(self, o):
+        if isinstance(o, mat33):
+            out = np.zeros((3, 3), np.float32)
+            for i in range(3):
+                for j in range(3):
+                    out[i, j] = _dot3(self.m[i], o.m[:, j])
+            return mat33(_arr=out)
+        if isinstance(o, _Vec):
+            return vec3(*[_dot3(self.m[i], o.a) for i in range(3)])
+        return mat33(_arr=self.m * np.float32(o))
+
+    def __rmul__(self, o):
+        return mat33(_arr=self.m * np.float32(o))
+
+    def __add__(self, o):
+        return mat33(_arr=self.m + o.m)
+
+    def __sub__(self, o):
+        return mat33(_arr=self.m - o.m)
+
+
+def transpose(m):
+    return mat33(_arr=m.m.T.copy())
+
+
+def diag(v):
+    out = np.zeros((3, 3), np.float32)
+    for i in range(3):
+        out[i, i] = v[i]
+    return mat33(_arr=out)
+
+
+def quat_to_matrix(q):
+    x, y, z, w = q[0], q[1], q[2], q[3]
+    one, two = np.float32(1.0), np.float32(2.0)
+    return mat33(one - two * (y * y + z * z), two * (x * y - w * z), two * (x * z + w * y),
+                 two * (x * y + w * z), one - two * (x * x + z * z), two * (y * z - w * x),
+                 two * (x * z - w * y), two * (y * z + w * x), one - two * (x * x + y * y))
+
+
+# ------------------------------------------------------------------ arrays
+class array:
+    """A Warp array over a numpy buffer. ``dtype`` is a stand-in scalar or vector type."""
+
+    def __class_getitem__(cls, item):
+        return cls
+
+    def __init__(self, data, dtype=None):
+        self.data = data
+        self.dtype = dtype
+        w = dtype._n if isinstance(dtype, type) and issubclass(dtype, _Vec) else 0
+        self.width = w
+        self.shape = data.shape[:-1] if w else data.shape
+        self.device = "cpu"
+
+    def __getitem__(self, idx):
+        if isinstance(idx, tuple):
+            idx = tuple(int(i) for i in idx)
+        else:
+            idx = int(idx)
+        if self.width:
+            return self.dtype(_view=self.data[idx])  # a view: component stores write through
+        v = self.data[idx]
+        if isinstance(v, np.ndarray):
+            return array(v, self.dtype)
+        return v
+
+    def __setitem__(self, idx, val):
+        if isinstance(idx, tuple):
+            idx = tuple(int(i) for i in idx)
+        else:
+            idx = int(idx)
+        self.data[idx] = val.a if isinstance(val, _Vec) else val
+
+    def zero_(self):
+        self.data[...] = 0
+
+    def view(self, dtype):
+        np_dt = {int32: np.int32, float32: np.float32, int64: np.int64}[dtype]
+        return array(self.data.view(np_dt), dtype)
+
+    def numpy(self):
+        return self.data
+
+
+array2d = array
+array3d = array
+
+
+# ------------------------------------------------------------------ builtins
+_TID = [0]
+_LOG = ["atanh"]
+
+
+def tid():
+    return np.int32(_TID[0])
+
+
+def _atanh_logf(x):
+    """Natural log by log(m) = 2 atanh((m-1)/(m+1)) (Abramowitz & Stegun 4.1.27) on
+    m in [sqrt(1/2), sqrt(2)) with a two-part ln 2 for the exponent, every step an fp32
+    operation; the logarithm the CUDA path and the C oracle evaluate."""
+    x = np.float32(x)
+    if not x > 0:
+        return np.float32(-np.inf) if x == 0 else np.float32(np.nan)
+    if np.isinf(x):
+        return x
+    e = 0
+    bits = int(np.array(x, np.float32).view(np.uint32))
+    if bits < 0x00800000:
+        x = x * np.float32(8388608.0)
+        bits = int(np.array(x, np.float32).view(np.uint32))
+        e = -23
+    e += (bits >> 23) - 127
+    m = np.array((bits & 0x007FFFFF) | 0x3F800000, np.uint32).view(np.float32)[()]
+    if m > np.float32(1.41421356):
+        m = m * np.float32(0.5)
+        e += 1
+    s = (m - np.float32(1.0)) / (m + np.float32(1.0))
+    s2 = s * s
+    p = np.float32(0.0909090936)
+    for c in (0.111111112, 0.142857149, 0.200000003, 0.333333343, 1.0):
+        p = p * s2 + np.float32(c)
+    fe = np.float32(e)
+    lm = (np.float32(2.0) * s) * p
+    return fe * np.float32(0.693145751953125) + (lm + fe * np.float32(1.42860677e-06))
+
+
+def set_log(kind: str) -> None:
+    """'atanh' (default): the restated series above; 'libm': numpy's float32 log."""
+    assert kind in ("atanh", "libm")
+    _LOG[0] = kind
+
+
+def log(x):
+    return _atanh_logf(x) if _LOG[0] == "atanh" else np.log(np.float32(x))
+
+
+def sqrt(x):
+    return np.sqrt(np.float32(x))
+
+
+def exp(x):
+    return np.exp(np.float32(x))
+
+
+def ceil(x):
+    return np.ceil(np.float32(x))
+
+
+def floor(x):
+    return np.floor(np.float32(x))
+
+
+def abs(x):  # noqa: A001
+    return np.abs(x)
+
+
+def min(a, b):  # noqa: A001
+    return a if a < b else b
+
+
+def max(a, b):  # noqa: A001
+    return a if a > b else b
+
+
+def clamp(x, lo, hi):
+    return min(max(x, lo), hi)
+
+
+def where(c, a, b):
+    return a if c else b
+
+
+def atomic_min(arr, i, v):
+    old = arr[i]
+    if v < old:
+        arr[i] = v
+    return old
+
+
+def atomic_max(arr, i, v):
+    old = arr[i]
+    if v > old:
+        arr[i] = v
+    return old
+
+
+def atomic_add(arr, i, v):
+    old = arr[i]
+    arr[i] = old + v
+    return old
+
+
+def _is_int(x):
+    return isinstance(x, (np.integer, int)) and not isinstance(x, builtins.bool)
+
+
+def _wp_div(a, b):
+    """``a / b`` with Warp's typing: C's truncating division for two integers of which one is
+    a Warp (numpy) integer, else the operands' own division."""
+    if _is_int(a) and _is_int(b) and (isinstance(a, np.integer) or isinstance(b, np.integer)):
+        dt = np.int64 if np.int64 in (type(a), type(b)) else np.int32
+        ia, ib = int(a), int(b)
+        q = builtins.abs(ia) // builtins.abs(ib)
+        return dt(q if (ia >= 0) == (ib >= 0) else -q)
+    return a / b
+
+
+# ------------------------------------------------------------------ decorators and launch
+def init():
+    pass
+
+
+def set_module_options(_opts):
+    pass
+
+
+def constant(x):
+    if isinstance(x, bool):
+        return x
+    if isinstance(x, int):
+        return np.int32(x)
+    if isinstance(x, float):
+        return np.float32(x)
+    return x
+
+
+def _convert(val, ann):
+    if ann is float32:
+        return np.float32(val)
+    if ann is int32:
+        return int32(val)
+    if ann is int64:
+        return int64(val)
+    if ann is uint32:
+        return uint32(val)
+    if ann is bool_:
+        return builtins.bool(val)
+    return val
+
+
+class Kernel:
+    def __init__(self, fn):
+        self.fn = fn
+        self.key = fn.__name__
+        self._hints = None
+
+    def hints(self):
+        if self._hints is None:
+            g = self.fn.__globals__
+            self._hints = [eval(a, g) if isinstance(a, str) else a  # noqa: S307
+                           for n, a in self.fn.__annotations__.items() if n != "return"]
+        return self._hints
+
+
+def kernel(fn=None, **_kw):
+    if fn is None:
+        return lambda f: Kernel(f)
+    return Kernel(fn)
+
+
+def func(fn=None, **_kw):
+    if fn is None:
+        return lambda f: f
+    return fn
+
+
+def struct(cls):
+    g = sys.modules[cls.__module__].__dict__
+    fields = {k: (eval(v, g) if isinstance(v, str) else v)  # noqa: S307
+              for k, v in cls.__annotations__.items()}
+
+    class _S:
+        __slots__ = tuple(fields)
+
+        def __init__(self):
+            for k, t in fields.items():
+                object.__setattr__(self, k, t())
+
+    _S.__name__ = cls.__name__
+    return _S
+
+
+bool = bool_  # noqa: A001  (wp.bool)
+
+
+def launch(kernel, dim, inputs=(), outputs=(), device=None, **_kw):
+    args = [*inputs, *outputs]
+    hints = kernel.hints()
+    conv = [_convert(a, h) for a, h in zip(args, hints)]
+    for i in range(int(dim)):
+        _TID[0] = i
+        kernel.fn(*conv)
+
+
+class _Utils:
+    @staticmethod
+    def radix_sort_pairs(keys, values, count):
+        count = int(count)
+        k = keys.data[:count]
+        order = np.argsort(k, kind="stable")
+        keys.data[:count] = k[order]
+        values.data[:count] = values.data[:count][order]
+
+    @staticmethod
+    def array_scan(inp, out, inclusive=True):
+        assert inclusive
+        out.data[:] = np.cumsum(inp.data.astype(np.int64)).astype(np.int32)
+
+
+utils = _Utils()
+
+
+class JaxCallableGraphMode:
+    WARP = "warp"
+    NONE = "none"
+    JAX = "jax"
+
+
+def jax_callable(*_a, **_k):
+    return None
+
+
+# ------------------------------------------------------------------ loading the reference
+class _DivRewriter(ast.NodeTransformer):
+    def visit_BinOp(self, node):
+        self.generic_visit(node)
+        if isinstance(node.op, ast.Div):
+            return ast.copy_location(ast.Call(ast.Name("_wp_div", ast.Load()),
+                                              [node.left, node.right], []), node)
+        return node
+
+
+def _exec_module(name: str, path: Path, pkg_root: Path) -> types.ModuleType:
+    src = path.read_text()
+    tree = _DivRewriter().visit(ast.parse(src, str(path)))
+    ast.fix_missing_locations(tree)
+    mod = types.ModuleType(name)
+    mod.__file__ = str(path)
+    mod.__dict__["_wp_div"] = _wp_div
+    sys.modules[name] = mod
+    exec(compile(tree, str(path), "exec"), mod.__dict__)  # noqa: S102
+    return mod
+
+
+def load_reference(ref_root: Path) -> dict:
+    """Execute the reference's kernel modules, unmodified except that ``/`` dispatches through
+    ``_wp_div``, with this module standing in for ``warp``. The host-side helpers they import
+    from splax._batching (the JAX FFI wrapper factory) and splax._cache (device buffers, recorded
+    launches and the pinned count readback) are replaced by plain CPU equivalents."""
+    this = sys.modules[__name__]
+    sys.modules["warp"] = this
+    for k in [k for k in sys.modules if k == "splax" or k.startswith("splax.")]:
+        del sys.modules[k]
+    for pkg in ("splax", "splax._project", "splax._rasterize", "splax._rasterize._sort"):
+        m = types.ModuleType(pkg)
+        m.__path__ = []
+        sys.modules[pkg] = m
+    batching = types.ModuleType("splax._batching")
+    batching.nested_vmap = lambda *a, **k: None
+    sys.modules["splax._batching"] = batching
+    cache = types.ModuleType("splax._cache")
+
+    def cached_scratch(device, sig, isect_need, bins_need, isect_dtype=int64):
+        np_dt = np.int32 if isect_dtype is int32 else np.int64
+        st = cache.state
+        if st.get("sig") != (sig, isect_dtype):  # a new workload signature drops the entry
+            st.clear()
+            st.update(sig=(sig, isect_dtype),
+                      tile_bins=array(np.zeros((int(bins_need), 2), np.int32), vec2i),
+                      depth_mm=array(np.zeros(2 * sig[0], np.float32), float32),
+                      isect_ids=array(np.zeros(0, np_dt), isect_dtype),
+                      gaussian_ids=array(np.zeros(0, np.int32), int32))
+        if st["isect_ids"].data.size < isect_need:  # only the sort buffers grow
+            st["isect_ids"] = array(np.zeros(int(isect_need), np_dt), isect_dtype)
+            st["gaussian_ids"] = array(np.zeros(int(isect_need), np.int32), int32)
+        return st
+
+    cache.state = {}
+    cache.cached_scratch = cached_scratch
+    cache.cached_launch = lambda k, dim, inputs, device, **kw: launch(k, dim, inputs)
+    cache.begin_count_read = lambda arr, i, device: int(arr[i])
+    cache.fetch_count_read = lambda pending: pending
+    sys.modules["splax._cache"] = cache
+    root = Path(ref_root) / "splax"
+    mods = {}
+    mods["intersect"] = _exec_module("splax._intersect", root / "_intersect.py", root)
+    mods["sort_kernels"] = _exec_module("splax._rasterize._sort._kernels",
+                                        root / "_rasterize" / "_sort" / "_kernels.py", root)
+    mods["sort"] = _exec_module("splax._rasterize._sort._sort",
+                                root / "_rasterize" / "_sort" / "_sort.py", root)
+    mods["project_kernels"] = _exec_module("splax._project._kernels",
+                                           root / "_project" / "_kernels.py", root)
+    return mods
