@@ -20,12 +20,19 @@
  *   projection backward  splax/_project/_kernels.py:356-606
  *
  * Parity pin: warp-lang 1.15.0 and jax 0.11.0 (the reference's pinned runtime) are not
- * installable here, so no output of the reference itself exists to compare with. The
- * restatement is pinned to the reference's own closed-form known-answer tests
- * (tests/test_depth_reg.py:75-107, tests/test_antialiased.py:71-97) and structural
- * invariants (tests/test_warp_rasterize.py:433-487, tests/test_warp_batch.py:102-126), and
- * cross-checked against an independent float64 numpy restatement (tests/golden). Against
- * Warp's fast-math outputs it is "parity unpinned".
+ * installable here. The reference's kernels are Warp-DSL Python, though, and
+ * tests/golden/make_reference_fixtures.py executes them unmodified under a CPU stand-in for
+ * warp's API (tests/golden/warp_standin.py): _project_warp with _project_kernel and the
+ * ellipse walk, sort_and_bin with its key, sort and bin kernels, and _project_bwd_warp. On
+ * those fixtures this restatement reproduces projection, keys, sorted ids and bins bit for bit
+ * and the per-pair projection gradients bit for bit (tests/test_reference_fixtures.py). The
+ * pin holds under the stand-in's builtin semantics (IEEE fp32 without contraction, this
+ * file's logarithm, the standard quaternion matrix), which Warp's own fast-math native code
+ * may differ from by an ulp. The blend kernels use Warp tile primitives that the stand-in does
+ * not run; they are pinned to the reference's known-answer tests (tests/test_depth_reg.py:
+ * 75-107, tests/test_antialiased.py:71-97), invariants (tests/test_warp_rasterize.py:433-487,
+ * tests/test_warp_batch.py:102-126) and an independent float64 numpy restatement
+ * (tests/golden/make_golden.py).
  *
  * Determinism contract shared with the CUDA path: every float operation that feeds an
  * integer output (tile counts, radii, keys, bins) uses IEEE-754 single precision +,-,*,/,sqrt

@@ -80,12 +80,13 @@ def cases():
     out = {}
     m, s, q, o = scene(rng, 3000, 0.6, 0.005, 0.08)
     out["single"] = dict(means=m, scales=s, quats=q, opac=o, views=look(0.2, -0.1, 4.0)[None],
-                         H=200, W=256, f=(220.0, 220.0), c=(128.0, 100.0), key64=False)
+                         H=200, W=256, f=(220.0, 220.0), c=(128.0, 100.0), key64=False,
+                         bwd=True)
     m, s, q, o = scene(rng, 1000, 0.6, 0.005, 0.06)
     views = np.stack([look(0.0, 0.0, 4.0), rotz(0.3, 4.5), look(-0.3, 0.2, 3.5)])
     out["batched32"] = dict(means=m, scales=s, quats=q, opac=o, views=views, H=96, W=144,
-                            f=(120.0, 120.0), c=(72.0, 48.0), key64=False)
-    out["batched64"] = dict(out["batched32"], key64=True)
+                            f=(120.0, 120.0), c=(72.0, 48.0), key64=False, bwd=True)
+    out["batched64"] = dict(out["batched32"], key64=True, bwd=False)
     m, s, q, o = scene(rng, 250, 0.8, 0.1, 0.6, 0.05, 1.0)
     out["large"] = dict(means=m, scales=s, quats=q, opac=o, views=look(0.1, 0.05, 5.0)[None],
                         H=256, W=320, f=(260.0, 260.0), c=(160.0, 128.0), key64=False)
@@ -96,14 +97,14 @@ def cases():
     out["transforms_shared"] = dict(means=m, scales=s, quats=q, opac=o,
                                     views=np.stack([look(0.0, 0.0, 4.0), rotz(-0.2, 4.2)]),
                                     H=96, W=128, f=(110.0, 110.0), c=(64.0, 48.0), key64=False,
-                                    tf=rigid(rng, 2), ids=ids)
+                                    tf=rigid(rng, 2), ids=ids, bwd=True)
     out["transforms_stacked"] = dict(out["transforms_shared"],
                                      tf=np.concatenate([rigid(rng, 2), rigid(rng, 2)]))
     m, s, q, o = scene(rng, 800, 3.0, 0.002, 0.2, 0.0, 1.0)
     m[:20, 2] = -6.0  # behind the camera
     o[20:40] = rng.uniform(0.0, 1.0 / 255.0, size=20).astype(np.float32)  # below threshold
     out["edge"] = dict(means=m, scales=s, quats=q, opac=o, views=look(0.0, 0.0, 4.0)[None],
-                       H=37, W=91, f=(60.0, 60.0), c=(45.5, 18.5), key64=False)
+                       H=37, W=91, f=(60.0, 60.0), c=(45.5, 18.5), key64=False, bwd=True)
     m, s, q, o = scene(rng, 300, 0.7, 0.01, 0.1)
     views = np.stack([rotz(0.25 * k - 0.5, 3.8 + 0.2 * k) for k in range(5)])
     out["five_cameras"] = dict(means=m, scales=s, quats=q, opac=o, views=views, H=40, W=72,
@@ -152,6 +153,27 @@ def run_case(mods, cs, log_kind="atanh"):
     sys.modules["splax._cache"].state.clear()
     gids, bins, count, tbx, ntiles = srt.sort_and_bin(
         xys, depths, radii, conics, arr(cs["opac"], wp.float32), cum, n, B, H, W)
+    if cs.get("bwd", False):
+        # projection backward: _project_bwd_warp (splax/_project/_kernels.py:257-341) with its
+        # tiled kernel (:356-484) and vjps (:487-606), for seeded cotangents of every pair
+        rng = np.random.default_rng(int(total))
+        v_xy = rng.normal(size=(total, 2)).astype(np.float32)
+        v_depth = rng.normal(size=total).astype(np.float32)
+        v_conic = rng.normal(size=(total, 3)).astype(np.float32)
+        grads = dict(v_mean3d=np.zeros((total, 3), np.float32),
+                     v_scale=np.zeros((total, 3), np.float32),
+                     v_quat=np.zeros((total, 4), np.float32),
+                     v_viewmat=np.zeros((4 * B, 4), np.float32),
+                     v_transforms=np.zeros((B * K, 4, 4), np.float32))
+        mods["project_kernels"]._project_bwd_warp(
+            arr(cs["means"], wp.vec3), arr(cs["scales"], wp.vec3), arr(cs["quats"], wp.quat),
+            arr(views.reshape(-1, 4), wp.float32), radii, conics, arr(v_xy, wp.vec2),
+            arr(v_depth, wp.float32), arr(v_conic, wp.vec3), arr(tf, wp.float32),
+            arr(ids, wp.int32), n, K, has_tf, cs["f"][0], cs["f"][1], 1.0,
+            arr(grads["v_mean3d"], wp.vec3), arr(grads["v_scale"], wp.vec3),
+            arr(grads["v_quat"], wp.vec4), arr(grads["v_viewmat"], wp.float32),
+            arr(grads["v_transforms"], wp.float32))
+        outs.update(cot_v_xy=v_xy, cot_v_depth=v_depth, cot_v_conic=v_conic, **grads)
     sorted_keys = sys.modules["splax._cache"].state["isect_ids"].data
     outs.update(gaussian_ids=gids.data[:count].copy(),
                 isect_ids=sorted_keys[:count].astype(np.int64), tile_bins=bins.data.copy(),
@@ -165,7 +187,7 @@ def main(ref_root: str) -> None:
     for name, cs in cases().items():
         t0 = time.time()
         res = run_case(mods, cs)
-        alt = run_case(mods, cs, "libm")
+        alt = run_case(mods, dict(cs, bwd=False), "libm")
         report[name] = {
             "pairs": int(res["radii"].size), "visible": int((res["radii"] > 0).sum()),
             "intersections": int(res["count"]),
@@ -175,6 +197,7 @@ def main(ref_root: str) -> None:
         print(name, report[name], flush=True)
         for k in ("means", "scales", "quats", "opac", "views", "H", "W", "f", "c", "key64"):
             data[f"{name}/{k}"] = np.asarray(cs[k])
+        data[f"{name}/bwd"] = np.asarray(bool(cs.get("bwd", False)))
         if "tf" in cs:
             data[f"{name}/tf"] = cs["tf"]
             data[f"{name}/ids"] = cs["ids"]

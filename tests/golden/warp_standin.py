@@ -39,6 +39,7 @@ from __future__ import annotations
 import ast
 import builtins
 import sys
+import threading
 import types
 import warnings
 from pathlib import Path
@@ -201,8 +202,36 @@ class mat33:
         return mat33(_arr=self.m - o.m)
 
 
+class mat22:
+    def __init__(self, *args, _arr=None):
+        if _arr is not None:
+            self.m = _arr.astype(np.float32)
+        else:
+            assert len(args) == 4
+            self.m = np.array([np.float32(v) for v in args], np.float32).reshape(2, 2)
+
+    def __getitem__(self, ij):
+        return self.m[int(ij[0]), int(ij[1])]
+
+    def __mul__(self, o):
+        assert isinstance(o, mat22)
+        out = np.zeros((2, 2), np.float32)
+        for i in range(2):
+            for j in range(2):
+                out[i, j] = self.m[i, 0] * o.m[0, j] + self.m[i, 1] * o.m[1, j]
+        return mat22(_arr=out)
+
+
 def transpose(m):
-    return mat33(_arr=m.m.T.copy())
+    return type(m)(_arr=m.m.T.copy())
+
+
+def outer(a, b):
+    out = np.zeros((3, 3), np.float32)
+    for i in range(3):
+        for j in range(3):
+            out[i, j] = a[i] * b[j]
+    return mat33(_arr=out)
 
 
 def diag(v):
@@ -272,9 +301,14 @@ array3d = array
 # ------------------------------------------------------------------ builtins
 _TID = [0]
 _LOG = ["atanh"]
+_LOCAL = threading.local()
+_ATOMIC = threading.Lock()
 
 
 def tid():
+    blk = getattr(_LOCAL, "block", None)
+    if blk is not None:  # inside launch_tiled: (block index, thread index in the block)
+        return np.int32(blk), np.int32(_LOCAL.thread)
     return np.int32(_TID[0])
 
 
@@ -354,6 +388,10 @@ def where(c, a, b):
     return a if c else b
 
 
+def _index(idx):
+    return idx[0] if len(idx) == 1 else tuple(idx)
+
+
 def atomic_min(arr, i, v):
     old = arr[i]
     if v < old:
@@ -368,10 +406,55 @@ def atomic_max(arr, i, v):
     return old
 
 
-def atomic_add(arr, i, v):
-    old = arr[i]
-    arr[i] = old + v
+def atomic_add(arr, *idx_v):
+    *idx, v = idx_v
+    with _ATOMIC:
+        old = arr[_index(idx)]
+        arr[_index(idx)] = old + v
     return old
+
+
+# ------------------------------------------------------------------ block tiles
+class _Tile:
+    def __init__(self, vals):
+        self.vals = vals
+
+
+def tile(x):
+    """Every thread of the block contributes its value; all see the whole tile (a barrier)."""
+    blk = _LOCAL.ctx
+    k = _LOCAL.ops
+    _LOCAL.ops = k + 1
+    with blk["lock"]:
+        slot = blk["tiles"].setdefault(k, [None] * blk["dim"])
+    slot[int(_LOCAL.thread)] = x
+    blk["barrier"].wait()
+    return _Tile(slot)
+
+
+def tile_sum(t):
+    acc = type(t.vals[0])(0)
+    for v in t.vals:  # ascending thread order
+        acc = acc + v
+    return _Tile([acc])
+
+
+def tile_min(t):
+    acc = t.vals[0]
+    for v in t.vals[1:]:
+        acc = min(acc, v)
+    return _Tile([acc])
+
+
+def tile_max(t):
+    acc = t.vals[0]
+    for v in t.vals[1:]:
+        acc = max(acc, v)
+    return _Tile([acc])
+
+
+def tile_extract(t, i):
+    return t.vals[int(i)]
 
 
 def _is_int(x):
@@ -474,6 +557,37 @@ def launch(kernel, dim, inputs=(), outputs=(), device=None, **_kw):
     for i in range(int(dim)):
         _TID[0] = i
         kernel.fn(*conv)
+
+
+def launch_tiled(kernel, dim, inputs=(), outputs=(), block_dim=256, device=None, **_kw):
+    """Blocks run one after another; the threads of a block run as host threads that meet at
+    every tile operation (the kernels call them in block-uniform control flow)."""
+    args = [*inputs, *outputs]
+    conv = [_convert(a, h) for a, h in zip(args, kernel.hints())]
+    nblocks = int(dim[0] if isinstance(dim, (list, tuple)) else dim)
+    for b in range(nblocks):
+        ctx = {"dim": int(block_dim), "tiles": {}, "lock": threading.Lock(),
+               "barrier": threading.Barrier(int(block_dim), timeout=60)}
+        errors = []
+
+        def body(t, b=b, ctx=ctx, errors=errors):
+            _LOCAL.block, _LOCAL.thread, _LOCAL.ctx, _LOCAL.ops = b, t, ctx, 0
+            try:
+                kernel.fn(*conv)
+            except BaseException as e:  # noqa: BLE001
+                errors.append(e)
+                ctx["barrier"].abort()
+            finally:
+                _LOCAL.block = None
+
+        threads = [threading.Thread(target=body, args=(t,)) for t in range(int(block_dim))]
+        for th in threads:
+            th.start()
+        for th in threads:
+            th.join()
+        real = [e for e in errors if not isinstance(e, threading.BrokenBarrierError)]
+        if real or errors:
+            raise (real or errors)[0]
 
 
 class _Utils:
