@@ -118,7 +118,67 @@ def cases():
                                    views=look(0.0, 0.0, 4.0)[None], H=64, W=64, f=(60.0, 60.0),
                                    c=(40.0, 40.0), key64=False)
     out["no_intersection"] = dict(out["one_intersection"], means=m + np.float32([0, 0, -9]))
+    # blends: forward (K8 / K9) and backward (K10 staged or K11 warp-aggregated, by the
+    # reference's own launch gate), for seeded colours, backgrounds and image cotangents
+    m, s, q, o = scene(rng, 600, 0.5, 0.01, 0.07, 0.1, 1.0)
+    out["blend_single"] = dict(means=m, scales=s, quats=q, opac=o, views=look(0.1, 0.0, 4.0)[None],
+                               H=64, W=96, f=(90.0, 90.0), c=(48.0, 32.0), key64=False,
+                               blend=dict(depth=False, B_out=1, cot_rows=64, bg_rows=1))
+    m, s, q, o = scene(rng, 400, 0.5, 0.01, 0.07, 0.1, 1.0)
+    out["blend_depth_batched"] = dict(
+        means=m, scales=s, quats=q, opac=o, views=np.stack([look(0.0, 0.0, 4.0), rotz(0.2, 4.3)]),
+        H=48, W=64, f=(70.0, 70.0), c=(32.0, 24.0), key64=False,
+        blend=dict(depth=True, B_out=2, cot_rows=96, bg_rows=2))
+    m, s, q, o = scene(rng, 2500, 0.35, 0.03, 0.12, 0.05, 0.6)
+    out["blend_dense"] = dict(means=m, scales=s, quats=q, opac=o, views=look(0.0, 0.0, 4.0)[None],
+                              H=48, W=48, f=(80.0, 80.0), c=(24.0, 24.0), key64=False,
+                              blend=dict(depth=False, B_out=1, cot_rows=48, bg_rows=1))
+    m, s, q, o = scene(rng, 300, 0.5, 0.01, 0.07, 0.1, 1.0)
+    out["blend_broadcast"] = dict(means=m, scales=s, quats=q, opac=o,
+                                  views=look(0.0, 0.1, 4.0)[None], H=40, W=56, f=(60.0, 60.0),
+                                  c=(28.0, 20.0), key64=False,
+                                  blend=dict(depth=True, B_out=2, cot_rows=40, bg_rows=1))
     return out
+
+
+def run_blend(mods, cs, n, B, H, W, geom):
+    """_rasterize(_depth)_warp and _rasterize_bwd(_depth)_warp (splax/_rasterize/_kernels.py:
+    37-87, 208-262, 386-500, 797-914) on the projected geometry of the case."""
+    bl = cs["blend"]
+    rng = np.random.default_rng(int(n) * 7 + B)
+    colors = rng.uniform(size=(n, 3)).astype(np.float32)
+    bg = rng.uniform(size=(bl["bg_rows"], 3)).astype(np.float32)
+    v_img = rng.uniform(-1, 1, size=(bl["cot_rows"], W, 3)).astype(np.float32)
+    v_dep = rng.uniform(-1, 1, size=(bl["cot_rows"], W)).astype(np.float32)
+    xys, depths, radii, conics, cum = geom
+    rk = mods["raster_kernels"]
+    res = dict(colors=colors, bg=bg, cot_img=v_img,
+               final_Ts=np.zeros((B * H, W), np.float32), final_idx=np.zeros((B * H, W), np.int32),
+               out_img=np.zeros((B * H, W, 3), np.float32))
+    fwd_in = [arr(colors, wp.vec3), arr(cs["opac"], wp.float32), arr(cs["opac"], wp.float32),
+              arr(bg, wp.vec3), xys, depths, radii, conics, cum, n, H, W]
+    fT, fi = arr(res["final_Ts"], wp.float32), arr(res["final_idx"], wp.int32)
+    img = arr(res["out_img"], wp.vec3)
+    if bl["depth"]:
+        res["out_depth"] = np.zeros((B * H, W), np.float32)
+        rk._rasterize_depth_warp(*fwd_in, fT, fi, img, arr(res["out_depth"], wp.float32))
+    else:
+        rk._rasterize_warp(*fwd_in, fT, fi, img)
+    rows = bl["B_out"] * n
+    for k, w in (("v_colors", 3), ("v_opacity", 0), ("v_xy", 2), ("v_conic", 3)):
+        res[k] = np.zeros((rows, w) if w else rows, np.float32)
+    grads = [arr(res["v_colors"], wp.vec3), arr(res["v_opacity"], wp.float32),
+             arr(res["v_xy"], wp.vec2), arr(res["v_conic"], wp.vec3)]
+    bwd_in = [arr(colors, wp.vec3), arr(cs["opac"], wp.float32), arr(cs["opac"], wp.float32),
+              arr(bg, wp.vec3), xys, depths, radii, conics, cum, fT, fi, arr(v_img, wp.vec3)]
+    if bl["depth"]:
+        res["cot_depth"] = v_dep
+        res["v_depths"] = np.zeros(rows, np.float32)
+        rk._rasterize_bwd_depth_warp(*bwd_in, arr(v_dep, wp.float32), n, H, W, *grads,
+                                     arr(res["v_depths"], wp.float32))
+    else:
+        rk._rasterize_bwd_warp(*bwd_in, n, H, W, *grads)
+    return res
 
 
 def arr(a, dt):
@@ -178,7 +238,13 @@ def run_case(mods, cs, log_kind="atanh"):
     outs.update(gaussian_ids=gids.data[:count].copy(),
                 isect_ids=sorted_keys[:count].astype(np.int64), tile_bins=bins.data.copy(),
                 count=np.int64(count), key_bits=np.int32(8 * sorted_keys.itemsize))
+    if cs.get("blend"):
+        ntiles = ((W + 15) // 16) * ((H + 15) // 16)
+        outs["bwd_staged"] = np.bool_(count >= B * ntiles * 256)  # the reference's launch gate
+        outs.update({"blend_" + k: v for k, v in
+                     run_blend(mods, cs, n, B, H, W, (xys, depths, radii, conics, cum)).items()})
     return outs
+
 
 
 def main(ref_root: str) -> None:
@@ -187,7 +253,7 @@ def main(ref_root: str) -> None:
     for name, cs in cases().items():
         t0 = time.time()
         res = run_case(mods, cs)
-        alt = run_case(mods, dict(cs, bwd=False), "libm")
+        alt = run_case(mods, dict(cs, bwd=False, blend=None), "libm")
         report[name] = {
             "pairs": int(res["radii"].size), "visible": int((res["radii"] > 0).sum()),
             "intersections": int(res["count"]),

@@ -38,9 +38,11 @@ from __future__ import annotations
 
 import ast
 import builtins
+import ctypes
+import ctypes.util
 import sys
 import threading
-import types
+import types as _pytypes
 import warnings
 from pathlib import Path
 
@@ -149,6 +151,15 @@ class _Vec:
 def _vec_type(name, n, dt):
     return type(name, (_Vec,), {"_n": n, "_dt": dt})
 
+
+class _Types:
+    @staticmethod
+    def vector(length, dtype):
+        np_dt = np.int32 if dtype is int32 else np.float32
+        return _vec_type(f"vec{int(length)}", int(length), np_dt)
+
+
+types = _Types()
 
 vec2 = _vec_type("vec2", 2, np.float32)
 vec3 = _vec_type("vec3", 3, np.float32)
@@ -356,8 +367,15 @@ def sqrt(x):
     return np.sqrt(np.float32(x))
 
 
+_LIBM = ctypes.CDLL(ctypes.util.find_library("m"))
+_LIBM.expf.restype = ctypes.c_float
+_LIBM.expf.argtypes = [ctypes.c_float]
+
+
 def exp(x):
-    return np.exp(np.float32(x))
+    """The C library's expf (single precision; Warp's fast-math exp is native code absent from
+    the reference tree)."""
+    return np.float32(_LIBM.expf(float(x)))
 
 
 def ceil(x):
@@ -419,12 +437,51 @@ class _Tile:
     def __init__(self, vals):
         self.vals = vals
 
+    def __getitem__(self, i):
+        return self.vals[int(i)]
 
-def tile(x):
-    """Every thread of the block contributes its value; all see the whole tile (a barrier)."""
-    blk = _LOCAL.ctx
+
+def _next_op():
     k = _LOCAL.ops
     _LOCAL.ops = k + 1
+    return _LOCAL.ctx, k
+
+
+def _shared(shape, make):
+    """A block-shared tile: the threads' k-th tile operation returns one common object."""
+    blk, k = _next_op()
+    n = int(shape if not isinstance(shape, (tuple, list)) else shape[0])
+    with blk["lock"]:
+        return blk["tiles"].setdefault(k, _Tile([make() for _ in range(n)]))
+
+
+def tile_empty(shape, dtype=None, storage="shared"):
+    return _shared(shape, lambda: None)
+
+
+def tile_zeros(shape, dtype=None, storage="shared"):
+    return _shared(shape, lambda: dtype(0) if dtype in (int32, float32) else dtype())
+
+
+def tile_scatter_add(t, i, v, mask):
+    """Adds v at i where mask holds, then the block meets (the barrier follows the write)."""
+    blk, _ = _next_op()
+    if mask:
+        with blk["lock"]:
+            t.vals[int(i)] = t.vals[int(i)] + v
+    blk["barrier"].wait()
+
+
+def tile_scatter_masked(t, i, v, mask):
+    blk, _ = _next_op()
+    if mask:
+        t.vals[int(i)] = v
+    blk["barrier"].wait()
+
+
+def tile(x, preserve_type=False):
+    """Every thread of the block contributes its value; all see the whole tile (a barrier)."""
+    blk, k = _next_op()
     with blk["lock"]:
         slot = blk["tiles"].setdefault(k, [None] * blk["dim"])
     slot[int(_LOCAL.thread)] = x
@@ -433,8 +490,8 @@ def tile(x):
 
 
 def tile_sum(t):
-    acc = type(t.vals[0])(0)
-    for v in t.vals:  # ascending thread order
+    acc = t.vals[0]
+    for v in t.vals[1:]:  # ascending thread order
         acc = acc + v
     return _Tile([acc])
 
@@ -628,11 +685,11 @@ class _DivRewriter(ast.NodeTransformer):
         return node
 
 
-def _exec_module(name: str, path: Path, pkg_root: Path) -> types.ModuleType:
+def _exec_module(name: str, path: Path, pkg_root: Path) -> _pytypes.ModuleType:
     src = path.read_text()
     tree = _DivRewriter().visit(ast.parse(src, str(path)))
     ast.fix_missing_locations(tree)
-    mod = types.ModuleType(name)
+    mod = _pytypes.ModuleType(name)
     mod.__file__ = str(path)
     mod.__dict__["_wp_div"] = _wp_div
     sys.modules[name] = mod
@@ -650,13 +707,13 @@ def load_reference(ref_root: Path) -> dict:
     for k in [k for k in sys.modules if k == "splax" or k.startswith("splax.")]:
         del sys.modules[k]
     for pkg in ("splax", "splax._project", "splax._rasterize", "splax._rasterize._sort"):
-        m = types.ModuleType(pkg)
+        m = _pytypes.ModuleType(pkg)
         m.__path__ = []
         sys.modules[pkg] = m
-    batching = types.ModuleType("splax._batching")
+    batching = _pytypes.ModuleType("splax._batching")
     batching.nested_vmap = lambda *a, **k: None
     sys.modules["splax._batching"] = batching
-    cache = types.ModuleType("splax._cache")
+    cache = _pytypes.ModuleType("splax._cache")
 
     def cached_scratch(device, sig, isect_need, bins_need, isect_dtype=int64):
         np_dt = np.int32 if isect_dtype is int32 else np.int64
@@ -675,7 +732,9 @@ def load_reference(ref_root: Path) -> dict:
 
     cache.state = {}
     cache.cached_scratch = cached_scratch
-    cache.cached_launch = lambda k, dim, inputs, device, **kw: launch(k, dim, inputs)
+    cache.cached_launch = lambda k, dim, inputs, device, block_dim=0: (
+        launch_tiled(k, [dim], inputs, block_dim=block_dim) if block_dim else
+        launch(k, dim, inputs))
     cache.begin_count_read = lambda arr, i, device: int(arr[i])
     cache.fetch_count_read = lambda pending: pending
     sys.modules["splax._cache"] = cache
@@ -688,4 +747,7 @@ def load_reference(ref_root: Path) -> dict:
                                 root / "_rasterize" / "_sort" / "_sort.py", root)
     mods["project_kernels"] = _exec_module("splax._project._kernels",
                                            root / "_project" / "_kernels.py", root)
+    sys.modules["splax._rasterize._sort"].sort_and_bin = mods["sort"].sort_and_bin
+    mods["raster_kernels"] = _exec_module("splax._rasterize._kernels",
+                                          root / "_rasterize" / "_kernels.py", root)
     return mods
