@@ -14,6 +14,12 @@
 //
 // The staged conic is pre-scaled (q = -log2(e)/2 * (a, 2b, c)), so the exponent is one ex2;
 // the xy cotangent rescales by -ln 2 to recover the conic.
+//
+// The 0.999 alpha clamp can only act on a gaussian whose opacity is close to 0.999 (2^p <= 1
+// for every entry that takes part). A staged batch without such a record (every batch of most
+// scenes) runs a loop that leaves out the clamp and its mask, with identical results.
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -25,6 +31,9 @@ namespace {
 constexpr int kBwdUnroll = 2;
 
 constexpr float kLn2 = 0.693147180559945f;
+// Below this opacity alpha = opacity * ex2.approx(p) stays under 0.999 for every p <= 0 (the
+// approximation's relative error, about 2^-22, leaves ex2.approx(p) far below 1.001 there).
+constexpr float kClampFreeOpacity = 0.998f;
 
 // Two vertically adjacent pixels of one thread, advanced in lock-step with packed fp32x2 math.
 struct BwdPair {
@@ -48,7 +57,7 @@ struct BwdAcc {
 // alpha 0, leaves T and the colour buffer unchanged and adds exact zeros. The colour buffer
 // is kept as its dot product with v_out, plus the background's share: v_alpha = T (c . v_out)
 // - ra (buf . v_out + t_final bg . v_out), and buf . v_out grows by (c . v_out) fac.
-template <bool DEPTH, bool COUNT>
+template <bool DEPTH, bool COUNT, bool CLAMP>
 __device__ __forceinline__ bool vjp_pair(BwdPair& s, int32_t idx, float2 p, float2 dy,
                                          float2 opac, float2 r, float2 g, float2 b, float2 depth,
                                          BwdAcc& acc, unsigned long long& contribs) {
@@ -60,7 +69,7 @@ __device__ __forceinline__ bool vjp_pair(BwdPair& s, int32_t idx, float2 p, floa
   if constexpr (COUNT) contribs += static_cast<unsigned>(v0) + static_cast<unsigned>(v1);
   // ov of the pixels that take part (0 elsewhere): alpha and the unclamped mask follow from it
   const float2 ovv = make_float2(v0 ? ov.x : 0.0f, v1 ? ov.y : 0.0f);
-  const float2 am = make_float2(fminf(kAlphaMax, ovv.x), fminf(kAlphaMax, ovv.y));
+  const float2 am = CLAMP ? make_float2(fminf(kAlphaMax, ovv.x), fminf(kAlphaMax, ovv.y)) : ovv;
   const float2 om = one_minus2(am);
   const float2 ra = make_float2(__fdividef(1.0f, om.x), __fdividef(1.0f, om.y));
   // a pixel that does not take part has am = 0, om = 1 and ra = rcp.approx(1) = 1 exactly
@@ -81,8 +90,9 @@ __device__ __forceinline__ bool vjp_pair(BwdPair& s, int32_t idx, float2 p, floa
   const float2 va = fma2(s.T, cv, make_float2(-rb.x, -rb.y));
   s.behind = fma2(cv, fac, s.behind);
   // where the 0.999 clamp is active alpha is constant: no sigma or opacity cotangent
-  const float2 ovm = make_float2(ovv.x <= kAlphaMax ? ovv.x : 0.0f,
-                                 ovv.y <= kAlphaMax ? ovv.y : 0.0f);
+  const float2 ovm = CLAMP ? make_float2(ovv.x <= kAlphaMax ? ovv.x : 0.0f,
+                                         ovv.y <= kAlphaMax ? ovv.y : 0.0f)
+                          : ovv;
   const float2 w = mul2(ovm, va);
   acc.w = add2(acc.w, w);
   const float2 wy = mul2(w, dy);
@@ -198,6 +208,7 @@ raster_bwd_kernel(RasterBwdArgs a) {
   for (int32_t bt = 0; bt < num_batches; ++bt) {
     __syncthreads();  // previous batch's shared reads are complete
     const int32_t batch_end = start_idx - bt * kBlockSize;
+    bool high_opacity = false;
 #pragma unroll
     for (int h = 0; h < kBlockSize / kBwdThreads; ++h) {
       const int slot = tr + h * kBwdThreads;
@@ -207,7 +218,9 @@ raster_bwd_kernel(RasterBwdArgs a) {
         if (g >= 0 && g < a.num_records) {
           const float4* rec = a.records + kRecordFloat4 * static_cast<int64_t>(g);
           s_r0[slot] = rec[0];
-          s_r1[slot] = rec[1];
+          const float4 r1 = rec[1];
+          s_r1[slot] = r1;
+          high_opacity |= r1.y > kClampFreeOpacity;
           const float4 r2 = rec[2];
           s_r2[slot] = make_float2(r2.x, r2.y);
           s_id[slot] = g;
@@ -219,10 +232,13 @@ raster_bwd_kernel(RasterBwdArgs a) {
         }
       }
     }
-    __syncthreads();
+    // the barrier publishing the batch also tells every lane whether it needs the clamp
+    const bool clamp = __syncthreads_or(high_opacity) != 0;
     const int32_t batch_size = min(kBlockSize, batch_end - range_start + 1);
     // entries above every pixel of the tile are skipped as a whole
     const int32_t t_begin = max(0, batch_end - wmax);
+    auto walk_batch = [&](auto clamp_tag) {
+      constexpr bool kClamp = decltype(clamp_tag)::value;
 #pragma unroll kBwdUnroll
     for (int32_t t = t_begin; t < batch_size; ++t) {
       const int32_t idx = batch_end - t;
@@ -247,7 +263,8 @@ raster_bwd_kernel(RasterBwdArgs a) {
       for (int q = 0; q < kPairs; ++q) {
         const float2 dy = add2(splat2(dy0), make_float2(-2.0f * q, -2.0f * q - 1.0f));
         const float2 p = fma2(fma2(qc, dy, qbx), dy, qxx);
-        any |= vjp_pair<DEPTH, COUNT>(pr[q], idx, p, dy, opac, cr, cg, cb, cd, acc, contribs);
+        any |= vjp_pair<DEPTH, COUNT, kClamp>(pr[q], idx, p, dy, opac, cr, cg, cb, cd, acc,
+                                              contribs);
       }
       if (__ballot_sync(0xffffffffu, any) == 0u) continue;
       if constexpr (COUNT) ++steps_active;
@@ -272,6 +289,9 @@ raster_bwd_kernel(RasterBwdArgs a) {
         atomicAdd(my_base + (s_id[t] + my_add) * my_stride, v[0]);
       }
     }
+    };
+    if (clamp) walk_batch(std::true_type{});
+    else walk_batch(std::false_type{});
   }
   if constexpr (COUNT) {
     evals = __reduce_add_sync(0xffffffffu, static_cast<unsigned>(evals));

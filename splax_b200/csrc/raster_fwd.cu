@@ -14,6 +14,13 @@
 //
 // Pixel semantics are the reference's: a gaussian is skipped when sigma < 0 (exponent > 0) or
 // alpha < 1/255, and the walk stops before the gaussian that would take T to <= 1e-4.
+//
+// The alpha clamp min(0.999, opacity * 2^p) can only act on a gaussian whose opacity is close
+// to 0.999, since 2^p <= 1 for every gaussian that is not skipped (p <= 0). Each staged batch
+// notes whether any of its records has an opacity above kClampFreeOpacity; batches without one
+// (all of them for most scenes) run a loop without the clamp, whose results are identical.
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -22,6 +29,10 @@ namespace {
 // the record loop unrolled by two: the next record's exponents overlap this one's blend
 // (1.84 -> 1.76 ms; by four: 1.79)
 constexpr int kFwdUnroll = 2;
+// Below this opacity alpha = opacity * ex2.approx(p) stays under 0.999 for every p <= 0 (the
+// approximation's relative error, about 2^-22, leaves ex2.approx(p) far below 1.001 there), so
+// min(0.999, alpha) == alpha exactly.
+constexpr float kClampFreeOpacity = 0.998f;
 
 
 struct PixelState {
@@ -31,7 +42,7 @@ struct PixelState {
 };
 
 // The reference blend step (splax/_rasterize/_kernels.py:185-197) for one pixel.
-template <bool DEPTH, bool COUNT>
+template <bool DEPTH, bool COUNT, bool CLAMP>
 __device__ __forceinline__ void blend_one(PixelState& s, float p, float opac, float r, float g,
                                           float b, float depth, int32_t idx,
                                           unsigned long long& evals,
@@ -41,7 +52,7 @@ __device__ __forceinline__ void blend_one(PixelState& s, float p, float opac, fl
   const float ov = opac * ex2_approx(p);
   // min(0.999, ov) < 1/255 exactly when ov < 1/255
   if (s.done || p > 0.0f || ov < kAlphaThreshold) return;
-  const float alpha = fminf(kAlphaMax, ov);
+  const float alpha = CLAMP ? fminf(kAlphaMax, ov) : ov;
   const float next_T = s.T * (1.0f - alpha);
   if (next_T <= kTransmittanceMin) {
     s.done = true;
@@ -93,6 +104,7 @@ raster_fwd_kernel(RasterFwdArgs a) {
     // block vote doubles as the barrier protecting the previous batch's shared reads
     if (__syncthreads_count(all_done) >= kFwdThreads) break;
     const int32_t batch_start = range_start + bt * kBlockSize;
+    bool high_opacity = false;
 #pragma unroll
     for (int h = 0; h < kBlockSize / kFwdThreads; ++h) {
       const int slot = tr + h * kFwdThreads;
@@ -102,7 +114,9 @@ raster_fwd_kernel(RasterFwdArgs a) {
         if (g >= 0 && g < a.num_records) {
           const float4* rec = a.records + kRecordFloat4 * g;
           s_r0[slot] = rec[0];
-          s_r1[slot] = rec[1];
+          const float4 r1 = rec[1];
+          s_r1[slot] = r1;
+          high_opacity |= r1.y > kClampFreeOpacity;
           const float4 r2 = rec[2];
           s_r2[slot] = make_float2(r2.x, r2.y);
         } else {  // only after a reported emission error: stage a transparent record
@@ -112,9 +126,11 @@ raster_fwd_kernel(RasterFwdArgs a) {
         }
       }
     }
-    __syncthreads();
+    // the barrier publishing the batch also tells every thread whether it needs the clamp
+    const bool clamp = __syncthreads_or(high_opacity) != 0;
     const int32_t batch_size = min(kBlockSize, range_end - batch_start);
-    if (!all_done) {
+    auto blend_batch = [&](auto clamp_tag) {
+      constexpr bool kClamp = decltype(clamp_tag)::value;
 #pragma unroll kFwdUnroll
       for (int32_t t = 0; t < batch_size; ++t) {
         const float4 r0 = s_r0[t];  // x, y, qa, qb  (q = -log2(e)/2 * (a, 2b, c))
@@ -130,14 +146,18 @@ raster_fwd_kernel(RasterFwdArgs a) {
           // the exponents of a pixel pair in packed form, then the branchy per-pixel step
           const float2 dy = add2(splat2(dy0), make_float2(-2.0f * q, -2.0f * q - 1.0f));
           const float2 p = fma2(fma2(qc, dy, qbx), dy, qxx);
-          blend_one<DEPTH, COUNT>(st[2 * q], p.x, r1.y, r1.z, r1.w, r2.x, r2.y, idx, evals,
-                                  contribs);
-          blend_one<DEPTH, COUNT>(st[2 * q + 1], p.y, r1.y, r1.z, r1.w, r2.x, r2.y, idx, evals,
-                                  contribs);
+          blend_one<DEPTH, COUNT, kClamp>(st[2 * q], p.x, r1.y, r1.z, r1.w, r2.x, r2.y, idx,
+                                          evals, contribs);
+          blend_one<DEPTH, COUNT, kClamp>(st[2 * q + 1], p.y, r1.y, r1.z, r1.w, r2.x, r2.y, idx,
+                                          evals, contribs);
           all_done &= st[2 * q].done && st[2 * q + 1].done;
         }
         if (all_done) break;
       }
+    };
+    if (!all_done) {
+      if (clamp) blend_batch(std::true_type{});
+      else blend_batch(std::false_type{});
     }
   }
   if constexpr (COUNT) {
