@@ -49,6 +49,8 @@ FWD_BWD = {
         "5 param arrays + viewmats", dict(viewmat_grad=True, antialiased=True)),
 }
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+NCCL_LABEL = ("nccl: two all-reduces, the colour and opacity gradients' overlapped with the "
+              "projection backward")
 L2_BYTES = 126 << 20
 # algorithmic work per unit: FLOPs per blend evaluation / contribution (FMA = 2), restated from
 # the reference blend loop (splax/_rasterize/_kernels.py:185-197) and vjp (:1235-1253)
@@ -68,6 +70,9 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="splax_b200", choices=["splax_b200", "reference"])
     ap.add_argument("--n", type=int, default=None, help="override the gaussian count (debug)")
+    ap.add_argument("--cams", type=int, default=None,
+                    help="render only the first K cameras of the configuration (debug: one "
+                         "rank's share of a sharded run on one GPU)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--collective", default="nccl", choices=["nccl", "nvls", "auto"],
                     help="gradient all-reduce for N>1: NCCL (default; 'auto' is the same), or "
@@ -260,7 +265,7 @@ def reference_arm(args) -> None:
               f"{'forward' if fwd_only else 'fwd+bwd'}), C oracle with {threads} threads")
     input_bytes = 4 * (14 * n + per * H * W * 3)
     collective = None if world == 1 else ("nvls (library kernel)" if args.collective == "nvls"
-                                          else "nccl")
+                                          else NCCL_LABEL)
     line = {
         "impl": "reference", "metric": metric, "value": value, "unit": "frames/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -316,6 +321,68 @@ def teardown(world: int, closers: list) -> None:
             dist.barrier()
     finally:
         dist.destroy_process_group()
+
+
+class SplitAllReduce:
+    """NCCL gradient exchange in two parts. The colour and opacity gradients are final once the
+    rasterize backward has run: a hook on their accumulation starts their all-reduce on NCCL's
+    stream while the projection backward computes the means / scales / quats gradients, which
+    follow, with the loss, in a second all-reduce. Every rank issues the two collectives in the
+    same order (the early one first), whether or not its hook fired."""
+
+    def __init__(self, params, early):
+        self.params = list(params)
+        self.early = list(early)
+        self.rest = [k for k in range(len(self.params)) if k not in self.early]
+        self.ready: set = set()
+        self.work = None
+        self.flat_early = None
+        self.armed = False
+        for k in self.early:
+            self.params[k].register_post_accumulate_grad_hook(self._hook(k))
+
+    def _hook(self, k):
+        def hook(p):
+            if not self.armed:
+                return
+            self.ready.add(k)
+            if len(self.ready) == len(self.early) and self.work is None:
+                self._start_early()
+        return hook
+
+    def _start_early(self):
+        import torch
+        import torch.distributed as dist
+
+        self.flat_early = torch.cat([self.params[k].grad.reshape(-1) for k in self.early])
+        self.work = dist.all_reduce(self.flat_early, async_op=True)
+
+    def arm(self):
+        self.ready.clear()
+        self.work = None
+        self.armed = True
+
+    def finish(self, loss):
+        """Second all-reduce, then p.grad becomes a view of the summed buffers; returns the summed
+        loss."""
+        import torch
+        import torch.distributed as dist
+
+        self.armed = False
+        if self.work is None:
+            self._start_early()
+        flat = torch.cat([self.params[k].grad.reshape(-1) for k in self.rest] +
+                         [loss.detach().reshape(1)])
+        dist.all_reduce(flat)
+        self.work.wait()
+        for bufs, idx in ((self.flat_early, self.early), (flat, self.rest)):
+            o = 0
+            for k in idx:
+                p = self.params[k]
+                p.grad = bufs[o:o + p.numel()].view_as(p)
+                o += p.numel()
+        self.work = None
+        return flat[-1].reshape(())
 
 
 def reduce_grads(reducer, params, loss, dev):
@@ -502,6 +569,10 @@ def main() -> None:
             metric = metric.replace("fwd+bwd", "forward")
             workload += " (forward render only)"
         scene = utils.synthetic_scene(args.config, n=args.n)
+        if args.cams:
+            scene["viewmats"] = scene["viewmats"][:args.cams]
+            scene["B"] = int(scene["viewmats"].shape[0])
+            workload += f" (debug: first {scene['B']} cameras only)"
         B, H, W, f = scene["B"], scene["H"], scene["W"], scene["f"]
         n = scene["means"].shape[0]
         if B % world:
@@ -521,6 +592,9 @@ def main() -> None:
         reducer = None if opts.get("forward_only") else make_reducer(args, params, dev, world)
         if reducer is not None:
             closers.append(reducer)
+        # NCCL: colours and opacities (params 3, 4) are summed while the projection backward runs
+        split = (SplitAllReduce(params, early=(3, 4))
+                 if world > 1 and reducer is None and not opts.get("forward_only") else None)
 
         def step(vm, tgt, ps=params, tgt_ready=None):
             """One step; returns the rendered images (forward only) or the loss. tgt_ready: an
@@ -537,7 +611,11 @@ def main() -> None:
             if tgt_ready is not None:
                 torch.cuda.current_stream(dev).wait_event(tgt_ready)
             loss = sx.mse_loss(imgs, tgt, denom=denom)
+            if split is not None:
+                split.arm()
             loss.backward()
+            if split is not None:  # the second half of the NCCL exchange (the first overlapped)
+                return split.finish(loss)
             if world > 1:  # the gradients of the shared gaussians (and the loss) summed over ranks
                 loss = reduce_grads(reducer, ps, loss, dev)
             return loss
@@ -779,7 +857,8 @@ def main() -> None:
                 "data": f"synthetic (seeded, config {args.config} distributions)",
                 "config": arm_config(workload, n, per, world, input_bytes, flush,
                                      None if world == 1 else
-                                     ("nvls (library kernel)" if reducer is not None else "nccl")),
+                                     ("nvls (library kernel)" if reducer is not None
+                                      else NCCL_LABEL)),
                 "roofline": roof,
                 "kernels": {k: {**v, "share": v["ms"] / max(sum(total_ms.values()), 1e-9)}
                             for k, v in kern.items()},

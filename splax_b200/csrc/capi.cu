@@ -400,6 +400,84 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
                              cudaMemcpyDeviceToHost, stream));
   SPLAX_CUDA(cudaEventRecord(st.ev, stream));
   SPLAX_CUDA(cudaMemsetAsync(st.tile_bins.p, 0, sizeof(int2) * bins_len, stream));
+
+  SortScratch ss;
+  ss.hist = static_cast<uint32_t*>(st.hist.p);
+  ss.tile_counters = st.sort_counters();
+  ss.err = st.err_word();
+  int32_t* offsets = static_cast<int32_t*>(st.poffs.p);
+  const int32_t* perm = nullptr;
+  int pair_bits = 0;
+  bool pair64 = false;
+  // 1. pairs in (image, depth key) order. Nothing here depends on the intersection count, so
+  // with packed keys (the key layout known on the host) this stage is queued before the host
+  // waits for the count and keeps the GPU busy across that wait.
+  auto pair_stage = [&](int key_shift) -> int {
+    pair_bits = image_n_bits + key_shift;
+    // 64-bit pair keys from 32 significant bits: the all-ones key marks pairs left out
+    pair64 = pair_bits > 31;
+    const int64_t t_pairs = (total + sort_tile_items(pair64) - 1) / sort_tile_items(pair64);
+    const size_t need = sizeof(unsigned long long) * kRadixMaxDigits * t_pairs;
+    if (st.status.bytes < need) {
+      SPLAX_CUDA(cudaStreamSynchronize(stream));
+      cudaError_t e = buf_reserve(st.status, need);
+      if (e != cudaSuccess) {
+        st.drop_entry();
+        return cuda_fail(e, "sort look-back allocation");
+      }
+    }
+    ss.status = static_cast<unsigned long long*>(st.status.p);
+    ss.status_words = static_cast<int64_t>(st.status.bytes / sizeof(unsigned long long));
+    PairKeyArgs pa;
+    pa.depths = in.depths;
+    pa.radii = in.radii;
+    pa.depth_mm = depth_mm;
+    pa.n = in.n;
+    pa.total = total;
+    pa.packed = packed;
+    pa.depth_bits = depth_bits;
+    pa.key_shift = key_shift;
+    pa.err = st.err_word();
+    pa.xys = in.xys;
+    pa.conics = in.conics;
+    pa.cum = in.cum;
+    pa.map_opacities = in.map_opacities;
+    pa.map_opac_rows = in.map_rows;
+    pa.opacities = in.opacities;
+    pa.opac_rows = in.opac_rows;
+    pa.colors = in.colors;
+    pa.color_rows = in.color_rows;
+    pa.counts = static_cast<int32_t*>(st.counts.p);
+    pa.walk = static_cast<float4*>(st.walk.p);
+    pa.records = in.colors ? static_cast<float4*>(st.records.p) : nullptr;
+    st.timer.begin(kPairKeys, 1, stream);
+    launch_pair_keys(pa, pair64, st.pkeys[0].p, static_cast<int32_t*>(st.pvals[0].p), stream);
+    st.timer.end(stream);
+    ss.keys[0] = st.pkeys[0].p;
+    ss.keys[1] = st.pkeys[1].p;
+    ss.vals[0] = static_cast<int32_t*>(st.pvals[0].p);
+    ss.vals[1] = static_cast<int32_t*>(st.pvals[1].p);
+    const int pair_passes = radix_passes(pair_bits);
+    st.timer.begin(kPairSort, total > 1 && pair_passes ? 2 + pair_passes : 0, stream);
+    // only the V pairs that hit a tile are sorted; V stays on the device
+    ss.filter_sentinel = true;
+    ss.vcount = st.vis_word();
+    const int pfin = radix_sort_pairs(ss, pair64, total, pair_bits, stream);
+    ss.filter_sentinel = false;
+    ss.vcount = nullptr;
+    st.timer.end(stream);
+    perm = ss.vals[pfin];
+    st.timer.begin(kPairScan, 1, stream);
+    launch_sorted_offsets(perm, static_cast<const int32_t*>(st.counts.p), total, st.vis_word(),
+                          offsets, static_cast<unsigned long long*>(st.scan_status.p),
+                          st.scan_ticket(), st.err_word(), stream);
+    st.timer.end(stream);
+    return SPLAX_OK;
+  };
+  if (packed) {
+    rc = pair_stage(depth_bits);
+    if (rc) return rc;
+  }
   SPLAX_CUDA(cudaEventSynchronize(st.ev));
   const unsigned werr = static_cast<unsigned>(st.pinned[1]);
   if (werr) return report_device_error(st, werr, stream);
@@ -408,11 +486,6 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
     return fail(SPLAX_ERR_COUNT_OVERFLOW,
                 "cum_tiles_hit[-1] is negative: the intersection count overflowed int32");
   const int kb = packed ? 32 : 64;
-  // pair key: image id above the depth key
-  const int key_shift = packed ? depth_bits : bit_length(static_cast<uint32_t>(st.pinned[2]));
-  const int pair_bits = image_n_bits + key_shift;
-  // 64-bit pair keys from 32 significant bits: the all-ones key marks pairs left out
-  const bool pair64 = pair_bits > 31;
   const int bin_bits = upper;
   if (st.isect_cap < count) {
     const int64_t cap = std::max<int64_t>(static_cast<int64_t>(count * kScratchHeadroom) + 1,
@@ -429,21 +502,6 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
       return cuda_fail(e, "sort scratch allocation");
     }
     st.isect_cap = cap;
-  }
-  {
-    // look-back words for the larger of the two sorts
-    const int64_t t_pairs = (total + sort_tile_items(pair64) - 1) / sort_tile_items(pair64);
-    const int64_t t_bins = (st.isect_cap + sort_tile_items(false) - 1) / sort_tile_items(false);
-    const size_t need =
-        sizeof(unsigned long long) * kRadixMaxDigits * std::max(t_pairs, t_bins);
-    if (st.status.bytes < need) {
-      SPLAX_CUDA(cudaStreamSynchronize(stream));
-      cudaError_t e = buf_reserve(st.status, need);
-      if (e != cudaSuccess) {
-        st.drop_entry();
-        return cuda_fail(e, "sort look-back allocation");
-      }
-    }
   }
   st.key_bits = kb;
   out.tbx = tbx;
@@ -465,60 +523,26 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
     st.last_out = out;
     return SPLAX_OK;
   }
-
-  SortScratch ss;
-  ss.hist = static_cast<uint32_t*>(st.hist.p);
-  ss.status = static_cast<unsigned long long*>(st.status.p);
-  ss.status_words = static_cast<int64_t>(st.status.bytes / sizeof(unsigned long long));
-  ss.tile_counters = st.sort_counters();
-  ss.err = st.err_word();
-
-  // 1. pairs in (image, depth key) order
-  PairKeyArgs pa;
-  pa.depths = in.depths;
-  pa.radii = in.radii;
-  pa.depth_mm = depth_mm;
-  pa.n = in.n;
-  pa.total = total;
-  pa.packed = packed;
-  pa.depth_bits = depth_bits;
-  pa.key_shift = key_shift;
-  pa.err = st.err_word();
-  pa.xys = in.xys;
-  pa.conics = in.conics;
-  pa.cum = in.cum;
-  pa.map_opacities = in.map_opacities;
-  pa.map_opac_rows = in.map_rows;
-  pa.opacities = in.opacities;
-  pa.opac_rows = in.opac_rows;
-  pa.colors = in.colors;
-  pa.color_rows = in.color_rows;
-  pa.counts = static_cast<int32_t*>(st.counts.p);
-  pa.walk = static_cast<float4*>(st.walk.p);
-  pa.records = in.colors ? static_cast<float4*>(st.records.p) : nullptr;
-  st.timer.begin(kPairKeys, 1, stream);
-  launch_pair_keys(pa, pair64, st.pkeys[0].p, static_cast<int32_t*>(st.pvals[0].p), stream);
-  st.timer.end(stream);
-  ss.keys[0] = st.pkeys[0].p;
-  ss.keys[1] = st.pkeys[1].p;
-  ss.vals[0] = static_cast<int32_t*>(st.pvals[0].p);
-  ss.vals[1] = static_cast<int32_t*>(st.pvals[1].p);
-  const int pair_passes = radix_passes(pair_bits);
-  st.timer.begin(kPairSort, total > 1 && pair_passes ? 2 + pair_passes : 0, stream);
-  // only the V pairs that hit a tile are sorted; V stays on the device
-  ss.filter_sentinel = true;
-  ss.vcount = st.vis_word();
-  const int pfin = radix_sort_pairs(ss, pair64, total, pair_bits, stream);
-  ss.filter_sentinel = false;
-  ss.vcount = nullptr;
-  st.timer.end(stream);
-  const int32_t* perm = ss.vals[pfin];
-  int32_t* offsets = static_cast<int32_t*>(st.poffs.p);
-  st.timer.begin(kPairScan, 1, stream);
-  launch_sorted_offsets(perm, static_cast<const int32_t*>(st.counts.p), total, st.vis_word(),
-                        offsets, static_cast<unsigned long long*>(st.scan_status.p),
-                        st.scan_ticket(), st.err_word(), stream);
-  st.timer.end(stream);
+  if (!packed) {
+    // wide keys: the pair key's depth field is as wide as the largest per-image span
+    rc = pair_stage(bit_length(static_cast<uint32_t>(st.pinned[2])));
+    if (rc) return rc;
+  }
+  {
+    // look-back words of the intersection sort
+    const int64_t t_bins = (st.isect_cap + sort_tile_items(false) - 1) / sort_tile_items(false);
+    const size_t need = sizeof(unsigned long long) * kRadixMaxDigits * t_bins;
+    if (st.status.bytes < need) {
+      SPLAX_CUDA(cudaStreamSynchronize(stream));
+      cudaError_t e = buf_reserve(st.status, need);
+      if (e != cudaSuccess) {
+        st.drop_entry();
+        return cuda_fail(e, "sort look-back allocation");
+      }
+      ss.status = static_cast<unsigned long long*>(st.status.p);
+      ss.status_words = static_cast<int64_t>(st.status.bytes / sizeof(unsigned long long));
+    }
+  }
 
   // 2. emission in pair order: (image | tile) keys, flat ids, blend records
   EmitArgs ea;
@@ -570,7 +594,7 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
   }
   st.units.pairs_sorted += sorted_pairs;
   st.units.pair_key_bytes += sorted_pairs * (pair64 ? 8 : 4);
-  st.units.pair_pass_keys += sorted_pairs > 1 ? sorted_pairs * pair_passes : 0;
+  st.units.pair_pass_keys += sorted_pairs > 1 ? sorted_pairs * radix_passes(pair_bits) : 0;
   st.last_valid = true;
   st.last_gen = st.sort_gen;
   st.last_in = in;

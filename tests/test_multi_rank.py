@@ -106,3 +106,53 @@ def test_missing_rank_fails_the_collective(tmp_path):
         pass
     outcome = (tmp_path / "outcome.txt").read_text()
     assert outcome.startswith("error"), outcome
+
+
+def _split_worker(rank, world, port, out_dir):
+    """bench.py's SplitAllReduce on CPU tensors: the hook-started all-reduce of params 3 and 4
+    and the closing one of the rest and the loss must give the summed gradients and loss."""
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, str(ROOT))
+    from bench import SplitAllReduce
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=20))
+    shapes = [(7, 3), (7, 3), (7, 4), (7, 3), (7,)]
+    params = [torch.zeros(s, dtype=torch.float64, requires_grad=True) for s in shapes]
+    split = SplitAllReduce(params, early=(3, 4))
+    results = []
+    for step in range(2):  # two steps: the hooks re-arm
+        for p in params:
+            p.grad = None
+        g = torch.Generator().manual_seed(100 * rank + step)
+        w = [torch.randn(s, generator=g, dtype=torch.float64) for s in shapes]
+        loss = sum((p * wk).sum() for p, wk in zip(params, w)) + float(rank + 1)
+        split.arm()
+        loss.backward()
+        total = split.finish(loss)
+        results.append([p.grad.clone() for p in params] + [total.detach().reshape(1)])
+    torch.save(results, Path(out_dir) / f"split_{rank}.pt")
+    dist.destroy_process_group()
+
+
+def test_split_all_reduce_sums_gradients_and_loss(tmp_path):
+    import torch
+
+    port = _free_port()
+    mp.start_processes(_split_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    r0 = torch.load(tmp_path / "split_0.pt")
+    r1 = torch.load(tmp_path / "split_1.pt")
+    shapes = [(7, 3), (7, 3), (7, 4), (7, 3), (7,)]
+    for step in range(2):
+        exp = [torch.zeros(s, dtype=torch.float64) for s in shapes]
+        for rank in range(2):
+            g = torch.Generator().manual_seed(100 * rank + step)
+            w = [torch.randn(s, generator=g, dtype=torch.float64) for s in shapes]
+            for k in range(5):
+                exp[k] += w[k]
+        for k in range(5):
+            assert torch.allclose(r0[step][k], exp[k]) and torch.equal(r0[step][k], r1[step][k])
+        assert float(r0[step][5]) == float(r1[step][5])
