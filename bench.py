@@ -49,8 +49,9 @@ FWD_BWD = {
         "5 param arrays + viewmats", dict(viewmat_grad=True, antialiased=True)),
 }
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
-NCCL_LABEL = ("nccl: two all-reduces, the colour and opacity gradients' overlapped with the "
-              "projection backward")
+NCCL_LABEL = "nccl: one all-reduce of the gradients and the loss"
+NCCL_SPLIT_LABEL = ("nccl: two all-reduces, the colour and opacity gradients' overlapped with "
+                    "the projection backward")
 L2_BYTES = 126 << 20
 # algorithmic work per unit: FLOPs per blend evaluation / contribution (FMA = 2), restated from
 # the reference blend loop (splax/_rasterize/_kernels.py:185-197) and vjp (:1235-1253)
@@ -70,6 +71,9 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="splax_b200", choices=["splax_b200", "reference"])
     ap.add_argument("--n", type=int, default=None, help="override the gaussian count (debug)")
+    ap.add_argument("--overlap", action="store_true",
+                    help="N>1 with NCCL: two all-reduces, the colour / opacity part started "
+                         "while the projection backward runs, instead of one after the backward")
     ap.add_argument("--cams", type=int, default=None,
                     help="render only the first K cameras of the configuration (debug: one "
                          "rank's share of a sharded run on one GPU)")
@@ -265,6 +269,7 @@ def reference_arm(args) -> None:
               f"{'forward' if fwd_only else 'fwd+bwd'}), C oracle with {threads} threads")
     input_bytes = 4 * (14 * n + per * H * W * 3)
     collective = None if world == 1 else ("nvls (library kernel)" if args.collective == "nvls"
+                                          else NCCL_SPLIT_LABEL if args.overlap
                                           else NCCL_LABEL)
     line = {
         "impl": "reference", "metric": metric, "value": value, "unit": "frames/s",
@@ -592,9 +597,10 @@ def main() -> None:
         reducer = None if opts.get("forward_only") else make_reducer(args, params, dev, world)
         if reducer is not None:
             closers.append(reducer)
-        # NCCL: colours and opacities (params 3, 4) are summed while the projection backward runs
+        # --overlap: colours and opacities (params 3, 4) summed while the projection backward runs
         split = (SplitAllReduce(params, early=(3, 4))
-                 if world > 1 and reducer is None and not opts.get("forward_only") else None)
+                 if world > 1 and reducer is None and not opts.get("forward_only")
+                 and args.overlap else None)
 
         def step(vm, tgt, ps=params, tgt_ready=None):
             """One step; returns the rendered images (forward only) or the loss. tgt_ready: an
@@ -675,6 +681,28 @@ def main() -> None:
             dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
         ms = float(ms_t.item())
         value = B * args.steps / (ms / 1e3)
+
+        # the exchange alone, outside the timed region: one all-reduce of the step's gradient
+        # and loss floats (CUDA events on the launching stream, max over ranks)
+        exchange = None
+        if world > 1 and reducer is None and not opts.get("forward_only"):
+            buf = torch.ones(sum(p.numel() for p in params) + 1, device=dev)
+            for _ in range(3):
+                dist.all_reduce(buf)
+            xe = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(10)]
+            torch.cuda.synchronize()
+            for a0, a1 in xe:
+                a0.record()
+                dist.all_reduce(buf)
+                a1.record()
+            torch.cuda.synchronize()
+            x_t = torch.tensor([statistics.median(a0.elapsed_time(a1) for a0, a1 in xe)],
+                               device=dev, dtype=torch.float64)
+            dist.all_reduce(x_t, op=dist.ReduceOp.MAX)
+            exchange = {"bytes": int(4 * buf.numel()), "allreduce_ms": float(x_t.item()),
+                        "how": "median of 10 back-to-back NCCL all-reduces, max over ranks"}
+            del buf
 
         # one instrumented step outside the timed region: exact work units per step
         _lib.profile_enable(timing=False, count_work=True)
@@ -858,6 +886,7 @@ def main() -> None:
                 "config": arm_config(workload, n, per, world, input_bytes, flush,
                                      None if world == 1 else
                                      ("nvls (library kernel)" if reducer is not None
+                                      else NCCL_SPLIT_LABEL if split is not None
                                       else NCCL_LABEL)),
                 "roofline": roof,
                 "kernels": {k: {**v, "share": v["ms"] / max(sum(total_ms.values()), 1e-9)}
@@ -865,6 +894,10 @@ def main() -> None:
                 "kernel_rooflines": rows,
                 "work_per_step": work,
                 "clocks": clocks,
+                "exchange": exchange,
+                "host": {"cpus": os.cpu_count(),
+                         "cpus_usable": len(os.sched_getaffinity(0))
+                         if hasattr(os, "sched_getaffinity") else None},
                 "e2e": e2e,
                 "cpu_baseline": cpu,
                 "gpu_launches": int(launches),
