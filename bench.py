@@ -57,7 +57,7 @@ L2_BYTES = 126 << 20
 # the reference blend loop (splax/_rasterize/_kernels.py:185-197) and vjp (:1235-1253)
 # DRAM bytes (read + write) per launch of the full config-2 workload from single-pass ncu
 # captures (dram__bytes_read.sum + dram__bytes_write.sum)
-TRAFFIC_BYTES_PER_LAUNCH = {"raster_bwd": 575.29e6, "raster_fwd": 491.80e6,
+TRAFFIC_BYTES_PER_LAUNCH = {"raster_bwd": 571.82e6, "raster_fwd": 491.21e6,
                             "emit_keys": 811.68e6}
 FWD_FLOPS_PER_EVAL = 22
 BWD_FLOPS_PER_EVAL = 12
