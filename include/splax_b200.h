@@ -357,6 +357,13 @@ void splax_debug_fail_alloc_after(int64_t successes);
  * contributions (the roofline's work units). Both default off. */
 void splax_profile_enable(int32_t timing, int32_t count_work);
 
+/* Restrict the timing of splax_profile_enable to some stages (no counterpart in the
+ * reference): bit k set times stage k, in the order project_fwd, project_bwd, depth_minmax,
+ * pair_keys, pair_sort, pair_scan, emit_keys, radix_sort, tile_bins, raster_fwd, raster_bwd,
+ * loss, optim, allreduce (the names of splax_profile_report). Each timed stage adds two event
+ * records to its stream; timing one stage keeps that cost out of the others. Default: all. */
+void splax_profile_stages(uint32_t mask);
+
 /* Zero the current device's timers and work counters. */
 int splax_profile_reset(void);
 

@@ -56,6 +56,7 @@ SIGNATURES: dict[str, list] = {
     "splax_last_sort_token": [],
     "splax_reuse_sort": [I64],
     "splax_profile_enable": [I32, I32],
+    "splax_profile_stages": [ctypes.c_uint32],
     "splax_profile_reset": [],
     "splax_profile_report": [P, I32],
     "splax_mse_loss": [P, P, I64, F32, P, P],
@@ -100,6 +101,7 @@ def load() -> ctypes.CDLL:
     lib.splax_clear_cache.restype = None
     lib.splax_debug_fail_alloc_after.restype = None
     lib.splax_profile_enable.restype = None
+    lib.splax_profile_stages.restype = None
     lib.splax_last_sort_token.restype = ctypes.c_int64
     lib.splax_reuse_sort.restype = None
     _lib = lib
@@ -146,6 +148,17 @@ def require_cuda(*tensors: torch.Tensor) -> torch.device:
 def profile_enable(timing: bool = True, count_work: bool = False) -> None:
     """Switch on per-launch CUDA-event timing and / or the instrumented work counters."""
     load().splax_profile_enable(int(timing), int(count_work))
+
+
+STAGES = ("project_fwd", "project_bwd", "depth_minmax", "pair_keys", "pair_sort", "pair_scan",
+          "emit_keys", "radix_sort", "tile_bins", "raster_fwd", "raster_bwd", "loss", "optim",
+          "allreduce")
+
+
+def profile_stages(names=None) -> None:
+    """Time only the named stages (all when None); the others add no events to the streams."""
+    mask = 0xFFFFFFFF if names is None else sum(1 << STAGES.index(n) for n in names)
+    load().splax_profile_stages(mask)
 
 
 def profile_reset() -> None:

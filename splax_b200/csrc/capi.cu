@@ -88,6 +88,7 @@ constexpr double kScratchHeadroom = 1.25;  // splax/_cache.py:149
 
 // ------------------------------------------------------------------ profiling (opt-in)
 std::atomic<bool> g_timing{false};
+std::atomic<uint32_t> g_timing_mask{0xffffffffu};  // bit k: stage kind k is timed
 std::atomic<bool> g_count_work{false};
 constexpr int kWorkWords = 6;  // device work counters (see DeviceState::work)
 
@@ -122,14 +123,18 @@ struct KernelTimer {
     }
     return e;
   }
+  bool open = false;  // the last begin() recorded an event that end() must close
   void begin(int kind, int nkernels, cudaStream_t s) {
-    if (!g_timing.load(std::memory_order_relaxed)) return;
+    open = g_timing.load(std::memory_order_relaxed) &&
+           (g_timing_mask.load(std::memory_order_relaxed) >> kind & 1u) != 0;
+    if (!open) return;
     Pending p{kind, nkernels, get(), get()};
     cudaEventRecord(p.a, s);
     pending.push_back(p);
   }
   void end(cudaStream_t s) {
-    if (!g_timing.load(std::memory_order_relaxed) || pending.empty()) return;
+    if (!open || pending.empty()) return;
+    open = false;
     cudaEventRecord(pending.back().b, s);
   }
   void collect() {
@@ -1612,6 +1617,8 @@ void splax_profile_enable(int32_t timing, int32_t count_work) {
   g_timing.store(timing != 0);
   g_count_work.store(count_work != 0);
 }
+
+void splax_profile_stages(uint32_t mask) { g_timing_mask.store(mask); }
 
 int splax_profile_reset(void) {
   DeviceState* st;
