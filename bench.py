@@ -49,9 +49,9 @@ FWD_BWD = {
         "5 param arrays + viewmats", dict(viewmat_grad=True, antialiased=True)),
 }
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
-NCCL_LABEL = "nccl: one all-reduce of the gradients and the loss"
-NCCL_SPLIT_LABEL = ("nccl: two all-reduces, the colour and opacity gradients' overlapped with "
-                    "the projection backward")
+NCCL_LABEL = "nccl (its NVLS algorithm off): one all-reduce of the gradients and the loss"
+NCCL_SPLIT_LABEL = ("nccl (its NVLS algorithm off): two all-reduces, the colour and opacity "
+                    "gradients' overlapped with the projection backward")
 L2_BYTES = 126 << 20
 # algorithmic work per unit: FLOPs per blend evaluation / contribution (FMA = 2), restated from
 # the reference blend loop (splax/_rasterize/_kernels.py:185-197) and vjp (:1235-1253)
@@ -296,6 +296,16 @@ TRAIN_LRS = {"means": 1.5e-3, "log_scales": 5e-3, "quats": 1e-3, "colors_logit":
 SSIM_LAMBDA = 0.2
 
 
+def nccl_environment(args) -> None:
+    """Before the process group exists: NCCL's own NVLS all-reduce off unless the caller set
+    NCCL_NVLS_ENABLE. On an NVSwitch B200 box NCCL otherwise picks NVLS for the 56 MB gradient
+    all-reduce, which binds its buffers to NVLink multicast objects for the whole run; its ring
+    measured faster there (8 ranks, 56 MB: 0.229 ms vs 0.257 ms). The opt-in library exchange
+    (--collective nvls) keeps NCCL's default."""
+    if args.collective != "nvls":
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+
+
 def make_reducer(args, params, dev, world):
     """The library's NVLS gradient all-reduce over the parameters' gradients plus the loss when
     --collective nvls asks for it, else None (NCCL). NVLS stays opt-in: it measured 2% faster
@@ -427,6 +437,7 @@ def train_bench(args) -> None:
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
+        nccl_environment(args)
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
     closers: list = []
     try:
@@ -564,6 +575,7 @@ def main() -> None:
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
+        nccl_environment(args)
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
     closers: list = []
     try:
@@ -602,9 +614,10 @@ def main() -> None:
                  if world > 1 and reducer is None and not opts.get("forward_only")
                  and args.overlap else None)
 
-        def step(vm, tgt, ps=params, tgt_ready=None):
+        def step(vm, tgt, ps=params, tgt_ready=None, xev=None):
             """One step; returns the rendered images (forward only) or the loss. tgt_ready: an
-            event the loss waits for (the targets' copy may overlap the forward render)."""
+            event the loss waits for (the targets' copy may overlap the forward render). xev: a
+            pair of events recorded around the gradient exchange (N>1)."""
             if opts.get("forward_only"):
                 with torch.no_grad():
                     imgs, _ = sx.render(*ps, viewmat=vm, **kw)
@@ -623,7 +636,11 @@ def main() -> None:
             if split is not None:  # the second half of the NCCL exchange (the first overlapped)
                 return split.finish(loss)
             if world > 1:  # the gradients of the shared gaussians (and the loss) summed over ranks
+                if xev is not None:
+                    xev[0].record()
                 loss = reduce_grads(reducer, ps, loss, dev)
+                if xev is not None:
+                    xev[1].record()
             return loss
 
         for _ in range(args.warmup):
@@ -663,29 +680,47 @@ def main() -> None:
         if world > 1:
             dist.barrier()
         # Inputs smaller than L2 (config 1): time each step alone and flush L2 between steps by
-        # writing a 256 MB buffer outside the timed events; otherwise one event pair around all.
+        # writing a 256 MB buffer outside the timed events; otherwise from the first step's start
+        # event to the last step's end event.
         input_bytes = 4 * (sum(p.numel() for p in params) + target.numel())
         flush = input_bytes < 2 * L2_BYTES
+        # N>1: events around each step's exchange split this rank's time into its own work
+        # (step start to exchange start) and the exchange as its stream sees it (waiting for
+        # the slowest rank included)
+        xevs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                for _ in range(args.steps)] if world > 1 and split is None else None
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
         if flush:
             scratch = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                   for _ in range(args.steps)]
-            for a, b in evs:
+            for k, (a, b) in enumerate(evs):
                 scratch.fill_(1)
                 a.record()
-                step(views, target)
+                step(views, target, xev=xevs[k] if xevs else None)
                 b.record()
             torch.cuda.synchronize()
             ms = sum(a.elapsed_time(b) for a, b in evs)
         else:
-            t0 = torch.cuda.Event(enable_timing=True)
-            t1 = torch.cuda.Event(enable_timing=True)
-            t0.record()
-            for _ in range(args.steps):
-                step(views, target)
-            t1.record()
+            for k, (a, b) in enumerate(evs):
+                a.record()
+                step(views, target, xev=xevs[k] if xevs else None)
+                b.record()
             torch.cuda.synchronize()
-            ms = t0.elapsed_time(t1)
+            ms = evs[0][0].elapsed_time(evs[-1][1])
+        rank_split = None
+        if xevs:
+            own = sum(a.elapsed_time(x0) for (a, _), (x0, _) in zip(evs, xevs)) / args.steps
+            xch = sum(x0.elapsed_time(x1) for x0, x1 in xevs) / args.steps
+            mine = torch.tensor([ms / args.steps, own, xch], device=dev, dtype=torch.float64)
+            every = [torch.zeros_like(mine) for _ in range(world)]
+            dist.all_gather(every, mine)
+            rank_split = {"ms_per_step": [round(float(t[0]), 4) for t in every],
+                          "own_work_ms": [round(float(t[1]), 4) for t in every],
+                          "exchange_ms": [round(float(t[2]), 4) for t in every],
+                          "how": "per rank, mean over the timed steps: CUDA events at the step's "
+                                 "start, around the gradient exchange (the concatenation of the "
+                                 "gradients and the wait for the slowest rank included) and at "
+                                 "its end"}
         if world > 1:
             dist.barrier()
         clocks = sampler.stop() if sampler else None
@@ -922,6 +957,7 @@ def main() -> None:
                 "work_per_step": work,
                 "clocks": clocks,
                 "exchange": exchange,
+                "ranks": rank_split,
                 "host": {"cpus": os.cpu_count(),
                          "cpus_usable": len(os.sched_getaffinity(0))
                          if hasattr(os, "sched_getaffinity") else None},
