@@ -44,7 +44,7 @@ struct PixelState {
 // The reference blend step (splax/_rasterize/_kernels.py:185-197) for one pixel.
 template <bool DEPTH, bool COUNT, bool CLAMP>
 __device__ __forceinline__ void blend_one(PixelState& s, float p, float opac, float r, float g,
-                                          float b, float depth, int32_t idx,
+                                          float b, float depth, int32_t idx, int& ndone,
                                           unsigned long long& evals,
                                           unsigned long long& contribs) {
   // the skip tests of a done pixel and of the reference's sigma / alpha tests share one branch
@@ -56,6 +56,7 @@ __device__ __forceinline__ void blend_one(PixelState& s, float p, float opac, fl
   const float next_T = s.T * (1.0f - alpha);
   if (next_T <= kTransmittanceMin) {
     s.done = true;
+    ++ndone;
     return;
   }
   const float vis = alpha * s.T;
@@ -91,18 +92,18 @@ raster_fwd_kernel(RasterFwdArgs a) {
   const float px = static_cast<float>(j) + 0.5f;
   const float py0 = static_cast<float>(i0) + 0.5f;
   PixelState st[kPixels];
-  bool all_done = true;
+  int ndone = 0;  // pixels of this thread that are done (outside the image or saturated)
 #pragma unroll
   for (int k = 0; k < kPixels; ++k) {
     st[k].done = !(i0 + k < a.img_h && j < a.img_w);
-    all_done &= st[k].done;
+    ndone += st[k].done ? 1 : 0;
   }
   const int2 range = reinterpret_cast<const int2*>(a.tile_bins)[tile_g];
   const int32_t range_start = range.x, range_end = range.y;
   const int32_t num_batches = (range_end - range_start + kBlockSize - 1) / kBlockSize;
   for (int32_t bt = 0; bt < num_batches; ++bt) {
     // block vote doubles as the barrier protecting the previous batch's shared reads
-    if (__syncthreads_count(all_done) >= kFwdThreads) break;
+    if (__syncthreads_count(ndone == kPixels) >= kFwdThreads) break;
     const int32_t batch_start = range_start + bt * kBlockSize;
     bool high_opacity = false;
 #pragma unroll
@@ -140,22 +141,20 @@ raster_fwd_kernel(RasterFwdArgs a) {
         const float dy0 = r0.y - py0;
         const float2 qxx = splat2(r0.z * dx * dx), qbx = splat2(r0.w * dx), qc = splat2(r1.x);
         const int32_t idx = batch_start + t;
-        all_done = true;
 #pragma unroll
         for (int q = 0; q < kPairs; ++q) {
           // the exponents of a pixel pair in packed form, then the branchy per-pixel step
           const float2 dy = add2(splat2(dy0), make_float2(-2.0f * q, -2.0f * q - 1.0f));
           const float2 p = fma2(fma2(qc, dy, qbx), dy, qxx);
           blend_one<DEPTH, COUNT, kClamp>(st[2 * q], p.x, r1.y, r1.z, r1.w, r2.x, r2.y, idx,
-                                          evals, contribs);
+                                          ndone, evals, contribs);
           blend_one<DEPTH, COUNT, kClamp>(st[2 * q + 1], p.y, r1.y, r1.z, r1.w, r2.x, r2.y, idx,
-                                          evals, contribs);
-          all_done &= st[2 * q].done && st[2 * q + 1].done;
+                                          ndone, evals, contribs);
         }
-        if (all_done) break;
+        if (ndone == kPixels) break;
       }
     };
-    if (!all_done) {
+    if (ndone < kPixels) {
       if (clamp) blend_batch(std::true_type{});
       else blend_batch(std::false_type{});
     }
