@@ -8,8 +8,9 @@ pairs per call). This test calls it through the C ABI twice in a row, before the
 allocating projection has run in this test, so its first call does the per-device set-up, and
 requires the same outputs, bit for bit, as splax_project -- the tolerance of every other
 projection test -- so a stale array left by the first call would show up in the second. The
-device's free memory must not change across the second call. It also checks that an oversized
-call is refused with a clear message.
+device's free memory must not change across the second call. After one eager call, a call
+also records into a CUDA graph under global capture mode, and the replay gives the same
+outputs. It also checks that an oversized call is refused with a clear message.
 
 The file is named to be collected last, so a run that stops at the first failure has already
 run every other test; it passes alone in a fresh process as well as after the others.
@@ -112,6 +113,56 @@ def test_project_noalloc_leaves_free_memory_unchanged():
     call()
     free1, _ = torch.cuda.mem_get_info()
     assert free1 == free0
+
+
+def test_project_noalloc_records_into_a_cuda_graph():
+    """After one eager call, a call records into a CUDA graph under global capture mode (which
+    refuses cudaMalloc and every other unsafe call while the capture runs); replayed over
+    overwritten outputs, the graph gives splax_project's outputs bit for bit."""
+    if not torch.cuda.is_available():
+        pytest.fail("CUDA device required for -m gpu tests")
+    from splax_b200 import _lib
+
+    lib = _lib.load()
+    n, H, W = 30_000, 224, 288
+    m, s, q, c, op, bg = random_scene(n, 25, spread=1.0, smin=0.005, smax=0.05)
+    views = np.stack([viewmat(0.1), viewmat(-0.2, 0.05, 4.8)])
+    B = views.shape[0]
+    t = lambda a: torch.tensor(np.ascontiguousarray(a), device="cuda")  # noqa: E731
+    ins = (t(m), t(s), t(np.roll(q, -1, -1)), t(views.reshape(-1, 4)), t(op),
+           torch.zeros((1, 4, 4), device="cuda"), torch.full((1,), -1, device="cuda",
+                                                              dtype=torch.int32))
+    total = B * n
+    outs = [torch.empty((total, 2), device="cuda"), torch.empty((total,), device="cuda"),
+            torch.empty((total,), device="cuda", dtype=torch.int32),
+            torch.empty((total, 3), device="cuda"),
+            torch.empty((total,), device="cuda", dtype=torch.int32),
+            torch.empty((total,), device="cuda", dtype=torch.int32)]
+    p = _lib.ptr
+    cm = cam(H, W)
+
+    def call():
+        return lib.splax_project_noalloc(
+            p(ins[0]), n, p(ins[1]), n, p(ins[2]), n, p(ins[3]), 4 * B, p(ins[4]), n, p(ins[5]),
+            1, p(ins[6]), n, 1, 0, H, W, cm["f"][0], cm["f"][1], float(cm["c"][0]),
+            float(cm["c"][1]), 1.0, 0.01, total, *[p(o) for o in outs], _lib.stream_of(ins[0]))
+
+    _lib.check(call())  # the per-device set-up happens outside the capture
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, capture_error_mode="global"):
+        rc = call()
+    _lib.check(rc)
+    for o in outs:
+        o.fill_(-9)
+    graph.replay()
+    torch.cuda.synchronize()
+    got = [o.cpu().numpy() for o in outs]
+    ref = _call(lib, "splax_project", ins, n, H, W, total, 0.0)
+    assert ref[5][-1] > 0
+    for name, a, b in zip(["xys", "depths", "radii", "conics", "num_tiles_hit", "cum"], got, ref):
+        assert np.array_equal(a, b), f"{name} differs after the graph replay"
+    del graph
 
 
 def test_project_noalloc_rejects_oversized_calls():
