@@ -35,51 +35,80 @@ __global__ void seed_minmax_kernel(int32_t* mm, int32_t B) {
   }
 }
 
+// Per-image [min, max] of the visible pairs' depths (as ordered ints). Each thread takes 16
+// consecutive pairs with all its loads issued up front (four 16-byte loads of radii and of
+// depths when the run is whole and aligned), so the kernel streams at memory speed instead of
+// waiting on one dependent load per pair. With n >= 16 a thread's run spans at most two images.
+__device__ __forceinline__ void mm_flush(int32_t* mm, int64_t im, int32_t lo, int32_t hi) {
+  if (lo <= hi) {
+    atomicMin(&mm[2 * im], lo);
+    atomicMax(&mm[2 * im + 1], hi);
+  }
+}
+
 __global__ void __launch_bounds__(kMmThreads)
 depth_minmax_kernel(const float* __restrict__ depths, const int32_t* __restrict__ radii,
                     int64_t total, int64_t n, int32_t* mm) {
-  const int64_t base = static_cast<int64_t>(blockIdx.x) * kMmThreads * kMmItems;
-  int64_t img_cur = -1;
-  int32_t lo = 0x7fffffff, hi = static_cast<int32_t>(0x80000000u);
-  // image of each index without a 64-bit division per item: one division, then boundaries
-  int64_t im = (base + threadIdx.x) / n, im_end = (im + 1) * n;
-#pragma unroll 4
+  const int64_t base = (static_cast<int64_t>(blockIdx.x) * kMmThreads + threadIdx.x) * kMmItems;
+  int32_t r[kMmItems];
+  float d[kMmItems];
+  if (base + kMmItems <= total) {
+    const int4* r4 = reinterpret_cast<const int4*>(radii + base);
+    const float4* d4 = reinterpret_cast<const float4*>(depths + base);
+#pragma unroll
+    for (int v = 0; v < kMmItems / 4; ++v) {
+      const int4 a = __ldg(r4 + v);
+      const float4 b = __ldg(d4 + v);
+      r[4 * v] = a.x; r[4 * v + 1] = a.y; r[4 * v + 2] = a.z; r[4 * v + 3] = a.w;
+      d[4 * v] = b.x; d[4 * v + 1] = b.y; d[4 * v + 2] = b.z; d[4 * v + 3] = b.w;
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < kMmItems; ++k) {
+      const bool in = base + k < total;
+      r[k] = in ? radii[base + k] : 0;
+      d[k] = in ? depths[base + k] : 0.0f;
+    }
+  }
+  // the run's first image and where the next one starts (n >= kMmItems: at most one boundary)
+  const int64_t im0 = base < total ? base / n : -1;
+  const int64_t cut = (im0 + 1) * n - base;  // items before the boundary
+  int32_t lo0 = 0x7fffffff, hi0 = static_cast<int32_t>(0x80000000u);
+  int32_t lo1 = 0x7fffffff, hi1 = static_cast<int32_t>(0x80000000u);
+#pragma unroll
   for (int k = 0; k < kMmItems; ++k) {
-    const int64_t idx = base + k * kMmThreads + threadIdx.x;
-    if (idx >= total) break;
-    while (idx >= im_end) {
-      ++im;
-      im_end += n;
-    }
-    if (radii[idx] <= 0) continue;
-    const int32_t d = float_to_ordered(depths[idx]);
-    if (im != img_cur) {
-      if (img_cur >= 0) {
-        atomicMin(&mm[2 * img_cur], lo);
-        atomicMax(&mm[2 * img_cur + 1], hi);
-      }
-      img_cur = im;
-      lo = d;
-      hi = d;
+    if (r[k] <= 0) continue;
+    const int32_t o = float_to_ordered(d[k]);
+    if (k < cut) {
+      lo0 = min(lo0, o);
+      hi0 = max(hi0, o);
     } else {
-      lo = min(lo, d);
-      hi = max(hi, d);
+      lo1 = min(lo1, o);
+      hi1 = max(hi1, o);
     }
   }
-  // one atomic pair per warp when the warp sits inside one image, per lane otherwise
-  const int rep = __reduce_max_sync(0xffffffffu, static_cast<int>(img_cur));
-  const bool uniform = __all_sync(0xffffffffu, img_cur == rep || img_cur < 0);
-  if (uniform) {
-    const int32_t wlo = __reduce_min_sync(0xffffffffu, lo);
-    const int32_t whi = __reduce_max_sync(0xffffffffu, hi);
-    if ((threadIdx.x & 31) == 0 && rep >= 0) {
-      atomicMin(&mm[2 * rep], wlo);
-      atomicMax(&mm[2 * rep + 1], whi);
-    }
-  } else if (img_cur >= 0) {
-    atomicMin(&mm[2 * img_cur], lo);
-    atomicMax(&mm[2 * img_cur + 1], hi);
+  // one atomic pair per warp when every lane's run lies in one image, per lane otherwise
+  const long long first = __shfl_sync(0xffffffffu, static_cast<long long>(im0), 0);
+  const bool one_image = __all_sync(0xffffffffu, im0 == first && (im0 < 0 || cut >= kMmItems));
+  if (one_image) {
+    const int32_t wlo = __reduce_min_sync(0xffffffffu, lo0);
+    const int32_t whi = __reduce_max_sync(0xffffffffu, hi0);
+    if ((threadIdx.x & 31) == 0 && first >= 0) mm_flush(mm, first, wlo, whi);
+  } else if (im0 >= 0) {
+    mm_flush(mm, im0, lo0, hi0);
+    if (cut < kMmItems) mm_flush(mm, im0 + 1, lo1, hi1);
   }
+}
+
+// Any n (also n < 16): one dependent pass per pair; used only when a run could span more
+// than two images.
+__global__ void __launch_bounds__(kMmThreads)
+depth_minmax_small_n_kernel(const float* __restrict__ depths, const int32_t* __restrict__ radii,
+                            int64_t total, int64_t n, int32_t* mm) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * kMmThreads + threadIdx.x;
+  if (idx >= total || radii[idx] <= 0) return;
+  const int32_t o = float_to_ordered(depths[idx]);
+  mm_flush(mm, idx / n, o, o);
 }
 
 // ------------------------------------------------------------------ depth-first ordering
@@ -751,11 +780,20 @@ int radix_digit_bits(int bits) {
 void launch_depth_minmax(const float* depths, const int32_t* radii, int64_t total, int64_t n,
                          int32_t B, int32_t* depth_mm, cudaStream_t stream) {
   seed_minmax_kernel<<<(B + 127) / 128, 128, 0, stream>>>(depth_mm, B);
-  const int64_t blocks = (total + kMmThreads * kMmItems - 1) / (kMmThreads * kMmItems);
-  if (blocks > 0)
+  if (total <= 0) return;
+  // the vector path needs 16-byte aligned runs (cudaMalloc'd operands; checked) and n >= 16
+  const bool aligned = (reinterpret_cast<uintptr_t>(depths) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(radii) % 16 == 0);
+  if (aligned && n >= kMmItems) {
+    const int64_t blocks = (total + kMmThreads * kMmItems - 1) / (kMmThreads * kMmItems);
     depth_minmax_kernel<<<static_cast<unsigned>(blocks), kMmThreads, 0, stream>>>(depths, radii,
                                                                                   total, n,
                                                                                   depth_mm);
+  } else {
+    const int64_t blocks = (total + kMmThreads - 1) / kMmThreads;
+    depth_minmax_small_n_kernel<<<static_cast<unsigned>(blocks), kMmThreads, 0, stream>>>(
+        depths, radii, total, n, depth_mm);
+  }
 }
 
 void launch_depth_span(const int32_t* depth_mm, int32_t B, unsigned* span_out,
