@@ -308,6 +308,16 @@ __device__ __forceinline__ void adam_one(float& p, float g, float& m, float& v, 
   p = p + (-lr) * (mh / (sqrtf(vh) + eps));
 }
 
+// Programmatic dependent launch (sm_90+). Every kernel of the path starts with pdl_enter():
+// griddepcontrol.wait returns once the stream predecessor has completed and its writes are
+// visible (at once for a launch without the attribute), so nothing is read early; then
+// launch_dependents lets the successor's CTAs be scheduled as soon as every CTA of this grid
+// has started, which hides the successor's launch and ramp behind this grid's last wave.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Hardware base-2 exponential (MUFU): the blend kernels' exponent is pre-scaled by log2(e).
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;

@@ -11,6 +11,7 @@
 
 #include <cstdint>
 
+#include "common.cuh"
 #include "kernels.h"
 
 namespace splax {
@@ -26,6 +27,7 @@ __device__ __forceinline__ float sq_diff_sum(float4 a, float4 b) {
 __global__ void __launch_bounds__(kLossThreads)
 mse_loss_kernel(const float* __restrict__ img, const float* __restrict__ tgt, int64_t count,
                 bool vec, double inv_denom, double* partials, unsigned* done, float* loss) {
+  pdl_enter();
   float acc = 0.0f;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kLossThreads;
   const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kLossThreads + threadIdx.x;
@@ -69,6 +71,7 @@ __global__ void __launch_bounds__(kLossThreads)
 mse_loss_bwd_kernel(const float* __restrict__ img, const float* __restrict__ tgt, int64_t count,
                     bool vec, float scale, const float* __restrict__ v_loss,
                     float* __restrict__ grad) {
+  pdl_enter();
   const float s = scale * *v_loss;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kLossThreads;
   const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kLossThreads + threadIdx.x;
@@ -103,15 +106,15 @@ void launch_mse_loss(const float* img, const float* tgt, int64_t count, double i
                      double* partials, unsigned* done, float* loss, int blocks,
                      cudaStream_t stream) {
   const bool vec = aligned16(img) && aligned16(tgt);
-  mse_loss_kernel<<<blocks, kLossThreads, 0, stream>>>(img, tgt, count, vec, inv_denom,
-                                                       partials, done, loss);
+  launch_pdl(mse_loss_kernel, blocks, kLossThreads, 0, stream, img, tgt, count, vec, inv_denom,
+      partials, done, loss);
 }
 
 void launch_mse_loss_bwd(const float* img, const float* tgt, int64_t count, float scale,
                          const float* v_loss, float* grad, int blocks, cudaStream_t stream) {
   const bool vec = aligned16(img) && aligned16(tgt) && aligned16(grad);
-  mse_loss_bwd_kernel<<<blocks, kLossThreads, 0, stream>>>(img, tgt, count, vec, scale, v_loss,
-                                                           grad);
+  launch_pdl(mse_loss_bwd_kernel, blocks, kLossThreads, 0, stream, img, tgt, count, vec, scale,
+      v_loss, grad);
 }
 
 }  // namespace splax

@@ -226,6 +226,7 @@ constexpr int kProjTile = kProjScanTile;
 template <bool AA>
 __global__ void __launch_bounds__(kProjThreads, 4)
 project_fwd_kernel(ProjectArgs a, unsigned long long* status, int* ticket, unsigned* err) {
+  pdl_enter();
   __shared__ int s_tile;
   __shared__ __align__(16) int32_t s_cnt[kProjTile];
   __shared__ long long s_warp[kProjThreads / 32];
@@ -317,6 +318,7 @@ constexpr int kBwdThreads = 256;
 // the caller would otherwise take over B*n rows). Otherwise one thread per (image, gaussian).
 template <bool AA, bool FOLD>
 __global__ void __launch_bounds__(kBwdThreads, 3) project_bwd_kernel(ProjectBwdArgs a) {
+  pdl_enter();
   const int64_t blocks_per_image = (a.n + kBwdThreads - 1) / kBwdThreads;
   const int64_t img0 = FOLD ? 0 : blockIdx.x / blocks_per_image;
   const int64_t img1 = FOLD ? a.B : img0 + 1;
@@ -544,11 +546,11 @@ void launch_project_fwd(const ProjectArgs& a, unsigned long long* status, int* t
   const int64_t blocks = project_scan_tiles(a.total);
   if (blocks == 0) return;
   if (a.rho)
-    project_fwd_kernel<true><<<static_cast<unsigned>(blocks), kProjThreads, 0, stream>>>(
-        a, status, ticket, err);
+    launch_pdl(project_fwd_kernel<true>, static_cast<unsigned>(blocks), kProjThreads, 0, stream, a,
+        status, ticket, err);
   else
-    project_fwd_kernel<false><<<static_cast<unsigned>(blocks), kProjThreads, 0, stream>>>(
-        a, status, ticket, err);
+    launch_pdl(project_fwd_kernel<false>, static_cast<unsigned>(blocks), kProjThreads, 0, stream, a,
+        status, ticket, err);
 }
 
 int64_t project_scan_tiles(int64_t total) { return (total + kProjTile - 1) / kProjTile; }
@@ -559,11 +561,11 @@ void launch_project_bwd(const ProjectBwdArgs& a, cudaStream_t stream) {
   if (blocks == 0) return;
   const unsigned g = static_cast<unsigned>(a.fold_batch ? blocks_per_image : blocks);
   if (a.v_rho) {
-    if (a.fold_batch) project_bwd_kernel<true, true><<<g, kBwdThreads, 0, stream>>>(a);
-    else project_bwd_kernel<true, false><<<g, kBwdThreads, 0, stream>>>(a);
+    if (a.fold_batch) launch_pdl(project_bwd_kernel<true, true>, g, kBwdThreads, 0, stream, a);
+    else launch_pdl(project_bwd_kernel<true, false>, g, kBwdThreads, 0, stream, a);
   } else {
-    if (a.fold_batch) project_bwd_kernel<false, true><<<g, kBwdThreads, 0, stream>>>(a);
-    else project_bwd_kernel<false, false><<<g, kBwdThreads, 0, stream>>>(a);
+    if (a.fold_batch) launch_pdl(project_bwd_kernel<false, true>, g, kBwdThreads, 0, stream, a);
+    else launch_pdl(project_bwd_kernel<false, false>, g, kBwdThreads, 0, stream, a);
   }
 }
 

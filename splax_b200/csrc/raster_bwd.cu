@@ -109,6 +109,7 @@ constexpr int kPairs = kPixels / 2;
 template <bool DEPTH, bool COUNT>
 __global__ void __launch_bounds__(kBlockSize / kPixels)
 raster_bwd_kernel(RasterBwdArgs a) {
+  pdl_enter();
   constexpr int kBwdThreads = kBlockSize / kPixels;
   constexpr int K = DEPTH ? 10 : 9;
   unsigned long long evals = 0, contribs = 0;
@@ -308,11 +309,11 @@ raster_bwd_kernel(RasterBwdArgs a) {
 void launch_bwd(const RasterBwdArgs& a, unsigned g, cudaStream_t stream) {
   constexpr int nt = kBlockSize / kPixels;
   if (a.v_out_depth) {
-    if (a.work) raster_bwd_kernel<true, true><<<g, nt, 0, stream>>>(a);
-    else raster_bwd_kernel<true, false><<<g, nt, 0, stream>>>(a);
+    if (a.work) launch_pdl(raster_bwd_kernel<true, true>, g, nt, 0, stream, a);
+    else launch_pdl(raster_bwd_kernel<true, false>, g, nt, 0, stream, a);
   } else {
-    if (a.work) raster_bwd_kernel<false, true><<<g, nt, 0, stream>>>(a);
-    else raster_bwd_kernel<false, false><<<g, nt, 0, stream>>>(a);
+    if (a.work) launch_pdl(raster_bwd_kernel<false, true>, g, nt, 0, stream, a);
+    else launch_pdl(raster_bwd_kernel<false, false>, g, nt, 0, stream, a);
   }
 }
 

@@ -77,6 +77,7 @@ constexpr int kPairs = kPixels / 2;
 template <bool DEPTH, bool COUNT>
 __global__ void __launch_bounds__(kBlockSize / kPixels)
 raster_fwd_kernel(RasterFwdArgs a) {
+  pdl_enter();
   constexpr int kFwdThreads = kBlockSize / kPixels;
   unsigned long long evals = 0, contribs = 0;
   __shared__ float4 s_r0[kBlockSize];
@@ -187,11 +188,11 @@ raster_fwd_kernel(RasterFwdArgs a) {
 void launch_fwd(const RasterFwdArgs& a, unsigned g, cudaStream_t stream) {
   constexpr int nt = kBlockSize / kPixels;
   if (a.out_depth) {
-    if (a.work) raster_fwd_kernel<true, true><<<g, nt, 0, stream>>>(a);
-    else raster_fwd_kernel<true, false><<<g, nt, 0, stream>>>(a);
+    if (a.work) launch_pdl(raster_fwd_kernel<true, true>, g, nt, 0, stream, a);
+    else launch_pdl(raster_fwd_kernel<true, false>, g, nt, 0, stream, a);
   } else {
-    if (a.work) raster_fwd_kernel<false, true><<<g, nt, 0, stream>>>(a);
-    else raster_fwd_kernel<false, false><<<g, nt, 0, stream>>>(a);
+    if (a.work) launch_pdl(raster_fwd_kernel<false, true>, g, nt, 0, stream, a);
+    else launch_pdl(raster_fwd_kernel<false, false>, g, nt, 0, stream, a);
   }
 }
 

@@ -28,6 +28,7 @@ constexpr int kMmThreads = 256;
 constexpr int kMmItems = 16;
 
 __global__ void seed_minmax_kernel(int32_t* mm, int32_t B) {
+  pdl_enter();
   int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b < B) {
     mm[2 * b] = float_to_ordered(1.0e30f);
@@ -49,6 +50,7 @@ __device__ __forceinline__ void mm_flush(int32_t* mm, int64_t im, int32_t lo, in
 __global__ void __launch_bounds__(kMmThreads)
 depth_minmax_kernel(const float* __restrict__ depths, const int32_t* __restrict__ radii,
                     int64_t total, int64_t n, int32_t* mm) {
+  pdl_enter();
   const int64_t base = (static_cast<int64_t>(blockIdx.x) * kMmThreads + threadIdx.x) * kMmItems;
   int32_t r[kMmItems];
   float d[kMmItems];
@@ -105,6 +107,7 @@ depth_minmax_kernel(const float* __restrict__ depths, const int32_t* __restrict_
 __global__ void __launch_bounds__(kMmThreads)
 depth_minmax_small_n_kernel(const float* __restrict__ depths, const int32_t* __restrict__ radii,
                             int64_t total, int64_t n, int32_t* mm) {
+  pdl_enter();
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * kMmThreads + threadIdx.x;
   if (idx >= total || radii[idx] <= 0) return;
   const int32_t o = float_to_ordered(depths[idx]);
@@ -122,6 +125,7 @@ depth_minmax_small_n_kernel(const float* __restrict__ depths, const int32_t* __r
 // Largest per-image span of visible depth bit patterns (64-bit key mode): the pair key stores
 // depth bits relative to the image's minimum, which orders positive floats like their values.
 __global__ void depth_span_kernel(const int32_t* mm, int32_t B, unsigned* span_out) {
+  pdl_enter();
   unsigned span = 0;
   for (int b = threadIdx.x; b < B; b += blockDim.x) {
     const int32_t lo = mm[2 * b], hi = mm[2 * b + 1];
@@ -203,6 +207,7 @@ __device__ __forceinline__ bool prep_one(const PairKeyArgs& a, int64_t idx, K& k
 template <typename K>
 __global__ void __launch_bounds__(kPrepThreads) pair_prep_kernel(PairKeyArgs a, K* keys,
                                                                  int32_t* vals) {
+  pdl_enter();
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * kPrepThreads + threadIdx.x;
   if (idx >= a.total) return;
   K kk = K(0);
@@ -220,6 +225,7 @@ __global__ void __launch_bounds__(kScanThreads)
 sorted_offsets_kernel(const int32_t* __restrict__ perm, const int32_t* __restrict__ counts,
                       int64_t total, const int32_t* dtotal, int32_t* __restrict__ offsets,
                       unsigned long long* status, int* ticket, unsigned* err) {
+  pdl_enter();
   __shared__ int s_tile;
   __shared__ long long s_warp[kScanThreads / 32];
   __shared__ long long s_prefix;
@@ -306,6 +312,7 @@ constexpr int kEmitWarps = 4;
 constexpr int kEmitThreads = 32 * kEmitWarps;
 
 __global__ void __launch_bounds__(kEmitThreads) emit_sorted_kernel(EmitArgs a) {
+  pdl_enter();
   __shared__ WarpWalk s_walk[kEmitWarps];
   __shared__ int32_t s_x[kEmitWarps][3][32];  // flat id, offset, image bits of each lane's pair
   const int lane = threadIdx.x & 31, wi = threadIdx.x >> 5;
@@ -392,6 +399,7 @@ __global__ void __launch_bounds__(kEmitThreads) emit_sorted_kernel(EmitArgs a) {
 __global__ void reference_keys_kernel(const uint32_t* __restrict__ bin_keys,
                                       const int32_t* __restrict__ gids, int64_t count,
                                       PairKeyArgs a, int64_t* out) {
+  pdl_enter();
   const int64_t p = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (p >= count) return;
   const int64_t idx = gids[p];
@@ -431,6 +439,7 @@ template <typename K, int RB>
 __global__ void __launch_bounds__(kHistThreads)
 radix_hist_kernel(const K* __restrict__ keys, int64_t count, bool filter, int passes,
                   uint32_t* hist) {
+  pdl_enter();
   constexpr int kSets = 4;
   constexpr int D = 1 << RB;
   constexpr int kMaxPasses = kRadixHistWords / D;
@@ -493,6 +502,7 @@ __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* s
 template <int D>
 __global__ void __launch_bounds__(D)
 radix_scan_kernel(const uint32_t* hist, uint32_t* offsets, int32_t* total_out) {
+  pdl_enter();
   __shared__ uint32_t s_warp[D / 32];
   const int p = blockIdx.x;
   const uint32_t v = hist[p * D + threadIdx.x];
@@ -509,6 +519,7 @@ onesweep_kernel(const K* __restrict__ kin, const int32_t* __restrict__ vin, K* _
                 int32_t* __restrict__ vout, int64_t count, const int32_t* dcount, int shift,
                 const uint32_t* __restrict__ goff, unsigned long long* status, int* tile_counter,
                 unsigned* err) {
+  pdl_enter();
   constexpr int TILE = NT * ITEMS;
   constexpr int kSortWarps = NT / 32;
   constexpr int D = 1 << RB;
@@ -675,6 +686,7 @@ constexpr int kBinItems = 8;
 __global__ void __launch_bounds__(kBinThreads)
 tile_bins_kernel(const uint32_t* __restrict__ keys, int64_t count, int32_t tile_n_bits,
                  int32_t num_tiles, int64_t num_bins, int2* bins, unsigned* err) {
+  pdl_enter();
   const int64_t base =
       (static_cast<int64_t>(blockIdx.x) * kBinThreads + threadIdx.x) * kBinItems;
   const int lane = threadIdx.x & 31;
@@ -739,10 +751,10 @@ int sort_impl(const SortScratch& s, int64_t count, int bits, cudaStream_t stream
   cudaMemsetAsync(hist, 0, sizeof(uint32_t) * kRadixHistWords, stream);
   cudaMemsetAsync(s.tile_counters, 0, sizeof(int) * 8, stream);
   const int64_t hblocks = (count + kHistThreads * kHistItems - 1) / (kHistThreads * kHistItems);
-  radix_hist_kernel<K, RB><<<static_cast<unsigned>(hblocks), kHistThreads, 0, stream>>>(
+  launch_pdl(radix_hist_kernel<K, RB>, static_cast<unsigned>(hblocks), kHistThreads, 0, stream,
       reinterpret_cast<const K*>(s.keys[0]), count, s.filter_sentinel, passes, hist);
-  radix_scan_kernel<D><<<passes, D, 0, stream>>>(hist, offsets,
-                                                s.filter_sentinel ? s.vcount : nullptr);
+  launch_pdl(radix_scan_kernel<D>, passes, D, 0, stream, hist, offsets,
+      s.filter_sentinel ? s.vcount : nullptr);
   constexpr int TILE = NT * ITEMS;
   const int64_t tiles = (count + TILE - 1) / TILE;
   const size_t smem = TILE * (sizeof(K) + sizeof(int32_t));
@@ -754,16 +766,14 @@ int sort_impl(const SortScratch& s, int64_t count, int bits, cudaStream_t stream
     const K* kin = reinterpret_cast<const K*>(s.keys[cur]);
     K* kout = reinterpret_cast<K*>(s.keys[cur ^ 1]);
     if (s.filter_sentinel && p == 0)
-      onesweep_kernel<K, ITEMS, NT, true, RB>
-          <<<static_cast<unsigned>(tiles), NT, smem, stream>>>(
-              kin, s.vals[cur], kout, s.vals[cur ^ 1], count, nullptr, RB * p,
-              offsets + p * D, s.status, s.tile_counters + p, s.err);
+      launch_pdl(onesweep_kernel<K, ITEMS, NT, true, RB>, static_cast<unsigned>(tiles), NT, smem,
+          stream, kin, s.vals[cur], kout, s.vals[cur ^ 1], count, nullptr, RB * p, offsets + p * D,
+          s.status, s.tile_counters + p, s.err);
     else
-      onesweep_kernel<K, ITEMS, NT, false, RB>
-          <<<static_cast<unsigned>(tiles), NT, smem, stream>>>(
-              kin, s.vals[cur], kout, s.vals[cur ^ 1], count,
-              s.filter_sentinel ? s.vcount : nullptr, RB * p, offsets + p * D, s.status,
-              s.tile_counters + p, s.err);
+      launch_pdl(onesweep_kernel<K, ITEMS, NT, false, RB>, static_cast<unsigned>(tiles), NT, smem,
+          stream, kin, s.vals[cur], kout, s.vals[cur ^ 1], count,
+          s.filter_sentinel ? s.vcount : nullptr, RB * p, offsets + p * D, s.status,
+          s.tile_counters + p, s.err);
     cur ^= 1;
   }
   return cur;
@@ -779,26 +789,26 @@ int radix_digit_bits(int bits) {
 
 void launch_depth_minmax(const float* depths, const int32_t* radii, int64_t total, int64_t n,
                          int32_t B, int32_t* depth_mm, cudaStream_t stream) {
-  seed_minmax_kernel<<<(B + 127) / 128, 128, 0, stream>>>(depth_mm, B);
+  launch_pdl(seed_minmax_kernel, static_cast<unsigned>((B + 127) / 128), 128, 0, stream, depth_mm,
+      B);
   if (total <= 0) return;
   // the vector path needs 16-byte aligned runs (cudaMalloc'd operands; checked) and n >= 16
   const bool aligned = (reinterpret_cast<uintptr_t>(depths) % 16 == 0) &&
                        (reinterpret_cast<uintptr_t>(radii) % 16 == 0);
   if (aligned && n >= kMmItems) {
     const int64_t blocks = (total + kMmThreads * kMmItems - 1) / (kMmThreads * kMmItems);
-    depth_minmax_kernel<<<static_cast<unsigned>(blocks), kMmThreads, 0, stream>>>(depths, radii,
-                                                                                  total, n,
-                                                                                  depth_mm);
+    launch_pdl(depth_minmax_kernel, static_cast<unsigned>(blocks), kMmThreads, 0, stream, depths,
+        radii, total, n, depth_mm);
   } else {
     const int64_t blocks = (total + kMmThreads - 1) / kMmThreads;
-    depth_minmax_small_n_kernel<<<static_cast<unsigned>(blocks), kMmThreads, 0, stream>>>(
+    launch_pdl(depth_minmax_small_n_kernel, static_cast<unsigned>(blocks), kMmThreads, 0, stream,
         depths, radii, total, n, depth_mm);
   }
 }
 
 void launch_depth_span(const int32_t* depth_mm, int32_t B, unsigned* span_out,
                        cudaStream_t stream) {
-  depth_span_kernel<<<1, 256, 0, stream>>>(depth_mm, B, span_out);
+  launch_pdl(depth_span_kernel, 1, 256, 0, stream, depth_mm, B, span_out);
 }
 
 void launch_pair_keys(const PairKeyArgs& a, bool key64, void* keys, int32_t* vals,
@@ -806,10 +816,10 @@ void launch_pair_keys(const PairKeyArgs& a, bool key64, void* keys, int32_t* val
   const int64_t blocks = (a.total + kPrepThreads - 1) / kPrepThreads;
   if (blocks == 0) return;
   if (key64)
-    pair_prep_kernel<uint64_t><<<static_cast<unsigned>(blocks), kPrepThreads, 0, stream>>>(
+    launch_pdl(pair_prep_kernel<uint64_t>, static_cast<unsigned>(blocks), kPrepThreads, 0, stream,
         a, static_cast<uint64_t*>(keys), vals);
   else
-    pair_prep_kernel<uint32_t><<<static_cast<unsigned>(blocks), kPrepThreads, 0, stream>>>(
+    launch_pdl(pair_prep_kernel<uint32_t>, static_cast<unsigned>(blocks), kPrepThreads, 0, stream,
         a, static_cast<uint32_t*>(keys), vals);
 }
 
@@ -824,22 +834,22 @@ void launch_sorted_offsets(const int32_t* perm, const int32_t* counts, int64_t t
   if (tiles == 0) return;
   cudaMemsetAsync(ticket, 0, sizeof(int), stream);
   cudaMemsetAsync(status, 0, sizeof(unsigned long long) * tiles, stream);
-  sorted_offsets_kernel<<<static_cast<unsigned>(tiles), kScanThreads, 0, stream>>>(
-      perm, counts, total, dtotal, offsets, status, ticket, err);
+  launch_pdl(sorted_offsets_kernel, static_cast<unsigned>(tiles), kScanThreads, 0, stream, perm,
+      counts, total, dtotal, offsets, status, ticket, err);
 }
 
 void launch_emit(const EmitArgs& a, cudaStream_t stream) {
   const int64_t blocks = (a.total + kEmitThreads - 1) / kEmitThreads;  // 32 pairs per warp
   if (blocks == 0) return;
-  emit_sorted_kernel<<<static_cast<unsigned>(blocks), kEmitThreads, 0, stream>>>(a);
+  launch_pdl(emit_sorted_kernel, static_cast<unsigned>(blocks), kEmitThreads, 0, stream, a);
 }
 
 void launch_reference_keys(const uint32_t* bin_keys, const int32_t* gids, int64_t count,
                            const PairKeyArgs& a, int64_t* out, cudaStream_t stream) {
   const int64_t blocks = (count + 255) / 256;
   if (blocks == 0) return;
-  reference_keys_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(bin_keys, gids,
-                                                                            count, a, out);
+  launch_pdl(reference_keys_kernel, static_cast<unsigned>(blocks), 256, 0, stream, bin_keys, gids,
+      count, a, out);
 }
 
 int sort_tile_items(bool key64) { return kSortThreads * (key64 ? kItems64 : kItems32); }
@@ -870,7 +880,7 @@ void launch_tile_bins(const uint32_t* keys, int64_t count, int32_t tile_n_bits,
   const int64_t per_block = static_cast<int64_t>(kBinThreads) * kBinItems;
   const int64_t blocks = (count + per_block - 1) / per_block;
   if (blocks == 0) return;
-  tile_bins_kernel<<<static_cast<unsigned>(blocks), kBinThreads, 0, stream>>>(
-      keys, count, tile_n_bits, num_tiles, num_bins, reinterpret_cast<int2*>(tile_bins), err);
+  launch_pdl(tile_bins_kernel, static_cast<unsigned>(blocks), kBinThreads, 0, stream, keys, count,
+      tile_n_bits, num_tiles, num_bins, reinterpret_cast<int2*>(tile_bins), err);
 }
 }  // namespace splax
