@@ -144,6 +144,22 @@ class _ProjectFn(torch.autograd.Function):
                 g_view.reshape(vs), None, g_tf, None, *([None] * 12))
 
 
+# Read-only stand-ins for "no transforms" (a zero 4x4 matrix and a -1 id), made once per device:
+# the kernels do not read them when has_transforms is 0, and making them on every call would put
+# two fill kernels in front of each projection.
+_NO_TRANSFORMS: dict = {}
+
+
+def _no_transforms(dev: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
+    key = (dev.type, dev.index)
+    got = _NO_TRANSFORMS.get(key)
+    if got is None:
+        got = (torch.zeros((1, 4, 4), device=dev, dtype=torch.float32),
+               torch.full((1,), -1, device=dev, dtype=torch.int32))
+        _NO_TRANSFORMS[key] = got
+    return got
+
+
 def _aa_consts(eps: float) -> tuple[float, float]:
     """eps and eps^2 as fp32 operands, rounded like the torch expression in
     ``opacity_compensation`` (a Python-float scalar times an fp32 tensor)."""
@@ -185,8 +201,7 @@ def project(
     has_transforms = gaussian_transforms is not None
     dev = mean3ds.device
     if not has_transforms:
-        gaussian_transforms = torch.zeros((1, 4, 4), device=dev, dtype=torch.float32)
-        transform_ids = torch.full((1,), -1, device=dev, dtype=torch.int32)
+        gaussian_transforms, transform_ids = _no_transforms(dev)
     elif transform_ids is None:
         raise ValueError("gaussian_transforms needs transform_ids")
     B = batch_size(n, mean3ds, scales, quats, viewmat, opacities,

@@ -404,7 +404,10 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
   SPLAX_CUDA(cudaMemcpyAsync(&st.pinned[2], st.span_word(), sizeof(int32_t),
                              cudaMemcpyDeviceToHost, stream));
   SPLAX_CUDA(cudaEventRecord(st.ev, stream));
-  SPLAX_CUDA(cudaMemsetAsync(st.tile_bins.p, 0, sizeof(int2) * bins_len, stream));
+  {
+    const ClearSpan span = {st.tile_bins.p, sizeof(int2) * static_cast<size_t>(bins_len)};
+    launch_clear(&span, 1, stream);
+  }
 
   SortScratch ss;
   ss.hist = static_cast<uint32_t*>(st.hist.p);
@@ -422,7 +425,8 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
     // 64-bit pair keys from 32 significant bits: the all-ones key marks pairs left out
     pair64 = pair_bits > 31;
     const int64_t t_pairs = (total + sort_tile_items(pair64) - 1) / sort_tile_items(pair64);
-    const size_t need = sizeof(unsigned long long) * kRadixMaxDigits * t_pairs;
+    // two halves: consecutive passes alternate between them (radix_sort_pairs)
+    const size_t need = 2 * sizeof(unsigned long long) * kRadixMaxDigits * t_pairs;
     if (st.status.bytes < need) {
       SPLAX_CUDA(cudaStreamSynchronize(stream));
       cudaError_t e = buf_reserve(st.status, need);
@@ -536,7 +540,7 @@ int sort_and_bin(DeviceState& st, const SortIn& in, cudaStream_t stream, SortOut
   {
     // look-back words of the intersection sort
     const int64_t t_bins = (st.isect_cap + sort_tile_items(false) - 1) / sort_tile_items(false);
-    const size_t need = sizeof(unsigned long long) * kRadixMaxDigits * t_bins;
+    const size_t need = 2 * sizeof(unsigned long long) * kRadixMaxDigits * t_bins;
     if (st.status.bytes < need) {
       SPLAX_CUDA(cudaStreamSynchronize(stream));
       cudaError_t e = buf_reserve(st.status, need);
@@ -732,13 +736,15 @@ int rasterize_bwd_common(const float* colors, int64_t colors_rows, const float* 
   int rc = current_state(&st);
   if (rc) return rc;
   std::lock_guard<std::mutex> lk(st->mu);
-  SPLAX_CUDA(cudaMemsetAsync(v_colors, 0, sizeof(float) * 3 * (fold_colors ? n : grad_rows),
-                             stream));
-  SPLAX_CUDA(cudaMemsetAsync(v_opacity, 0, sizeof(float) * (fold_opacity ? n : grad_rows),
-                             stream));
-  SPLAX_CUDA(cudaMemsetAsync(v_xy, 0, sizeof(float) * 2 * grad_rows, stream));
-  SPLAX_CUDA(cudaMemsetAsync(v_conic, 0, sizeof(float) * 3 * grad_rows, stream));
-  if (v_depths) SPLAX_CUDA(cudaMemsetAsync(v_depths, 0, sizeof(float) * grad_rows, stream));
+  {
+    const ClearSpan spans[5] = {
+        {v_colors, sizeof(float) * 3 * static_cast<size_t>(fold_colors ? n : grad_rows)},
+        {v_opacity, sizeof(float) * static_cast<size_t>(fold_opacity ? n : grad_rows)},
+        {v_xy, sizeof(float) * 2 * static_cast<size_t>(grad_rows)},
+        {v_conic, sizeof(float) * 3 * static_cast<size_t>(grad_rows)},
+        {v_depths, v_depths ? sizeof(float) * static_cast<size_t>(grad_rows) : 0}};
+    launch_clear(spans, 5, stream);
+  }
   SortIn in{xys, depths, radii, conics, map_opacities, map_rows, opacities, opacities_rows,
             colors, colors_rows, cum, n, B_geom, img_h, img_w, key_bits};
   SortOut so;
@@ -836,7 +842,10 @@ static int project_impl(const float* means3d, int64_t means3d_rows, const float*
   const int64_t tiles = project_scan_tiles(total);
   // [ticket (8 bytes)] [look-back words]
   SPLAX_CUDA(buf_reserve(st->proj_status, sizeof(unsigned long long) * (tiles + 1)));
-  SPLAX_CUDA(cudaMemsetAsync(st->proj_status.p, 0, sizeof(unsigned long long) * (tiles + 1), stream));
+  {
+    const ClearSpan span = {st->proj_status.p, sizeof(unsigned long long) * (tiles + 1)};
+    launch_clear(&span, 1, stream);
+  }
   ProjectArgs a;
   a.means = means3d;
   a.scales = scales;
@@ -955,8 +964,11 @@ static int project_bwd_impl(const float* means3d, int64_t means3d_rows, const fl
   std::lock_guard<std::mutex> lk(st->mu);
   rc = st->init();
   if (rc) return rc;
-  SPLAX_CUDA(cudaMemsetAsync(v_viewmat, 0, sizeof(float) * 16 * B, stream));
-  SPLAX_CUDA(cudaMemsetAsync(v_transforms, 0, sizeof(float) * 16 * K * B, stream));
+  {
+    const ClearSpan spans[2] = {{v_viewmat, sizeof(float) * 16 * static_cast<size_t>(B)},
+                                {v_transforms, sizeof(float) * 16 * static_cast<size_t>(K * B)}};
+    launch_clear(spans, 2, stream);
+  }
   ProjectBwdArgs a;
   a.means = means3d;
   a.scales = scales;

@@ -9,6 +9,15 @@
 
 namespace splax {
 
+// Zero-filled device spans (4-byte aligned, whole 4-byte words), cleared by one launch_pdl
+// kernel instead of one cudaMemsetAsync each, so the launch chain stays programmatic.
+struct ClearSpan {
+  void* p;
+  size_t bytes;
+};
+constexpr int kClearMaxSpans = 6;
+void launch_clear(const ClearSpan* spans, int count, cudaStream_t stream);
+
 // Launch with programmatic stream serialization: the kernel (which begins with pdl_enter) may
 // be scheduled while its stream predecessor finishes. Errors surface through cudaGetLastError
 // like a <<<>>> launch.
