@@ -4,7 +4,11 @@ The kernel's rho must equal the reference formula (``opacity_compensation``, the
 restatement of splax/_project/_project.py:95-117) bit for bit -- both evaluate the same fp32
 operations in the same order -- and an antialiased render's gradients must match the same
 render taken through the torch formula (relative L2 <= 1e-4: only the rounding of the chained
-conic cotangent differs)."""
+conic cotangent differs). Against the C oracle, an antialiased render (splax/_render.py:103-107:
+blend opacities opacity * rho, tile intersection on the raw opacity) must give the image within
+max-abs 1e-4 on the pixels whose threshold decisions the oracle does not flag, and the
+gradients of all five arrays and the viewmat within relative L2 1e-3, with rho's vjp derived
+independently on the CPU (tests/_oracle_chain.py)."""
 
 from __future__ import annotations
 
@@ -73,3 +77,40 @@ def test_antialiased_render_matches_torch_formula():
     for name, a, b in zip(("means", "scales", "quats", "colors", "opacities"), g_a, g_b):
         rel = ((a - b).norm() / b.norm().clamp_min(1e-30)).item()
         assert rel <= 1e-4, (name, rel)
+
+
+@pytest.mark.gpu
+def test_antialiased_render_vs_oracle(oracle_lib):
+    """End to end with antialiased=True: the CUDA path (rho and its cotangent folded into the
+    projection kernels) against the oracle's projection, fp32 rho, blend and the float64 vjp
+    chain; the image cotangent is zero on pixels the oracle flags as threshold ties."""
+    import _oracle_chain as ch
+    from conftest import cam, random_scene, viewmat
+
+    n, H, W, eps = 3000, 128, 128, 0.3
+    m, s, q, c, op, bg = random_scene(n, 21, smin=0.005, smax=0.05)
+    vm = viewmat()
+    ref_img, _, st = ch.render(m, s, q, c, op, bg, vm, antialias_eps=eps, **cam(H, W))
+    flags = st["flags"].reshape(H, W)
+    assert (flags == 0).mean() > 0.99
+    rho = st["rho"][np.asarray(st["radii"]).reshape(-1) > 0]
+    assert rho.min() < 0.99  # the compensation is active on part of the scene
+    w = np.random.default_rng(4).uniform(size=(H, W, 3)).astype(np.float32) / (H * W)
+    w[flags != 0] = 0.0
+    t = lambda a: torch.tensor(np.ascontiguousarray(a), device="cuda")  # noqa: E731
+    params = [t(x).requires_grad_() for x in (m, s, q, c, op)]
+    vm_t = t(vm).requires_grad_()
+    img, _ = sx.render(*params, viewmat=vm_t, background=t(bg), antialiased=True, **cam(H, W))
+    diff = np.abs(img.detach().cpu().numpy() - ref_img).max(axis=-1)
+    assert diff[flags == 0].max() <= 1e-4
+    (img * t(w)).sum().backward()
+    ref = ch.grads(m, s, q, c, op, bg, vm, w, antialias_eps=eps, **cam(H, W))
+
+    def rel(a, b):
+        a, b = np.asarray(a, np.float64).reshape(b.shape), np.asarray(b, np.float64)
+        return np.linalg.norm(a - b) / (np.linalg.norm(b) + 1e-30)
+
+    names = ["means", "scales", "quats", "colors", "opacities"]
+    errs = {k: rel(p.grad.cpu().numpy(), g) for k, p, g in zip(names, params, ref[:5])}
+    errs["viewmat"] = rel(vm_t.grad.cpu().numpy(), ref[5])
+    assert max(errs.values()) <= 1e-3, errs
