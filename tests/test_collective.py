@@ -29,7 +29,8 @@ def test_nvls_allreduce_matches_nccl_on_two_gpus():
     if "unavailable" in out:
         pytest.skip("no NVLink multicast on this fabric")
     assert res.returncode == 0, out[-3000:]
-    assert "mismatches 0" in out, out[-3000:]
+    for r in range(2):  # each rank reports on a line of its own
+        assert f"rank {r} mismatches 0" in out, out[-3000:]
 
 
 @pytest.mark.gpu
@@ -45,4 +46,5 @@ def test_nvls_adam_matches_allreduce_then_adam_on_two_gpus():
     if "unavailable" in out:
         pytest.skip("no NVLink multicast on this fabric")
     assert res.returncode == 0, out[-3000:]
-    assert "mismatches 0" in out, out[-3000:]
+    for r in range(2):  # each rank reports on a line of its own
+        assert f"rank {r} mismatches 0" in out, out[-3000:]
