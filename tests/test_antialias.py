@@ -114,3 +114,31 @@ def test_antialiased_render_vs_oracle(oracle_lib):
     errs = {k: rel(p.grad.cpu().numpy(), g) for k, p, g in zip(names, params, ref[:5])}
     errs["viewmat"] = rel(vm_t.grad.cpu().numpy(), ref[5])
     assert max(errs.values()) <= 1e-3, errs
+
+
+def test_oracle_chain_compensation_matches_formula():
+    """The oracle chain's fp32 rho2 (numpy) equals the torch restatement of the reference
+    formula bit for bit on the CPU, its rho is the correctly rounded square root of the clipped
+    rho2 (1 for culled entries; torch's vectorised CPU sqrt is not correctly rounded, the GPU's
+    is), and its vjp agrees with torch autograd of the formula inside the clip."""
+    import _oracle_chain as ch
+
+    rng = np.random.default_rng(12)
+    conics = np.abs(rng.normal(0.0, 1.5, size=(4000, 3))).astype(np.float32)
+    conics[:, 1] = rng.normal(0.0, 0.3, size=4000).astype(np.float32)
+    conics[:5] = [[0, 0, 0], [1e-6, 0, 1e-6], [20, 0, 20], [3.3333, 0, 0], [0, 0, 3.3333]]
+    radii = rng.integers(-1, 5, size=4000).astype(np.int32)
+    rho, rho2 = ch.compensation(conics, radii, 0.3)
+    t = torch.tensor(conics)
+    a, b, c = t[:, 0], t[:, 1], t[:, 2]
+    assert np.array_equal(rho2, (1.0 - 0.3 * (a + c) + (0.3 * 0.3) * (a * c - b * b)).numpy())
+    exact = np.sqrt(np.clip(rho2.astype(np.float64), 0.0, 1.0)).astype(np.float32)
+    assert np.array_equal(rho, np.where(radii > 0, exact, np.float32(1.0)))
+    ct = torch.tensor(conics, requires_grad=True)
+    ref = sx.opacity_compensation(ct, torch.tensor(radii))
+    v = rng.normal(size=4000)
+    ref.backward(torch.tensor(v, dtype=torch.float32))
+    mine = ch.compensation_vjp(conics, radii, 0.3, v)
+    inside = (radii > 0) & (rho2 > 0) & (rho2 < 1)
+    got, want = mine[inside], ct.grad.numpy()[inside].astype(np.float64)
+    assert np.linalg.norm(got - want) <= 1e-6 * np.linalg.norm(want)
