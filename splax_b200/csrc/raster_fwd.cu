@@ -13,7 +13,9 @@
 // A block vote (__syncthreads_count) ends the walk once every pixel has saturated.
 //
 // Pixel semantics are the reference's: a gaussian is skipped when sigma < 0 (exponent > 0) or
-// alpha < 1/255, and the walk stops before the gaussian that would take T to <= 1e-4.
+// alpha < 1/255, and the walk stops before the gaussian that would take T to <= 1e-4. The
+// transmittance update T (1 - alpha) is one FMA, T - alpha T rounded once, where the reference
+// rounds 1 - alpha and the product separately: within an ulp of it per step.
 //
 // The alpha clamp min(0.999, opacity * 2^p) can only act on a gaussian whose opacity is close
 // to 0.999, since 2^p <= 1 for every gaussian that is not skipped (p <= 0). Each staged batch
@@ -53,7 +55,7 @@ __device__ __forceinline__ void blend_one(PixelState& s, float p, float opac, fl
   // min(0.999, ov) < 1/255 exactly when ov < 1/255
   if (s.done || p > 0.0f || ov < kAlphaThreshold) return;
   const float alpha = CLAMP ? fminf(kAlphaMax, ov) : ov;
-  const float next_T = s.T * (1.0f - alpha);
+  const float next_T = fmaf(-alpha, s.T, s.T);  // T (1 - alpha), rounded once
   if (next_T <= kTransmittanceMin) {
     s.done = true;
     ++ndone;
@@ -152,7 +154,9 @@ raster_fwd_kernel(RasterFwdArgs a) {
           blend_one<DEPTH, COUNT, kClamp>(st[2 * q + 1], p.y, r1.y, r1.z, r1.w, r2.x, r2.y, idx,
                                           ndone, evals, contribs);
         }
-        if (ndone == kPixels) break;
+        // tested once per pair of records (the loop is unrolled by two): 1.708 -> 1.685 ms
+        // per config-2 step together with the single-rounding transmittance update
+        if ((t & 1) && ndone == kPixels) break;
       }
     };
     if (ndone < kPixels) {
