@@ -325,6 +325,9 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// -infinity: log2 of a zero opacity, the staged exponent offset of a transparent record
+__device__ __forceinline__ float neg_inf() { return __int_as_float(0xff800000); }
+
 // Packed fp32x2 arithmetic (sm_100 FFMA2 / FMUL2 / FADD2): two lanes of IEEE round-to-nearest
 // math per instruction, each lane bit-identical to the scalar fmaf / * / +.
 __device__ __forceinline__ float2 splat2(float s) { return make_float2(s, s); }

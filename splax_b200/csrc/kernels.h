@@ -95,9 +95,9 @@ struct ProjectBwdArgs {
 };
 
 // Per-gaussian record staged by the blend kernels: 3 x float4 =
-// (x, y, qa, qb), (qc, opacity, r, g), (b, depth, 0, 0), with the conic pre-scaled for a
-// base-2 exponent, (qa, qb, qc) = -log2(e)/2 * (a, 2b, c); the last two floats pad the record
-// to 16-byte loads.
+// (x, y, qa, qb), (qc, opacity, r, g), (b, depth, log2 opacity, 0), with the conic pre-scaled
+// for a base-2 exponent, (qa, qb, qc) = -log2(e)/2 * (a, 2b, c), and log2(opacity) added to the
+// exponent so that alpha = 2^p; the last float pads the record to 16-byte loads.
 constexpr int kRecordFloat4 = 3;
 
 struct EmitArgs {

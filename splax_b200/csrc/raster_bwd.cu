@@ -12,12 +12,14 @@
 // reduce-scatter (~K shuffles instead of 5K) and issues ONE atomic instruction across K
 // lanes. Entries to which no pixel of the tile contributes skip the reduction.
 //
-// The staged conic is pre-scaled (q = -log2(e)/2 * (a, 2b, c)), so the exponent is one ex2;
-// the xy cotangent rescales by -ln 2 to recover the conic.
+// The staged conic is pre-scaled (q = -log2(e)/2 * (a, 2b, c)) and log2(opacity) is added to
+// the x-term once per record exactly as the forward adds it, so alpha is one ex2 of the same p
+// the forward computed; the xy cotangent rescales by -ln 2 to recover the conic.
 //
-// The 0.999 alpha clamp can only act on a gaussian whose opacity is close to 0.999 (2^p <= 1
-// for every entry that takes part). A staged batch without such a record (every batch of most
-// scenes) runs a loop that leaves out the clamp and its mask, with identical results.
+// The 0.999 alpha clamp can only act on a gaussian whose opacity is close to 0.999 (p <=
+// log2(opacity) for every entry that takes part). A staged batch without such a record (every
+// batch of most scenes) runs a loop that leaves out the clamp and its mask, with identical
+// results.
 #include <type_traits>
 
 #include "common.cuh"
@@ -31,8 +33,9 @@ namespace {
 constexpr int kBwdUnroll = 2;
 
 constexpr float kLn2 = 0.693147180559945f;
-// Below this opacity alpha = opacity * ex2.approx(p) stays under 0.999 for every p <= 0 (the
-// approximation's relative error, about 2^-22, leaves ex2.approx(p) far below 1.001 there).
+// Below this opacity alpha = ex2.approx(p) stays under 0.999 for every p <= log2(opacity) (the
+// approximation's relative error, about 2^-22, and the rounding of p leave it within 1.001 of
+// the opacity).
 constexpr float kClampFreeOpacity = 0.998f;
 
 // Two vertically adjacent pixels of one thread, advanced in lock-step with packed fp32x2 math.
@@ -59,13 +62,13 @@ struct BwdAcc {
 // - ra (buf . v_out + t_final bg . v_out), and buf . v_out grows by (c . v_out) fac.
 template <bool DEPTH, bool COUNT, bool CLAMP>
 __device__ __forceinline__ bool vjp_pair(BwdPair& s, int32_t idx, float2 p, float2 dy,
-                                         float2 opac, float2 r, float2 g, float2 b, float2 depth,
+                                         float lo, float2 r, float2 g, float2 b, float2 depth,
                                          BwdAcc& acc, unsigned long long& contribs) {
-  const float2 vis = make_float2(ex2_approx(p.x), ex2_approx(p.y));
-  const float2 ov = mul2(opac, vis);
+  // p carries log2(opacity) (as in the forward): ov = opacity * 2^(p - lo) = 2^p
+  const float2 ov = make_float2(ex2_approx(p.x), ex2_approx(p.y));
   // alpha = min(0.999, ov) < 1/255 exactly when ov < 1/255
-  const bool v0 = idx <= s.bf0 && !(p.x > 0.0f) && !(ov.x < kAlphaThreshold);
-  const bool v1 = idx <= s.bf1 && !(p.y > 0.0f) && !(ov.y < kAlphaThreshold);
+  const bool v0 = idx <= s.bf0 && !(p.x > lo) && !(ov.x < kAlphaThreshold);
+  const bool v1 = idx <= s.bf1 && !(p.y > lo) && !(ov.y < kAlphaThreshold);
   if constexpr (COUNT) contribs += static_cast<unsigned>(v0) + static_cast<unsigned>(v1);
   // ov of the pixels that take part (0 elsewhere): alpha and the unclamped mask follow from it
   const float2 ovv = make_float2(v0 ? ov.x : 0.0f, v1 ? ov.y : 0.0f);
@@ -116,7 +119,8 @@ raster_bwd_kernel(RasterBwdArgs a) {
   unsigned steps = 0, steps_active = 0;  // warp steps (COUNT builds only)
   __shared__ float4 s_r0[kBlockSize];
   __shared__ float4 s_r1[kBlockSize];
-  __shared__ float2 s_r2[kBlockSize];
+  // (b, log2 opacity), or (b, depth, log2 opacity, 0) with depth
+  __shared__ std::conditional_t<DEPTH, float4, float2> s_r2[kBlockSize];
   __shared__ int32_t s_id[kBlockSize];
   __shared__ int32_t s_wmax[kBwdThreads / 32];
 
@@ -223,12 +227,14 @@ raster_bwd_kernel(RasterBwdArgs a) {
           s_r1[slot] = r1;
           high_opacity |= r1.y > kClampFreeOpacity;
           const float4 r2 = rec[2];
-          s_r2[slot] = make_float2(r2.x, r2.y);
+          if constexpr (DEPTH) s_r2[slot] = r2;
+          else s_r2[slot] = make_float2(r2.x, r2.z);
           s_id[slot] = g;
         } else {  // only after a reported emission error: a transparent record, id 0
           s_r0[slot] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
           s_r1[slot] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-          s_r2[slot] = make_float2(0.0f, 0.0f);
+          if constexpr (DEPTH) s_r2[slot] = make_float4(0.0f, 0.0f, neg_inf(), 0.0f);
+          else s_r2[slot] = make_float2(0.0f, neg_inf());
           s_id[slot] = 0;
         }
       }
@@ -244,7 +250,10 @@ raster_bwd_kernel(RasterBwdArgs a) {
     for (int32_t t = t_begin; t < batch_size; ++t) {
       const int32_t idx = batch_end - t;
       const float4 r0 = s_r0[t];
-      const float2 r2 = s_r2[t];  // b, depth
+      const auto r2 = s_r2[t];
+      float rb, rd, lo;  // b, depth, log2 opacity
+      if constexpr (DEPTH) { rb = r2.x; rd = r2.y; lo = r2.z; }
+      else { rb = r2.x; rd = 0.0f; lo = r2.y; }
       if constexpr (COUNT) {
 #pragma unroll
         for (int q = 0; q < kPairs; ++q)
@@ -254,9 +263,10 @@ raster_bwd_kernel(RasterBwdArgs a) {
       const float4 r1 = s_r1[t];  // qc, opacity, r, g
       const float dx = r0.x - px;
       const float dy0 = r0.y - py0;
-      const float2 qxx = splat2(r0.z * dx * dx), qbx = splat2(r0.w * dx), qc = splat2(r1.x);
-      const float2 opac = splat2(r1.y), cr = splat2(r1.z), cg = splat2(r1.w),
-                   cb = splat2(r2.x), cd = splat2(r2.y);
+      // the x-term carries log2(opacity): one explicit FMA, as the forward computes it
+      const float2 qxx = splat2(fmaf(r0.z * dx, dx, lo)), qbx = splat2(r0.w * dx),
+                   qc = splat2(r1.x);
+      const float2 cr = splat2(r1.z), cg = splat2(r1.w), cb = splat2(rb), cd = splat2(rd);
       BwdAcc acc;
       acc.c0 = acc.c1 = acc.c2 = acc.w = acc.wy = acc.wyy = acc.d = make_float2(0.0f, 0.0f);
       bool any = false;
@@ -264,7 +274,7 @@ raster_bwd_kernel(RasterBwdArgs a) {
       for (int q = 0; q < kPairs; ++q) {
         const float2 dy = add2(splat2(dy0), make_float2(-2.0f * q, -2.0f * q - 1.0f));
         const float2 p = fma2(fma2(qc, dy, qbx), dy, qxx);
-        any |= vjp_pair<DEPTH, COUNT, kClamp>(pr[q], idx, p, dy, opac, cr, cg, cb, cd, acc,
+        any |= vjp_pair<DEPTH, COUNT, kClamp>(pr[q], idx, p, dy, lo, cr, cg, cb, cd, acc,
                                               contribs);
       }
       if (__ballot_sync(0xffffffffu, any) == 0u) continue;

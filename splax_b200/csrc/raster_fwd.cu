@@ -9,16 +9,17 @@
 // is walked in batches of 256: the CTA gathers the packed 48-byte records (three 16-byte loads
 // each, written by the emission pass) into shared memory, then blends the batch front to back
 // from shared memory with broadcast reads, two records per loop trip. Records carry the conic
-// pre-scaled by -log2(e)/2, so the exponent is a quadratic form evaluated with FMAs and one ex2.
+// pre-scaled by -log2(e)/2 and log2(opacity), which is added to the x-term once per record, so
+// p = log2(alpha) is a quadratic form evaluated with FMAs and alpha one ex2 (no multiply).
 // A block vote (__syncthreads_count) ends the walk once every pixel has saturated.
 //
-// Pixel semantics are the reference's: a gaussian is skipped when sigma < 0 (exponent > 0) or
-// alpha < 1/255, and the walk stops before the gaussian that would take T to <= 1e-4. The
+// Pixel semantics are the reference's: a gaussian is skipped when sigma < 0 (p > log2 opacity)
+// or alpha < 1/255, and the walk stops before the gaussian that would take T to <= 1e-4. The
 // transmittance update T (1 - alpha) is one FMA, T - alpha T rounded once, where the reference
 // rounds 1 - alpha and the product separately: within an ulp of it per step.
 //
-// The alpha clamp min(0.999, opacity * 2^p) can only act on a gaussian whose opacity is close
-// to 0.999, since 2^p <= 1 for every gaussian that is not skipped (p <= 0). Each staged batch
+// The alpha clamp min(0.999, 2^p) can only act on a gaussian whose opacity is close to 0.999,
+// since p <= log2(opacity) for every gaussian that is not skipped. Each staged batch
 // notes whether any of its records has an opacity above kClampFreeOpacity; batches without one
 // (all of them for most scenes) run a loop without the clamp, whose results are identical.
 #include <type_traits>
@@ -31,9 +32,9 @@ namespace {
 // the record loop unrolled by two: the next record's exponents overlap this one's blend
 // (1.84 -> 1.76 ms; by four: 1.79)
 constexpr int kFwdUnroll = 2;
-// Below this opacity alpha = opacity * ex2.approx(p) stays under 0.999 for every p <= 0 (the
-// approximation's relative error, about 2^-22, leaves ex2.approx(p) far below 1.001 there), so
-// min(0.999, alpha) == alpha exactly.
+// Below this opacity alpha = ex2.approx(p) stays under 0.999 for every p <= log2(opacity) (the
+// approximation's relative error, about 2^-22, and the rounding of p leave it within 1.001 of
+// the opacity), so min(0.999, alpha) == alpha exactly.
 constexpr float kClampFreeOpacity = 0.998f;
 
 
@@ -45,15 +46,16 @@ struct PixelState {
 
 // The reference blend step (splax/_rasterize/_kernels.py:185-197) for one pixel.
 template <bool DEPTH, bool COUNT, bool CLAMP>
-__device__ __forceinline__ void blend_one(PixelState& s, float p, float opac, float r, float g,
+__device__ __forceinline__ void blend_one(PixelState& s, float p, float lo, float r, float g,
                                           float b, float depth, int32_t idx, int& ndone,
                                           unsigned long long& evals,
                                           unsigned long long& contribs) {
   // the skip tests of a done pixel and of the reference's sigma / alpha tests share one branch
   if constexpr (COUNT) evals += s.done ? 0 : 1;
-  const float ov = opac * ex2_approx(p);
+  // p carries log2(opacity): alpha = 2^p, and the exponent itself is p - lo
+  const float ov = ex2_approx(p);
   // min(0.999, ov) < 1/255 exactly when ov < 1/255
-  if (s.done || p > 0.0f || ov < kAlphaThreshold) return;
+  if (s.done || p > lo || ov < kAlphaThreshold) return;
   const float alpha = CLAMP ? fminf(kAlphaMax, ov) : ov;
   const float next_T = fmaf(-alpha, s.T, s.T);  // T (1 - alpha), rounded once
   if (next_T <= kTransmittanceMin) {
@@ -84,7 +86,8 @@ raster_fwd_kernel(RasterFwdArgs a) {
   unsigned long long evals = 0, contribs = 0;
   __shared__ float4 s_r0[kBlockSize];
   __shared__ float4 s_r1[kBlockSize];
-  __shared__ float2 s_r2[kBlockSize];
+  // (b, log2 opacity), or (b, depth, log2 opacity, 0) with depth
+  __shared__ std::conditional_t<DEPTH, float4, float2> s_r2[kBlockSize];
   const int64_t tile_g = blockIdx.x;
   const int64_t image_id = tile_g / a.num_tiles;
   const int32_t tile_local = static_cast<int32_t>(tile_g % a.num_tiles);
@@ -122,11 +125,13 @@ raster_fwd_kernel(RasterFwdArgs a) {
           s_r1[slot] = r1;
           high_opacity |= r1.y > kClampFreeOpacity;
           const float4 r2 = rec[2];
-          s_r2[slot] = make_float2(r2.x, r2.y);
+          if constexpr (DEPTH) s_r2[slot] = r2;
+          else s_r2[slot] = make_float2(r2.x, r2.z);
         } else {  // only after a reported emission error: stage a transparent record
           s_r0[slot] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
           s_r1[slot] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-          s_r2[slot] = make_float2(0.0f, 0.0f);
+          if constexpr (DEPTH) s_r2[slot] = make_float4(0.0f, 0.0f, neg_inf(), 0.0f);
+          else s_r2[slot] = make_float2(0.0f, neg_inf());
         }
       }
     }
@@ -139,19 +144,24 @@ raster_fwd_kernel(RasterFwdArgs a) {
       for (int32_t t = 0; t < batch_size; ++t) {
         const float4 r0 = s_r0[t];  // x, y, qa, qb  (q = -log2(e)/2 * (a, 2b, c))
         const float4 r1 = s_r1[t];  // qc, opacity, r, g
-        const float2 r2 = s_r2[t];  // b, depth
+        const auto r2 = s_r2[t];
+        float b, depth, lo;
+        if constexpr (DEPTH) { b = r2.x; depth = r2.y; lo = r2.z; }
+        else { b = r2.x; depth = 0.0f; lo = r2.y; }
         const float dx = r0.x - px;
         const float dy0 = r0.y - py0;
-        const float2 qxx = splat2(r0.z * dx * dx), qbx = splat2(r0.w * dx), qc = splat2(r1.x);
+        // the x-term carries log2(opacity): one explicit FMA, as the backward computes it
+        const float2 qxx = splat2(fmaf(r0.z * dx, dx, lo)), qbx = splat2(r0.w * dx),
+                     qc = splat2(r1.x);
         const int32_t idx = batch_start + t;
 #pragma unroll
         for (int q = 0; q < kPairs; ++q) {
           // the exponents of a pixel pair in packed form, then the branchy per-pixel step
           const float2 dy = add2(splat2(dy0), make_float2(-2.0f * q, -2.0f * q - 1.0f));
           const float2 p = fma2(fma2(qc, dy, qbx), dy, qxx);
-          blend_one<DEPTH, COUNT, kClamp>(st[2 * q], p.x, r1.y, r1.z, r1.w, r2.x, r2.y, idx,
-                                          ndone, evals, contribs);
-          blend_one<DEPTH, COUNT, kClamp>(st[2 * q + 1], p.y, r1.y, r1.z, r1.w, r2.x, r2.y, idx,
+          blend_one<DEPTH, COUNT, kClamp>(st[2 * q], p.x, lo, r1.z, r1.w, b, depth, idx, ndone,
+                                          evals, contribs);
+          blend_one<DEPTH, COUNT, kClamp>(st[2 * q + 1], p.y, lo, r1.z, r1.w, b, depth, idx,
                                           ndone, evals, contribs);
         }
         // tested once per pair of records (the loop is unrolled by two): 1.708 -> 1.685 ms
