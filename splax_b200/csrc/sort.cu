@@ -229,7 +229,9 @@ __device__ __forceinline__ bool prep_one(const PairKeyArgs& a, int64_t idx, K& k
     // conic pre-scaled for the blends' base-2 exponent: q = -log2(e)/2 * (a, 2b, c)
     rec[0] = make_float4(x, y, -kHalfLog2e * ca, -kLog2e * cb);
     rec[1] = make_float4(-kHalfLog2e * cc, op, a.colors[3 * ci], a.colors[3 * ci + 1]);
-    rec[2] = make_float4(a.colors[3 * ci + 2], depth, log2f(op), 0.0f);
+    // log2 of the blend opacity, added to the blends' exponent (alpha = 2^p); a zero or
+    // negative opacity is never blended (alpha < 1/255), so it gets -inf: alpha 0
+    rec[2] = make_float4(a.colors[3 * ci + 2], depth, op > 0.0f ? log2f(op) : neg_inf(), 0.0f);
   }
   return count > 0;
 }

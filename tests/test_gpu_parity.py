@@ -160,6 +160,27 @@ def test_rasterize_parity(sx, oracle_lib, n, H, W, seed):
     _compare_images(N(img).reshape(H, W, 3), img_o.reshape(H, W, 3), flags.reshape(H, W))
 
 
+def test_rasterize_zero_and_negative_blend_opacities(sx, oracle_lib):
+    """Blend opacities that are zero or negative while the tile intersection uses positive map
+    opacities (the rasterize API takes both): the reference skips such gaussians (alpha below
+    1/255), and so must the blends, whose exponent carries log2 of the blend opacity."""
+    n, H, W = 4000, 128, 160
+    (m, s, q, c, op, bg, views, B), cu, orc = _raster_inputs(sx, oracle_lib, n, H, W, 9)
+    xys, d, r, cn, nth, cum = cu
+    blend = op.copy()
+    rng = np.random.default_rng(19)
+    pick = rng.permutation(n)
+    blend[pick[: n // 8]] = 0.0
+    neg = pick[n // 8: n // 4]
+    blend[neg] = -rng.uniform(0.05, 0.9, size=neg.size).astype(np.float32)
+    img = sx.rasterize(T(c), T(blend), T(bg), xys, d, r, cn, cum, img_shape=(H, W),
+                       map_opacities=T(op))
+    fT, fi, img_o, _, flags = oracle_lib.rasterize(c, blend, op, bg, *orc[:4], orc[5], n=n, B=1,
+                                                   img_shape=(H, W))
+    assert np.isfinite(N(img)).all()
+    _compare_images(N(img).reshape(H, W, 3), img_o.reshape(H, W, 3), flags.reshape(H, W))
+
+
 def test_rasterize_residuals_and_depth(sx, oracle_lib):
     from splax_b200._rasterize import _RasterizeFn
 
